@@ -1,0 +1,485 @@
+"""Benchmark of the B200 KV-cache decode path (append + split-K GQA attention).
+
+Default workload (N=1 and the scaling run): BASELINE config 3, Llama-3-8B
+geometry batched decode — 32 layers, 32 q-heads, 8 KV heads, head_dim 128,
+32 sequences per GPU with cached lengths drawn U[1024, 8192] from a seed, one
+appended token each, fp16 paged pool of 16-token pages in a random page
+permutation, N(0,1) K/V/q.  A step is one decode step over all 32 layers:
+per layer, append each sequence's new K/V row and attend over its whole
+context.  Multi-GPU: one process per GPU, each with its own 32 sequences
+(sequences are independent; no collective in the data path) -> weak scaling.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                  [--config 3|2|4]
+
+Prints one JSON line (rank 0).  ``value`` is the whole-job algorithmic HBM
+throughput in GB/s (KV bytes read + appended rows written + q read + out
+written, per step, summed over ranks, divided by the max-over-ranks device
+time); ``e2e`` is the same metric through the reference-facing host-buffer
+call (kvc_decode_host: H2D of q and the new rows, append, attend, D2H, wait —
+per layer, like gqa_attention_cached).  ``--impl reference`` times the
+reference algorithm's CPU restatement (oracle/gqa_online.c, OpenMP on all host
+cores) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gfx1150-inference_b200"))
+
+METRIC = "decode-attn+append HBM GB/s (% of ~8 TB/s) and decode steps/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIGS = {
+    # name: layers, q-heads, kv-heads, head_dim, batch per GPU, ctx generator
+    "3": dict(workload="llama3-8b-batched-decode", layers=32, H=32, Hkv=8, D=128, batch=32,
+              lens=("uniform", 1024, 8192), seed=2024),
+    "2": dict(workload="llama2-7b-decode-4k", layers=32, H=32, Hkv=32, D=128, batch=1,
+              lens=("fixed", 4095), seed=2),
+    "4": dict(workload="llama3-70b-long-context-decode", layers=80, H=64, Hkv=8, D=128, batch=8,
+              lens=("fixed", 32768), seed=4),
+}
+PAGE = 16
+
+
+def cached_lengths(cfg):
+    kind = cfg["lens"][0]
+    if kind == "fixed":
+        return np.full(cfg["batch"], cfg["lens"][1], dtype=np.int64)
+    rng = np.random.default_rng(cfg["seed"])
+    return rng.integers(cfg["lens"][1], cfg["lens"][2] + 1, size=cfg["batch"]).astype(np.int64)
+
+
+def step_bytes(cfg, ctx):
+    """Algorithmic bytes of one decode step (all layers), fp16."""
+    es = 2
+    L, H, Hkv, D = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"]
+    kv_read = int(ctx.sum()) * Hkv * D * es * 2 * L
+    appended = len(ctx) * Hkv * D * es * 2 * L
+    qo = len(ctx) * H * D * es * 2 * L
+    return kv_read, appended, qo
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = max(smax, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------
+# CPU baseline: reference algorithm (C restatement, OpenMP) on a bounded sample
+# ---------------------------------------------------------------------------------
+class CpuWorkload:
+    """One layer of the workload in host memory for the reference algorithm's
+    C restatement (oracle/gqa_online.c, OpenMP over (sequence, q-head))."""
+
+    def __init__(self, cfg, ctx, threads=None):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import build_oracle  # test infrastructure: the CPU baseline leg only
+
+        self.lib = build_oracle.load()
+        self.threads = threads or os.cpu_count() or 1
+        self.H, self.Hkv, self.D = cfg["H"], cfg["Hkv"], cfg["D"]
+        self.n = len(ctx)
+        rng = np.random.default_rng(cfg["seed"] + 99)
+        block = rng.standard_normal(1 << 22, dtype=np.float32).astype(np.float16)
+        self.ks, self.vs = [], []
+        for c in ctx:
+            m = int(c) * self.Hkv * self.D
+            self.ks.append(np.resize(block, m).reshape(int(c), self.Hkv, self.D))
+            self.vs.append(np.resize(block[::-1], m).reshape(int(c), self.Hkv, self.D))
+        self.q = rng.standard_normal((self.n, self.H, self.D), dtype=np.float32).astype(np.float16)
+        self.out = np.empty_like(self.q)
+        self.kp = (ctypes.c_void_p * self.n)(*[k.ctypes.data for k in self.ks])
+        self.vp = (ctypes.c_void_p * self.n)(*[v.ctypes.data for v in self.vs])
+        self.cp = (ctypes.c_int * self.n)(*[int(c) for c in ctx])
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.layer_bytes = (int(ctx.sum()) * self.Hkv * self.D * 2 * 2
+                            + self.n * self.H * self.D * 2 * 2)
+
+    def run_layer(self) -> float:
+        t0 = time.perf_counter()
+        rc = self.lib.gqa_decode_batch_f16(self.n, self.q.ctypes.data, self.kp, self.vp, self.cp,
+                                           self.out.ctypes.data, self.H, self.Hkv, self.D,
+                                           self.scale, self.threads)
+        if rc != 0:
+            raise RuntimeError("CPU baseline rejected its arguments")
+        return time.perf_counter() - t0
+
+
+def cpu_sample(cfg, ctx, min_seconds=10.0, max_reps=50):
+    """Time one layer of the workload (all sequences) on the host cores, repeated
+    until min_seconds.  Returns (GB/s, seconds per layer, threads, reps)."""
+    w = CpuWorkload(cfg, ctx)
+    w.run_layer()  # warm-up
+    reps, total = 0, 0.0
+    while reps < max_reps:
+        total += w.run_layer()
+        reps += 1
+        if total >= min_seconds:
+            break
+    dt = total / reps
+    return w.layer_bytes / dt / 1e9, dt, w.threads, reps
+
+
+# ---------------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------------
+def run_b200(args, rank, world, local_rank):
+    import torch
+
+    import kvcache_ffi as ffi
+    import paged
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS[args.config]
+    L, H, Hkv, D, B = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["batch"]
+    cached = cached_lengths(cfg)
+    ctx = cached + 1                                  # context includes the appended token
+    table, total_pages = paged.random_block_tables(ctx, PAGE, cfg["seed"] + 17 * rank)
+    pool = paged.PagedKVCache(L, total_pages, PAGE, Hkv, D, dtype=torch.float16,
+                              device=local_rank)
+    pool.fill_normal(seed=1000 + rank, stddev=1.0)
+    bt = torch.from_numpy(table).to(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    q = torch.randn((L, B, H, D), generator=g, device=dev, dtype=torch.float32).half()
+    kn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
+    vn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
+    out = torch.empty_like(q)
+    pos = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
+    rows = torch.arange(B, dtype=torch.int32, device=dev)
+    scale = 1.0 / math.sqrt(D)
+    stream = torch.cuda.current_stream()
+    plan = pool.plan(ctx, H, stream=stream)
+    torch.cuda.synchronize()
+
+    def step(events=None):
+        for l in range(L):
+            if events is not None:
+                events[l][0].record(stream)
+            pool.append(l, kn[l], vn[l], bt, pos, rows, stream=stream)
+            if events is not None:
+                events[l][1].record(stream)
+            pool.decode(plan, l, q[l], out[l], bt, scale, stream=stream)
+            if events is not None:
+                events[l][2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    code, info = ffi.device_error(local_rank)
+    if code:
+        raise RuntimeError(f"device error {code} ({info}) during warm-up")
+
+    # per-launch events for every layer of every timed step
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)]
+           for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for s in range(args.steps):
+        step(evs[s])
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed_ms = t_start.elapsed_time(t_stop)
+    dec_ms = [evs[s][l][1].elapsed_time(evs[s][l][2]) for s in range(args.steps) for l in range(L)]
+    app_ms = [evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(args.steps) for l in range(L)]
+    code, info = ffi.device_error(local_rank)
+    if code:
+        raise RuntimeError(f"device error {code} ({info}) during timing")
+
+    kv_read, appended, qo = step_bytes(cfg, ctx)
+    rank_bytes = kv_read + appended + qo
+    # aggregate: max time over ranks, sum of bytes
+    if world > 1:
+        t = torch.tensor([elapsed_ms, float(rank_bytes)], dtype=torch.float64, device=dev)
+        tmax = t[:1].clone()
+        torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
+        tsum = t[1:].clone()
+        torch.distributed.all_reduce(tsum, op=torch.distributed.ReduceOp.SUM)
+        elapsed_ms, job_bytes = float(tmax.item()), float(tsum.item())
+    else:
+        job_bytes = float(rank_bytes)
+    ms_per_step = elapsed_ms / args.steps
+    value = job_bytes / (ms_per_step / 1e3) / 1e9
+
+    # ---- e2e: reference-facing host-buffer call, per layer, copies inside ----
+    e2e = None
+    if not args.no_e2e:
+        hq = q.cpu().pin_memory()
+        hk = kn.cpu().pin_memory()
+        hv = vn.cpu().pin_memory()
+        ho = torch.empty_like(hq).pin_memory()
+        e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+        def e2e_step():
+            for l in range(L):
+                pool.decode_host(plan, l, hq[l], hk[l], hv[l], ho[l], bt, scale, stream=stream)
+
+        for _ in range(min(2, args.warmup)):
+            e2e_step()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        h2d = L * B * (H * D + 2 * Hkv * D) * 2
+        d2h = L * B * H * D * 2
+        e2e = {"value": round(job_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+               "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "call": "kvc_decode_host (pinned host q/k_new/v_new/out, per layer, waits)"}
+
+    if rank != 0:
+        return None
+
+    peak, peak_kind = load_peaks()
+    dec_avg_ms = float(np.mean(dec_ms))
+    dec_bytes = (kv_read + qo) / L                      # per launch (one layer)
+    achieved = dec_bytes / (dec_avg_ms / 1e3) / 1e9
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "steps_per_s": round(1e3 / ms_per_step, 2),
+        "pct_of_peak": round(100.0 * value / (peak * world), 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 storage, f32 accumulate",
+        "data": "synthetic: seeded N(0,1) K/V/q, random page permutation",
+        "config": {
+            "workload": f"{cfg['workload']} (BASELINE config {args.config})",
+            "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D,
+            "sequences_per_gpu": B, "global_batch": B * world,
+            "cached_len": (f"U[{cfg['lens'][1]},{cfg['lens'][2]}] seed {cfg['seed']}"
+                           if cfg["lens"][0] == "uniform" else int(cfg["lens"][1])),
+            "ctx_tokens_per_gpu": int(ctx.sum()), "page_size": PAGE,
+            "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * PAGE * D * 2 / 1e9, 2),
+            "kv_bytes_read_per_step_per_gpu": kv_read,
+            "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
+            "parallelism": f"sequence-sharded x{world} (independent batches, no collective)",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": "decode_mma_kernel",
+            "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+            "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "bytes_per_launch": int(dec_bytes), "avg_launch_us": round(dec_avg_ms * 1e3, 2),
+            "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
+            "append_avg_us": round(float(np.mean(app_ms)) * 1e3, 2),
+        },
+        "gpu_launches": 2 * L * args.steps,
+        "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
+    }
+    if e2e:
+        res["e2e"] = e2e
+    if clocks:
+        res["clocks"] = clocks
+    if not args.no_cpu_baseline:
+        gbs, dt, thr, reps = cpu_sample(cfg, ctx, min_seconds=args.cpu_seconds)
+        res["cpu_baseline"] = {
+            "value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+            "sample": f"1 of {L} layers x {B} sequences, {reps} reps, {dt * 1e3:.1f} ms/layer; "
+                      "oracle/gqa_online.c (reference kernel's algorithm, OpenMP)",
+            "steps_per_s_extrapolated": round(1.0 / (dt * L), 4),
+        }
+    plan.close()
+    pool.close()
+    return res
+
+
+# DRAM traffic per decode launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from the committed ncu captures; None until captured for a workload.
+TRAFFIC_PER_LAUNCH = {}
+
+
+# ---------------------------------------------------------------------------------
+# reference arm: the reference algorithm on the host cores
+# ---------------------------------------------------------------------------------
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    cfg = CONFIGS[args.config]
+    ctx = cached_lengths(cfg) + 1
+    w = CpuWorkload(cfg, ctx)
+    threads = w.threads
+    times = [w.run_layer() for _ in range(args.warmup + args.steps)][args.warmup:]
+    dt = float(np.mean(times))
+    gbs = w.layer_bytes / dt / 1e9
+    sample = (f"each step: 1 of {cfg['layers']} layers x {cfg['batch']} sequences of the "
+              f"workload; oracle/gqa_online.c, the reference kernel's algorithm "
+              f"(attention.hip:35-123), OpenMP")
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * cfg["layers"] * 1e3, 3),
+        "ms_per_step_note": "extrapolated from the 1-layer sample x layers",
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 storage, f32 accumulate",
+        "data": "synthetic: seeded N(0,1) K/V/q",
+        "config": {"workload": f"{cfg['workload']} (BASELINE config {args.config})",
+                   "layers": cfg["layers"], "q_heads": cfg["H"], "kv_heads": cfg["Hkv"],
+                   "head_dim": cfg["D"], "sequences": cfg["batch"],
+                   "ctx_tokens": int(ctx.sum())},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            import datetime
+
+            import torch
+
+            torch.cuda.set_device(local_rank)
+            torch.distributed.init_process_group(
+                "nccl", timeout=datetime.timedelta(seconds=120),
+                device_id=torch.device("cuda", local_rank))
+        try:
+            res = run_b200(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                import torch
+
+                torch.distributed.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

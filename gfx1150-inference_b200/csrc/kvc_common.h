@@ -1,0 +1,91 @@
+// Host-side objects shared by kvc_host.cpp and kvc_offload.cpp.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "kvc_internal.h"
+
+namespace kvc {
+
+// Grow-only device buffer.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t bytes);
+  void release();
+};
+
+// Grow-only page-locked host buffer.
+struct HostBuf {
+  void* ptr = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t bytes);
+  void release();
+};
+
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+int check_device_error(const char* what);
+int elem_size_of(int dtype);
+int make_geom(int num_layers, int num_pages, int page_size, int num_kv_heads, int head_dim,
+              int dtype, PoolGeom* g);
+
+}  // namespace kvc
+
+// Paged KV pool: K and V each num_layers x num_pages x num_kv_heads page-heads.
+struct kvc_pool {
+  kvc::PoolGeom g;
+  int device = 0;
+  uint8_t* k = nullptr;
+  uint8_t* v = nullptr;
+  size_t cap_bytes = 0;   // bytes allocated per K (and per V), grow-only
+  kvc::DevBuf io;         // staging for the host-buffer entry points
+};
+
+// Split-K decode plan for one batch of queries.
+struct kvc_plan {
+  bool valid = false;
+  int device = -1;
+  int n_queries = 0, n_items = 0, n_slots = 0;
+  int num_heads = 0, num_kv_heads = 0, group = 0, n_hchunk = 0;
+  int head_dim = 0, page_size = 0, max_ctx = 0;
+  kvc::PoolGeom pool_geom;
+  std::vector<int4> items, qinfo;
+  std::vector<int32_t> rows, positions;
+  kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters;
+  kvc::HostBuf h_stage;
+  cudaEvent_t upload_done = nullptr;
+
+  void release() {
+    d_items.release();
+    d_qinfo.release();
+    d_rows.release();
+    d_pos.release();
+    d_part_o.release();
+    d_part_ml.release();
+    d_counters.release();
+    h_stage.release();
+    if (upload_done) cudaEventDestroy(upload_done);
+    upload_done = nullptr;
+    valid = false;
+  }
+};
+
+namespace kvc {
+int pool_alloc(kvc_pool* p, const PoolGeom& g, int device);
+void pool_release(kvc_pool* p);
+int do_append(kvc_pool* pool, int layer, const void* d_k_new, const void* d_v_new,
+              const int32_t* d_bt, int bt_stride, const int32_t* d_rows, const int32_t* d_pos,
+              int pos0, int n, cudaStream_t s);
+int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, void* d_out,
+              const int32_t* d_bt, int bt_stride, float scale, cudaStream_t s);
+// Plan for q_len queries m = 0..q_len-1 of one sequence (block-table row 0)
+// whose context is min(kv_len, start_pos + m + 1) if causal, else kv_len
+// (attention.hip:75).
+int plan_queries(kvc_plan* plan, const PoolGeom& g, int q_len, int num_heads, int start_pos,
+                 int kv_len, bool causal, int device, cudaStream_t s);
+}  // namespace kvc

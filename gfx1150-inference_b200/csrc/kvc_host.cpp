@@ -1,0 +1,917 @@
+// Host runtime of libkvcache.so: the C ABI declared in include/kvcache.h.
+//
+// Ownership and threading follow the reference's FFI layer
+// (src/python_bindings/bindings.cpp): the native side owns device memory, every
+// reference-compatible entry point runs under one process-wide mutex
+// (bindings.cpp:18), and errors come back as status codes whose classes match
+// the reference's exceptions (invalid_argument / out_of_range / runtime_error).
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kvcache.h"
+#include "kvc_common.h"
+#include "kvc_internal.h"
+
+using kvc::PoolGeom;
+
+// ============================================================================
+// errors
+// ============================================================================
+namespace kvc {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(KVC_ERR_CUDA, "CUDA error in %s - %s", what, cudaGetErrorString(e));
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int check_device_error(const char* what) {
+  uint32_t code = 0, info = 0;
+  cudaError_t e = read_device_error(&code, &info, true);
+  if (e != cudaSuccess) return cuda_error(e, what);
+  if (code == KVC_DEVERR_NONE) return KVC_OK;
+  const char* name = code == KVC_DEVERR_BAD_PAGE       ? "block table entry out of range"
+                     : code == KVC_DEVERR_WAIT_LIMIT   ? "pipeline wait gave up after its time limit"
+                     : code == KVC_DEVERR_BAD_POSITION ? "append position outside the block table"
+                                                       : "unknown device error";
+  return set_error(KVC_ERR_DEVICE, "%s: %s (value %d)", what, name, static_cast<int>(info));
+}
+
+int elem_size_of(int dtype) {
+  switch (dtype) {
+    case KVC_DTYPE_F16: return 2;
+    case KVC_DTYPE_BF16: return 2;
+    case KVC_DTYPE_F32: return 4;
+    default: return 0;
+  }
+}
+
+cudaError_t DevBuf::ensure(size_t bytes) {
+  if (bytes <= cap) return cudaSuccess;
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  cap = 0;
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  if (e != cudaSuccess) {
+    ptr = nullptr;
+    return e;
+  }
+  cap = bytes;
+  return cudaSuccess;
+}
+
+void DevBuf::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  cap = 0;
+}
+
+cudaError_t HostBuf::ensure(size_t bytes) {
+  if (bytes <= cap) return cudaSuccess;
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  cap = 0;
+  cudaError_t e = cudaMallocHost(&ptr, bytes);
+  if (e != cudaSuccess) {
+    ptr = nullptr;
+    return e;
+  }
+  cap = bytes;
+  return cudaSuccess;
+}
+
+void HostBuf::release() {
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  cap = 0;
+}
+
+int make_geom(int num_layers, int num_pages, int page_size, int num_kv_heads, int head_dim,
+              int dtype, PoolGeom* g) {
+  if (num_layers <= 0 || num_pages <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return set_error(KVC_ERR_INVALID_ARG, "KV cache dimensions must all be positive.");
+  const int es = elem_size_of(dtype);
+  if (es == 0) return set_error(KVC_ERR_INVALID_ARG, "unsupported KV storage dtype %d.", dtype);
+  if (page_size <= 0 || page_size % kSlab != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "page_size must be a positive multiple of 16 (got %d).",
+                     page_size);
+  if (head_dim > 256)
+    return set_error(KVC_ERR_INVALID_ARG, "head_dim must be in (0, 256] (got %d).", head_dim);
+  if ((head_dim * es) % 16 != 0)
+    return set_error(KVC_ERR_INVALID_ARG,
+                     "head_dim * element size must be a multiple of 16 bytes (got head_dim %d).",
+                     head_dim);
+  g->num_layers = num_layers;
+  g->num_pages = num_pages;
+  g->page_size = page_size;
+  g->num_kv_heads = num_kv_heads;
+  g->head_dim = head_dim;
+  g->dtype = dtype;
+  g->elem_size = es;
+  g->layout = (es == 2) ? kLayoutCore : kLayoutLinear;
+  g->page_head_bytes = static_cast<size_t>(page_size) * head_dim * es;
+  g->page_bytes = g->page_head_bytes * num_kv_heads;
+  g->layer_bytes = g->page_bytes * num_pages;
+  return KVC_OK;
+}
+
+}  // namespace kvc
+
+using namespace kvc;
+
+// ============================================================================
+// pool
+// ============================================================================
+namespace kvc {
+
+int pool_alloc(kvc_pool* p, const PoolGeom& g, int device) {
+  const size_t bytes = g.layer_bytes * g.num_layers;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+  if (bytes > p->cap_bytes) {
+    if (p->k) cudaFree(p->k);
+    if (p->v) cudaFree(p->v);
+    p->k = p->v = nullptr;
+    p->cap_bytes = 0;
+    e = cudaMalloc(&p->k, bytes);
+    if (e != cudaSuccess) {
+      p->k = nullptr;
+      return cuda_error(e, "cudaMalloc(K pool)");
+    }
+    e = cudaMalloc(&p->v, bytes);
+    if (e != cudaSuccess) {
+      cudaFree(p->k);
+      p->k = p->v = nullptr;
+      return cuda_error(e, "cudaMalloc(V pool)");
+    }
+    p->cap_bytes = bytes;
+  }
+  p->g = g;
+  p->device = device;
+  return KVC_OK;
+}
+
+void pool_release(kvc_pool* p) {
+  if (p->k) cudaFree(p->k);
+  if (p->v) cudaFree(p->v);
+  p->k = p->v = nullptr;
+  p->cap_bytes = 0;
+  p->g = PoolGeom();
+}
+
+}  // namespace kvc
+
+extern "C" int kvc_version(void) { return 1; }
+
+extern "C" const char* kvc_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int kvc_device_error(int device, int clear, uint32_t* code, uint32_t* info) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+  e = read_device_error(code, info, clear != 0);
+  if (e != cudaSuccess) return cuda_error(e, "read_device_error");
+  return KVC_OK;
+}
+
+extern "C" int kvc_device_sm_count(int device, int* out) {
+  if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");
+  cudaError_t e = cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return cuda_error(e, "cudaDeviceGetAttribute");
+  return KVC_OK;
+}
+
+extern "C" int kvc_pool_create(int num_layers, int num_pages, int page_size, int num_kv_heads,
+                               int head_dim, int dtype, int device, kvc_pool_t** out) {
+  if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");
+  *out = nullptr;
+  PoolGeom g;
+  int rc = make_geom(num_layers, num_pages, page_size, num_kv_heads, head_dim, dtype, &g);
+  if (rc) return rc;
+  kvc_pool* p = new kvc_pool();
+  rc = pool_alloc(p, g, device);
+  if (rc) {
+    delete p;
+    return rc;
+  }
+  *out = p;
+  return KVC_OK;
+}
+
+extern "C" int kvc_pool_destroy(kvc_pool_t* pool) {
+  if (!pool) return KVC_OK;
+  cudaSetDevice(pool->device);
+  pool_release(pool);
+  delete pool;
+  return KVC_OK;
+}
+
+extern "C" int kvc_pool_info(const kvc_pool_t* pool, void** k_base, void** v_base,
+                             size_t* bytes_per_layer, size_t* bytes_per_page_head) {
+  if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
+  if (k_base) *k_base = pool->k;
+  if (v_base) *v_base = pool->v;
+  if (bytes_per_layer) *bytes_per_layer = pool->g.layer_bytes;
+  if (bytes_per_page_head) *bytes_per_page_head = pool->g.page_head_bytes;
+  return KVC_OK;
+}
+
+extern "C" int kvc_pool_fill_normal(kvc_pool_t* pool, int layer_begin, int layer_end,
+                                    int page_begin, int page_end, uint64_t seed, float stddev,
+                                    void* stream) {
+  if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
+  const PoolGeom& g = pool->g;
+  if (layer_begin < 0 || layer_end > g.num_layers || layer_begin > layer_end || page_begin < 0 ||
+      page_end > g.num_pages || page_begin > page_end)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "fill range outside the pool.");
+  cudaSetDevice(pool->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t elems_per_page = g.page_bytes / g.elem_size;
+  const size_t elems_per_layer = g.layer_bytes / g.elem_size;
+  for (int l = layer_begin; l < layer_end; ++l) {
+    for (int kv = 0; kv < 2; ++kv) {
+      FillArgs f;
+      uint8_t* base = kv == 0 ? pool->k : pool->v;
+      f.base = base + static_cast<size_t>(l) * g.layer_bytes +
+               static_cast<size_t>(page_begin) * g.page_bytes;
+      f.n_elems = elems_per_page * static_cast<size_t>(page_end - page_begin);
+      f.seed = seed + static_cast<uint64_t>(kv) * 0x5851F42D4C957F2Dull;
+      f.index0 = static_cast<uint64_t>(l) * elems_per_layer +
+                 static_cast<uint64_t>(page_begin) * elems_per_page;
+      f.stddev = stddev;
+      f.dtype = g.dtype;
+      cudaError_t e = launch_fill_normal(f, s);
+      if (e != cudaSuccess) return cuda_error(e, "fill_normal_kernel");
+    }
+  }
+  return KVC_OK;
+}
+
+namespace kvc {
+
+int do_append(kvc_pool* pool, int layer, const void* d_k_new, const void* d_v_new,
+              const int32_t* d_bt, int bt_stride, const int32_t* d_rows, const int32_t* d_pos,
+              int pos0, int n, cudaStream_t s) {
+  const PoolGeom& g = pool->g;
+  if (layer < 0 || layer >= g.num_layers)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "layer_idx out of range for the KV pool.");
+  if (n < 0) return set_error(KVC_ERR_INVALID_ARG, "row count must be non-negative.");
+  if (n == 0) return KVC_OK;
+  if (!d_k_new || !d_v_new || !d_bt)
+    return set_error(KVC_ERR_INVALID_ARG, "K/V rows and block tables must not be null.");
+  if ((reinterpret_cast<uintptr_t>(d_k_new) | reinterpret_cast<uintptr_t>(d_v_new)) & 15u)
+    return set_error(KVC_ERR_INVALID_ARG, "K/V row buffers must be 16-byte aligned.");
+  if (bt_stride <= 0) return set_error(KVC_ERR_INVALID_ARG, "bt_stride must be positive.");
+  AppendArgs a;
+  a.k_layer = pool->k + static_cast<size_t>(layer) * g.layer_bytes;
+  a.v_layer = pool->v + static_cast<size_t>(layer) * g.layer_bytes;
+  a.k_new = static_cast<const uint8_t*>(d_k_new);
+  a.v_new = static_cast<const uint8_t*>(d_v_new);
+  a.block_tables = d_bt;
+  a.rows = d_rows;
+  a.positions = d_pos;
+  a.pos0 = pos0;
+  a.bt_stride = bt_stride;
+  a.n = n;
+  a.num_kv_heads = g.num_kv_heads;
+  a.row_units = g.head_dim * g.elem_size / 16;
+  a.page_size = g.page_size;
+  a.num_pages = g.num_pages;
+  a.layout = g.layout;
+  a.page_head_bytes = g.page_head_bytes;
+  cudaError_t e = launch_append(a, g.elem_size, s);
+  if (e != cudaSuccess) return cuda_error(e, "append_kernel");
+  return KVC_OK;
+}
+
+}  // namespace kvc
+
+extern "C" int kvc_append(kvc_pool_t* pool, int layer, const void* d_k_new, const void* d_v_new,
+                          const int32_t* d_block_tables, int bt_stride, const int32_t* d_rows,
+                          const int32_t* d_positions, int n, void* stream) {
+  if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
+  if (!d_positions) return set_error(KVC_ERR_INVALID_ARG, "positions must not be null.");
+  cudaSetDevice(pool->device);
+  return do_append(pool, layer, d_k_new, d_v_new, d_block_tables, bt_stride, d_rows, d_positions,
+                   0, n, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_tables,
+                          int bt_stride, int row, int start, int count, void* d_k_out,
+                          void* d_v_out, void* stream) {
+  if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
+  const PoolGeom& g = pool->g;
+  if (layer < 0 || layer >= g.num_layers)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "layer_idx out of range for the KV pool.");
+  if (start < 0 || count < 0 ||
+      static_cast<int64_t>(start) + count > static_cast<int64_t>(bt_stride) * g.page_size)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "gather range outside the block table.");
+  if (row < 0) return set_error(KVC_ERR_OUT_OF_RANGE, "row must be non-negative.");
+  if ((reinterpret_cast<uintptr_t>(d_k_out) | reinterpret_cast<uintptr_t>(d_v_out)) & 15u)
+    return set_error(KVC_ERR_INVALID_ARG, "output buffers must be 16-byte aligned.");
+  cudaSetDevice(pool->device);
+  GatherArgs a;
+  a.k_layer = pool->k + static_cast<size_t>(layer) * g.layer_bytes;
+  a.v_layer = pool->v + static_cast<size_t>(layer) * g.layer_bytes;
+  a.k_out = static_cast<uint8_t*>(d_k_out);
+  a.v_out = static_cast<uint8_t*>(d_v_out);
+  a.bt_row = d_block_tables + static_cast<size_t>(row) * bt_stride;
+  a.bt_stride = bt_stride;
+  a.start = start;
+  a.count = count;
+  a.num_kv_heads = g.num_kv_heads;
+  a.row_units = g.head_dim * g.elem_size / 16;
+  a.page_size = g.page_size;
+  a.num_pages = g.num_pages;
+  a.layout = g.layout;
+  a.page_head_bytes = g.page_head_bytes;
+  cudaError_t e = launch_gather(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "gather_kernel");
+  return KVC_OK;
+}
+
+// ============================================================================
+// plans
+// ============================================================================
+namespace kvc {
+
+int split_tokens_for(int page_size) {
+  return ((kSplitTokens + page_size - 1) / page_size) * page_size;
+}
+
+// Build the split list on the host.  ctx_of(i) / row_of(i) describe query i.
+template <typename CtxFn, typename RowFn>
+int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, CtxFn ctx_of,
+               RowFn row_of, int device, cudaStream_t s) {
+  if (n_queries < 0) return set_error(KVC_ERR_INVALID_ARG, "n_queries must be non-negative.");
+  if (num_heads <= 0 || num_heads % g.num_kv_heads != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
+  const int C = split_tokens_for(g.page_size);
+  p->items.clear();
+  p->qinfo.clear();
+  p->rows.clear();
+  p->positions.clear();
+  int slot = 0, max_ctx = 0;
+  for (int i = 0; i < n_queries; ++i) {
+    const int ctx = ctx_of(i);
+    const int row = row_of(i);
+    if (ctx < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
+    if (row < 0) return set_error(KVC_ERR_INVALID_ARG, "block-table row must be non-negative.");
+    const int ns = ctx > 0 ? (ctx + C - 1) / C : 1;
+    p->qinfo.push_back(make_int4(row, ctx, slot, ns));
+    p->rows.push_back(row);
+    p->positions.push_back(ctx - 1);
+    for (int k = 0; k < ns; ++k)
+      p->items.push_back(make_int4(i, k, k * C, std::min((k + 1) * C, ctx)));
+    slot += ns;
+    max_ctx = std::max(max_ctx, ctx);
+  }
+  // Longest splits first: CTAs are dispatched roughly in index order, so the
+  // short tail splits fill the last wave.
+  std::stable_sort(p->items.begin(), p->items.end(), [](const int4& x, const int4& y) {
+    return (x.w - x.z) > (y.w - y.z);
+  });
+  p->n_queries = n_queries;
+  p->n_items = static_cast<int>(p->items.size());
+  p->n_slots = slot;
+  p->num_heads = num_heads;
+  p->num_kv_heads = g.num_kv_heads;
+  p->group = num_heads / g.num_kv_heads;
+  p->n_hchunk = (p->group + 7) / 8;
+  p->head_dim = g.head_dim;
+  p->page_size = g.page_size;
+  p->max_ctx = max_ctx;
+  p->device = device;
+
+  cudaError_t e;
+  // device buffers (grow-only)
+  const size_t items_b = sizeof(int4) * std::max<size_t>(1, p->items.size());
+  const size_t qinfo_b = sizeof(int4) * std::max(1, n_queries);
+  const size_t rows_b = sizeof(int32_t) * std::max(1, n_queries);
+  const size_t po_b = sizeof(float) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads * g.head_dim);
+  const size_t pml_b = sizeof(float2) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads);
+  const size_t cnt_b = sizeof(unsigned) * std::max<size_t>(1, static_cast<size_t>(n_queries) * g.num_kv_heads * p->n_hchunk);
+  if ((e = p->d_items.ensure(items_b)) || (e = p->d_qinfo.ensure(qinfo_b)) ||
+      (e = p->d_rows.ensure(rows_b)) || (e = p->d_pos.ensure(rows_b)) ||
+      (e = p->d_part_o.ensure(po_b)) || (e = p->d_part_ml.ensure(pml_b)))
+    return cuda_error(e, "plan buffers");
+  if (cnt_b > p->d_counters.cap) {
+    if ((e = p->d_counters.ensure(cnt_b))) return cuda_error(e, "plan counters");
+    if ((e = cudaMemsetAsync(p->d_counters.ptr, 0, p->d_counters.cap, s)))
+      return cuda_error(e, "cudaMemsetAsync(counters)");
+  }
+  // upload through pinned staging; wait for the previous upload to leave it
+  const size_t stage_b = items_b + qinfo_b + 2 * rows_b;
+  if (p->upload_done) {
+    if ((e = cudaEventSynchronize(p->upload_done))) return cuda_error(e, "plan upload wait");
+  } else if ((e = cudaEventCreateWithFlags(&p->upload_done, cudaEventDisableTiming))) {
+    return cuda_error(e, "cudaEventCreate");
+  }
+  if ((e = p->h_stage.ensure(stage_b))) return cuda_error(e, "cudaMallocHost(plan)");
+  uint8_t* h = static_cast<uint8_t*>(p->h_stage.ptr);
+  memcpy(h, p->items.data(), sizeof(int4) * p->items.size());
+  memcpy(h + items_b, p->qinfo.data(), sizeof(int4) * n_queries);
+  memcpy(h + items_b + qinfo_b, p->rows.data(), sizeof(int32_t) * n_queries);
+  memcpy(h + items_b + qinfo_b + rows_b, p->positions.data(), sizeof(int32_t) * n_queries);
+  if ((e = cudaMemcpyAsync(p->d_items.ptr, h, sizeof(int4) * p->items.size(), cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(p->d_qinfo.ptr, h + items_b, sizeof(int4) * n_queries, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(p->d_rows.ptr, h + items_b + qinfo_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(p->d_pos.ptr, h + items_b + qinfo_b + rows_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "plan upload");
+  if ((e = cudaEventRecord(p->upload_done, s))) return cuda_error(e, "cudaEventRecord(plan)");
+  p->pool_geom = g;
+  p->valid = true;
+  return KVC_OK;
+}
+
+int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, void* d_out,
+              const int32_t* d_bt, int bt_stride, float scale, cudaStream_t s) {
+  const PoolGeom& g = pool->g;
+  if (!plan || !plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
+  if (layer < 0 || layer >= g.num_layers)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "layer_idx out of range for the KV pool.");
+  if (plan->head_dim != g.head_dim || plan->num_kv_heads != g.num_kv_heads ||
+      plan->page_size != g.page_size)
+    return set_error(KVC_ERR_INVALID_ARG, "plan was built for a pool of another geometry.");
+  if (plan->n_queries == 0) return KVC_OK;
+  if (!d_q || !d_out || !d_bt)
+    return set_error(KVC_ERR_INVALID_ARG, "q, out and block tables must not be null.");
+  if ((reinterpret_cast<uintptr_t>(d_q) | reinterpret_cast<uintptr_t>(d_out)) & 3u)
+    return set_error(KVC_ERR_INVALID_ARG, "q and out must be 4-byte aligned.");
+  if (static_cast<int64_t>(plan->max_ctx) > static_cast<int64_t>(bt_stride) * g.page_size)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "a context length exceeds the block-table width.");
+  DecodeArgs a;
+  a.k_layer = pool->k + static_cast<size_t>(layer) * g.layer_bytes;
+  a.v_layer = pool->v + static_cast<size_t>(layer) * g.layer_bytes;
+  a.q = d_q;
+  a.out = d_out;
+  a.block_tables = d_bt;
+  a.bt_stride = bt_stride;
+  a.items = static_cast<const int4*>(plan->d_items.ptr);
+  a.qinfo = static_cast<const int4*>(plan->d_qinfo.ptr);
+  a.part_o = static_cast<float*>(plan->d_part_o.ptr);
+  a.part_ml = static_cast<float2*>(plan->d_part_ml.ptr);
+  a.counters = static_cast<unsigned*>(plan->d_counters.ptr);
+  a.n_items = plan->n_items;
+  a.num_heads = plan->num_heads;
+  a.num_kv_heads = g.num_kv_heads;
+  a.group = plan->group;
+  a.n_hchunk = plan->n_hchunk;
+  a.head_dim = g.head_dim;
+  a.page_size = g.page_size;
+  a.num_pages = g.num_pages;
+  a.scale_log2 = scale * kLog2e;
+  cudaError_t e = launch_decode(a, g.dtype, g.layout, s);
+  if (e != cudaSuccess) return cuda_error(e, "decode kernel");
+  return KVC_OK;
+}
+
+int plan_queries(kvc_plan* plan, const PoolGeom& g, int q_len, int num_heads, int start_pos,
+                 int kv_len, bool causal, int device, cudaStream_t s) {
+  return plan_build(
+      plan, g, q_len, num_heads,
+      [&](int m) { return causal ? std::max(0, std::min(kv_len, start_pos + m + 1)) : kv_len; },
+      [](int) { return 0; }, device, s);
+}
+
+}  // namespace kvc
+
+extern "C" int kvc_plan_create(kvc_plan_t** out) {
+  if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");
+  *out = new kvc_plan();
+  return KVC_OK;
+}
+
+extern "C" int kvc_plan_destroy(kvc_plan_t* plan) {
+  if (!plan) return KVC_OK;
+  if (plan->device >= 0) cudaSetDevice(plan->device);
+  plan->release();
+  delete plan;
+  return KVC_OK;
+}
+
+extern "C" int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const int32_t* h_rows,
+                               const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                               void* stream) {
+  if (!plan || !pool) return set_error(KVC_ERR_INVALID_ARG, "plan and pool must not be null.");
+  if (n_queries > 0 && !h_ctx_lens)
+    return set_error(KVC_ERR_INVALID_ARG, "ctx_lens must not be null.");
+  cudaSetDevice(pool->device);
+  return plan_build(
+      plan, pool->g, n_queries, num_heads, [&](int i) { return h_ctx_lens[i]; },
+      [&](int i) { return h_rows ? h_rows[i] : i; }, pool->device,
+      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvc_plan_info(const kvc_plan_t* plan, int* n_items, int* n_ctas,
+                             size_t* scratch_bytes) {
+  if (!plan) return set_error(KVC_ERR_INVALID_ARG, "plan must not be null.");
+  if (n_items) *n_items = plan->n_items;
+  if (n_ctas) *n_ctas = plan->n_items * plan->num_kv_heads * plan->n_hchunk;
+  if (scratch_bytes)
+    *scratch_bytes = plan->d_part_o.cap + plan->d_part_ml.cap + plan->d_counters.cap;
+  return KVC_OK;
+}
+
+extern "C" int kvc_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int layer, const void* d_q,
+                          void* d_out, const int32_t* d_block_tables, int bt_stride, float scale,
+                          void* stream) {
+  if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
+  cudaSetDevice(pool->device);
+  return do_decode(pool, plan, layer, d_q, d_out, d_block_tables, bt_stride, scale,
+                   static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvc_append_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
+                                 const void* d_q, const void* d_k_new, const void* d_v_new,
+                                 void* d_out, const int32_t* d_block_tables, int bt_stride,
+                                 float scale, void* stream) {
+  if (!pool || !plan) return set_error(KVC_ERR_INVALID_ARG, "pool and plan must not be null.");
+  if (!plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
+  cudaSetDevice(pool->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = do_append(pool, layer, d_k_new, d_v_new, d_block_tables, bt_stride,
+                     static_cast<const int32_t*>(plan->d_rows.ptr),
+                     static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
+  if (rc) return rc;
+  return do_decode(pool, plan, layer, d_q, d_out, d_block_tables, bt_stride, scale, s);
+}
+
+extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
+                               const void* h_q, const void* h_k_new, const void* h_v_new,
+                               void* h_out, const int32_t* d_block_tables, int bt_stride,
+                               float scale, void* stream) {
+  if (!pool || !plan) return set_error(KVC_ERR_INVALID_ARG, "pool and plan must not be null.");
+  if (!plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
+  if (!h_q || !h_k_new || !h_v_new || !h_out)
+    return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
+  const PoolGeom& g = pool->g;
+  cudaSetDevice(pool->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t n = static_cast<size_t>(plan->n_queries);
+  const size_t qb = n * plan->num_heads * g.head_dim * g.elem_size;
+  const size_t kb = n * g.num_kv_heads * g.head_dim * g.elem_size;
+  const size_t kb_al = (kb + 255) & ~static_cast<size_t>(255);
+  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
+  cudaError_t e = pool->io.ensure(2 * qb_al + 2 * kb_al);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(io)");
+  uint8_t* d = static_cast<uint8_t*>(pool->io.ptr);
+  uint8_t* d_q = d;
+  uint8_t* d_out = d + qb_al;
+  uint8_t* d_k = d + 2 * qb_al;
+  uint8_t* d_v = d_k + kb_al;
+  if ((e = cudaMemcpyAsync(d_q, h_q, qb, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(d_k, h_k_new, kb, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(d_v, h_v_new, kb, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpyAsync(H2D)");
+  int rc = do_append(pool, layer, d_k, d_v, d_block_tables, bt_stride,
+                     static_cast<const int32_t*>(plan->d_rows.ptr),
+                     static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
+  if (rc) return rc;
+  rc = do_decode(pool, plan, layer, d_q, d_out, d_block_tables, bt_stride, scale, s);
+  if (rc) return rc;
+  if ((e = cudaMemcpyAsync(h_out, d_out, qb, cudaMemcpyDeviceToHost, s)))
+    return cuda_error(e, "cudaMemcpyAsync(D2H)");
+  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  return check_device_error("kvc_decode_host");
+}
+
+// ============================================================================
+// reference-compatible process-wide pool (DeviceKVCachePool, attention.hip:168-224)
+// ============================================================================
+namespace {
+
+struct Singleton {
+  std::mutex mu;             // bindings.cpp:18 (g_hip_workspace_mutex)
+  kvc_pool pool;             // paged pool, one sequence, identity block table
+  bool live = false;
+  int max_seq_len = 0;
+  DevBuf bt;                 // identity block table
+  int bt_len = 0;
+  kvc_plan plan;
+  cudaStream_t stream = nullptr;
+  int stream_device = -1;
+};
+
+Singleton& singleton() {
+  static Singleton s;
+  return s;
+}
+
+// Scratch context of the full-KV host entry point (launch_gqa_attention_fp16,
+// attention.hip:228-284 keeps an AttentionWorkspace for the same purpose).
+struct HostAttnCtx {
+  kvc_pool pool;
+  DevBuf bt;
+  int bt_len = 0;
+  DevBuf bounce;
+  kvc_plan plan;
+  cudaStream_t stream = nullptr;
+  int stream_device = -1;
+};
+
+HostAttnCtx& host_attn_ctx() {
+  static HostAttnCtx c;
+  return c;
+}
+
+int ensure_stream(cudaStream_t* s, int* s_dev, int device) {
+  if (*s && *s_dev == device) return KVC_OK;
+  cudaError_t e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return cuda_error(e, "cudaStreamCreate");
+  *s_dev = device;
+  return KVC_OK;
+}
+
+int ensure_identity_table(DevBuf* bt, int* bt_len, int pages, cudaStream_t s) {
+  if (pages <= *bt_len) return KVC_OK;
+  cudaError_t e = bt->ensure(sizeof(int32_t) * pages);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(block table)");
+  std::vector<int32_t> ids(pages);
+  for (int i = 0; i < pages; ++i) ids[i] = i;
+  if ((e = cudaMemcpyAsync(bt->ptr, ids.data(), sizeof(int32_t) * pages, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpy(block table)");
+  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  *bt_len = pages;
+  return KVC_OK;
+}
+
+constexpr int kDefaultPageSize = 16;
+
+int cache_init_locked(Singleton& S, int num_layers, int max_seq_len, int num_kv_heads,
+                      int head_dim, int dtype, int page_size) {
+  if (num_layers <= 0 || max_seq_len <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return set_error(KVC_ERR_INVALID_ARG, "KV cache dimensions must all be positive.");
+  if (page_size == 0) page_size = kDefaultPageSize;
+  const int pages = (max_seq_len + page_size - 1) / page_size;
+  PoolGeom g;
+  int rc = make_geom(num_layers, pages, page_size, num_kv_heads, head_dim, dtype, &g);
+  if (rc) return rc;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if ((rc = ensure_stream(&S.stream, &S.stream_device, device))) return rc;
+  if ((rc = pool_alloc(&S.pool, g, device))) {
+    S.live = false;
+    return rc;
+  }
+  if ((rc = ensure_identity_table(&S.bt, &S.bt_len, pages, S.stream))) return rc;
+  S.max_seq_len = max_seq_len;
+  S.live = true;
+  return KVC_OK;
+}
+
+// Validation of attention.hip:316-329, in the same order and with the same classes.
+int validate_cached(const Singleton& S, int layer_idx, int q_len, int start_pos, int num_heads,
+                    int num_kv_heads, int head_dim) {
+  if (!S.live)
+    return set_error(KVC_ERR_RUNTIME, "Device KV cache not initialized. Call kv_cache_init first.");
+  if (layer_idx < 0 || layer_idx >= S.pool.g.num_layers)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "layer_idx out of range for DeviceKVCachePool.");
+  const int64_t kv_len = static_cast<int64_t>(start_pos) + q_len;
+  if (start_pos < 0 || kv_len > S.max_seq_len)
+    return set_error(KVC_ERR_OUT_OF_RANGE,
+                     "start_pos + q_len exceeds max_seq_len in DeviceKVCachePool.");
+  if (num_kv_heads != S.pool.g.num_kv_heads || head_dim != S.pool.g.head_dim)
+    return set_error(KVC_ERR_INVALID_ARG,
+                     "num_kv_heads or head_dim mismatch with DeviceKVCachePool.");
+  if (num_heads <= 0 || num_heads % num_kv_heads != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
+  if (q_len < 0) return set_error(KVC_ERR_INVALID_ARG, "q_len must be non-negative.");
+  return KVC_OK;
+}
+
+// Append q_len rows at start_pos of row 0 and attend for queries m = 0..q_len-1.
+int cached_attend(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_len,
+                  const void* d_Q, const void* d_Kn, const void* d_Vn, void* d_Out, int layer_idx,
+                  int q_len, int start_pos, int num_heads, float scale, bool causal,
+                  cudaStream_t s) {
+  const int kv_len = start_pos + q_len;
+  int rc = do_append(pool, layer_idx, d_Kn, d_Vn, d_bt, bt_len, nullptr, nullptr, start_pos,
+                     q_len, s);
+  if (rc) return rc;
+  rc = plan_queries(plan, pool->g, q_len, num_heads, start_pos, kv_len, causal, pool->device, s);
+  if (rc) return rc;
+  return do_decode(pool, plan, layer_idx, d_Q, d_Out, d_bt, bt_len, scale, s);
+}
+
+}  // namespace
+
+extern "C" int kvc_cache_init(int num_layers, int max_seq_len, int num_kv_heads, int head_dim) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  return cache_init_locked(S, num_layers, max_seq_len, num_kv_heads, head_dim, KVC_DTYPE_F16,
+                           kDefaultPageSize);
+}
+
+extern "C" int kvc_cache_init_ex(int num_layers, int max_seq_len, int num_kv_heads, int head_dim,
+                                 int dtype, int page_size) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  return cache_init_locked(S, num_layers, max_seq_len, num_kv_heads, head_dim, dtype, page_size);
+}
+
+extern "C" int kvc_cache_free(void) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  if (S.pool.k || S.pool.v) {
+    cudaSetDevice(S.pool.device);
+    pool_release(&S.pool);
+  }
+  S.live = false;
+  S.max_seq_len = 0;
+  return KVC_OK;
+}
+
+extern "C" int kvc_cache_dtype(void) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  return S.live ? S.pool.g.dtype : -1;
+}
+
+extern "C" int kvc_gqa_attention_cached(const void* h_Q, const void* h_K_new,
+                                        const void* h_V_new, void* h_Out, int layer_idx,
+                                        int q_len, int start_pos, int num_heads,
+                                        int num_kv_heads, int head_dim, float scale,
+                                        int causal) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  int rc = validate_cached(S, layer_idx, q_len, start_pos, num_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (q_len == 0) return KVC_OK;
+  if (!h_Q || !h_K_new || !h_V_new || !h_Out)
+    return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
+  cudaSetDevice(S.pool.device);
+  const PoolGeom& g = S.pool.g;
+  const size_t qb = static_cast<size_t>(q_len) * num_heads * head_dim * g.elem_size;
+  const size_t kb = static_cast<size_t>(q_len) * num_kv_heads * head_dim * g.elem_size;
+  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
+  const size_t kb_al = (kb + 255) & ~static_cast<size_t>(255);
+  cudaError_t e = S.pool.io.ensure(2 * qb_al + 2 * kb_al);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(io)");
+  uint8_t* d = static_cast<uint8_t*>(S.pool.io.ptr);
+  uint8_t *d_q = d, *d_out = d + qb_al, *d_k = d + 2 * qb_al, *d_v = d + 2 * qb_al + kb_al;
+  cudaStream_t s = S.stream;
+  if ((e = cudaMemcpyAsync(d_k, h_K_new, kb, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(d_v, h_V_new, kb, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpyAsync(H2D)");
+  rc = cached_attend(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_q, d_k,
+                     d_v, d_out, layer_idx, q_len, start_pos, num_heads, scale, causal != 0, s);
+  if (rc) return rc;
+  if ((e = cudaMemcpyAsync(h_Out, d_out, qb, cudaMemcpyDeviceToHost, s)))
+    return cuda_error(e, "cudaMemcpyAsync(D2H)");
+  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  return check_device_error("gqa_attention_cached");
+}
+
+extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_new,
+                                               const void* d_V_new, void* d_Out, int layer_idx,
+                                               int q_len, int start_pos, int num_heads,
+                                               int num_kv_heads, int head_dim, float scale,
+                                               int causal, void* stream) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  int rc = validate_cached(S, layer_idx, q_len, start_pos, num_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
+  if (q_len == 0) return KVC_OK;
+  cudaSetDevice(S.pool.device);
+  return cached_attend(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_Q,
+                       d_K_new, d_V_new, d_Out, layer_idx, q_len, start_pos, num_heads, scale,
+                       causal != 0, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvc_cache_gather(int layer_idx, int start, int count, void* h_K_out,
+                                void* h_V_out) {
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  if (!S.live)
+    return set_error(KVC_ERR_RUNTIME, "Device KV cache not initialized. Call kv_cache_init first.");
+  if (layer_idx < 0 || layer_idx >= S.pool.g.num_layers)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "layer_idx out of range for DeviceKVCachePool.");
+  if (start < 0 || count < 0 || static_cast<int64_t>(start) + count > S.max_seq_len)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "gather range exceeds max_seq_len.");
+  if (count == 0) return KVC_OK;
+  if (!h_K_out || !h_V_out) return set_error(KVC_ERR_INVALID_ARG, "outputs must not be null.");
+  cudaSetDevice(S.pool.device);
+  const PoolGeom& g = S.pool.g;
+  const size_t rb = static_cast<size_t>(count) * g.num_kv_heads * g.head_dim * g.elem_size;
+  const size_t rb_al = (rb + 255) & ~static_cast<size_t>(255);
+  cudaError_t e = S.pool.io.ensure(2 * rb_al);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(io)");
+  uint8_t* d = static_cast<uint8_t*>(S.pool.io.ptr);
+  cudaStream_t s = S.stream;
+  int rc = kvc_gather(&S.pool, layer_idx, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, 0,
+                      start, count, d, d + rb_al, s);
+  if (rc) return rc;
+  if ((e = cudaMemcpyAsync(h_K_out, d, rb, cudaMemcpyDeviceToHost, s)) ||
+      (e = cudaMemcpyAsync(h_V_out, d + rb_al, rb, cudaMemcpyDeviceToHost, s)))
+    return cuda_error(e, "cudaMemcpyAsync(D2H)");
+  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  return check_device_error("kv_cache_gather");
+}
+
+// Full-KV host attention (launch_gqa_attention_fp16, attention.hip:228-284): the
+// layer's K/V rows come from host memory on every call.  They are copied to a
+// device bounce buffer, scattered into a one-layer scratch pool with the same
+// page geometry as the resident pool and attended by the same kernels, so the
+// result is bit-identical to the resident path for the same rows.
+extern "C" int kvc_gqa_attention_ex(const void* h_Q, const void* h_K, const void* h_V,
+                                    void* h_Out, int q_len, int kv_len, int num_heads,
+                                    int num_kv_heads, int head_dim, int start_pos, float scale,
+                                    int causal, int dtype) {
+  // attention.hip:242-247
+  if (head_dim <= 0 || head_dim > 256)
+    return set_error(KVC_ERR_INVALID_ARG, "head_dim must be in (0, 256] for gqa_attention.");
+  if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
+  if (num_heads <= 0) return set_error(KVC_ERR_INVALID_ARG, "num_heads must be positive.");
+  if (q_len < 0 || kv_len < 0)
+    return set_error(KVC_ERR_INVALID_ARG, "q_len and kv_len must be non-negative.");
+  const int es = elem_size_of(dtype);
+  if (es == 0) return set_error(KVC_ERR_INVALID_ARG, "unsupported KV storage dtype %d.", dtype);
+  if (q_len == 0) return KVC_OK;
+  if (!h_Q || !h_Out || (kv_len > 0 && (!h_K || !h_V)))
+    return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
+
+  Singleton& S = singleton();  // one process-wide mutex, as bindings.cpp:18
+  std::lock_guard<std::mutex> lock(S.mu);
+  HostAttnCtx& C = host_attn_ctx();
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  int rc = ensure_stream(&C.stream, &C.stream_device, device);
+  if (rc) return rc;
+  const int pages = std::max(1, (kv_len + kDefaultPageSize - 1) / kDefaultPageSize);
+  PoolGeom g;
+  if ((rc = make_geom(1, pages, kDefaultPageSize, num_kv_heads, head_dim, dtype, &g))) return rc;
+  if ((rc = pool_alloc(&C.pool, g, device))) return rc;
+  if ((rc = ensure_identity_table(&C.bt, &C.bt_len, pages, C.stream))) return rc;
+  cudaStream_t s = C.stream;
+  const size_t kvb = static_cast<size_t>(kv_len) * num_kv_heads * head_dim * es;
+  const size_t qb = static_cast<size_t>(q_len) * num_heads * head_dim * es;
+  const size_t kvb_al = (kvb + 255) & ~static_cast<size_t>(255);
+  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
+  if ((e = C.bounce.ensure(2 * kvb_al + 2 * qb_al))) return cuda_error(e, "cudaMalloc(bounce)");
+  uint8_t* d = static_cast<uint8_t*>(C.bounce.ptr);
+  uint8_t *d_k = d, *d_v = d + kvb_al, *d_q = d + 2 * kvb_al, *d_out = d + 2 * kvb_al + qb_al;
+  if (kvb > 0 && ((e = cudaMemcpyAsync(d_k, h_K, kvb, cudaMemcpyHostToDevice, s)) ||
+                  (e = cudaMemcpyAsync(d_v, h_V, kvb, cudaMemcpyHostToDevice, s))))
+    return cuda_error(e, "cudaMemcpyAsync(H2D K/V)");
+  if ((e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpyAsync(H2D Q)");
+  const int32_t* bt = static_cast<const int32_t*>(C.bt.ptr);
+  if ((rc = do_append(&C.pool, 0, d_k, d_v, bt, C.bt_len, nullptr, nullptr, 0, kv_len, s)))
+    return rc;
+  rc = plan_queries(&C.plan, g, q_len, num_heads, start_pos, kv_len, causal != 0, device, s);
+  if (rc) return rc;
+  if ((rc = do_decode(&C.pool, &C.plan, 0, d_q, d_out, bt, C.bt_len, scale, s))) return rc;
+  if ((e = cudaMemcpyAsync(h_Out, d_out, qb, cudaMemcpyDeviceToHost, s)))
+    return cuda_error(e, "cudaMemcpyAsync(D2H)");
+  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  return check_device_error("gqa_attention");
+}
+
+extern "C" int kvc_gqa_attention(const void* h_Q, const void* h_K, const void* h_V, void* h_Out,
+                                 int q_len, int kv_len, int num_heads, int num_kv_heads,
+                                 int head_dim, int start_pos, float scale, int causal) {
+  return kvc_gqa_attention_ex(h_Q, h_K, h_V, h_Out, q_len, kv_len, num_heads, num_kv_heads,
+                              head_dim, start_pos, scale, causal, KVC_DTYPE_F16);
+}
+
+extern "C" int kvc_host_alloc(size_t bytes, void** out) {
+  if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");
+  *out = nullptr;
+  if (bytes == 0) return set_error(KVC_ERR_INVALID_ARG, "bytes must be positive.");
+  cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return cuda_error(e, "cudaHostAlloc");
+  }
+  return KVC_OK;
+}
+
+extern "C" int kvc_host_free(void* ptr) {
+  if (!ptr) return KVC_OK;
+  cudaError_t e = cudaFreeHost(ptr);
+  if (e != cudaSuccess) return cuda_error(e, "cudaFreeHost");
+  return KVC_OK;
+}

@@ -1,0 +1,144 @@
+// Internal interface between the host runtime (kvc_host.cpp, kvc_offload.cpp)
+// and the CUDA kernels (kvc_kernels.cu).  Not part of the public C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace kvc {
+
+// Running-max sentinel for "no position seen yet".  Finite on purpose: the
+// difference of two sentinels is 0, never NaN, and every weight that involves
+// an empty partial is multiplied by a zero sum.
+constexpr float kNegBig = -1.0e30f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Upper bound of one mbarrier wait before a kernel gives up and reports
+// KVC_DEVERR_WAIT_LIMIT (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Tokens per shared-memory slab.  A slab is the unit of one bulk copy per K and
+// per V: 16 positions x head_dim of one KV head, contiguous in the pool for
+// every layout and page size (page_size is a multiple of 16).
+constexpr int kSlab = 16;
+
+// ---- pool layouts -------------------------------------------------------------
+// A page-head is one contiguous block of page_size x head_dim elements.  Inside
+// it, positions and dims are arranged in 16-byte units (8 x 16-bit or 4 x fp32):
+//   kLayoutCore   (16-bit storage): unit (t, u) at ((t / 8) * U + u) * 8 + t % 8,
+//                 i.e. 8-position x 16-byte "core matrices" stored contiguously,
+//                 the operand tile shape of ldmatrix / mma (and of tcgen05's
+//                 no-swizzle canonical layout); reads are bank-conflict free.
+//   kLayoutLinear (fp32 storage):  unit (t, u) at t * U + u, row-major.
+// Both keep every 16-position slab contiguous, so a slab is one bulk copy.
+enum : int { kLayoutCore = 0, kLayoutLinear = 1 };
+
+__host__ __device__ __forceinline__ size_t unit_offset(int layout, int t, int u, int U) {
+  return layout == kLayoutCore ? (static_cast<size_t>((t >> 3) * U + u) * 8 + (t & 7))
+                               : (static_cast<size_t>(t) * U + u);
+}
+
+
+// Split-K chunk: every query's context is cut into splits of this many
+// positions (rounded up to a whole number of pages).  The partition depends
+// only on the context length, never on the storage mode, batch composition or
+// GPU count, so resident, offloaded and sharded runs add in the same order.
+constexpr int kSplitTokens = 512;
+
+struct PoolGeom {
+  int num_layers = 0;
+  int num_pages = 0;
+  int page_size = 0;
+  int num_kv_heads = 0;
+  int head_dim = 0;
+  int dtype = 0;       // KVC_DTYPE_*
+  int elem_size = 0;   // bytes per element
+  int layout = 0;      // kLayoutCore / kLayoutLinear
+  size_t page_head_bytes = 0;   // page_size * head_dim * elem_size
+  size_t page_bytes = 0;        // num_kv_heads * page_head_bytes
+  size_t layer_bytes = 0;       // num_pages * page_bytes
+};
+
+struct AppendArgs {
+  uint8_t* k_layer;
+  uint8_t* v_layer;
+  const uint8_t* k_new;          // (n, Hkv, D) token-major rows
+  const uint8_t* v_new;
+  const int32_t* block_tables;   // (rows, bt_stride)
+  const int32_t* rows;           // (n) block-table row per appended row, or null (row 0)
+  const int32_t* positions;      // (n) position per appended row, or null (pos0 + i)
+  int pos0;
+  int bt_stride;
+  int n;
+  int num_kv_heads;
+  int row_units;                 // head_dim * elem_size / 16
+  int page_size;
+  int num_pages;
+  int layout;
+  size_t page_head_bytes;
+};
+
+struct GatherArgs {
+  const uint8_t* k_layer;
+  const uint8_t* v_layer;
+  uint8_t* k_out;                // (count, Hkv, D)
+  uint8_t* v_out;
+  const int32_t* bt_row;         // block-table row of the sequence
+  int bt_stride;
+  int start;
+  int count;
+  int num_kv_heads;
+  int row_units;
+  int page_size;
+  int num_pages;
+  int layout;
+  size_t page_head_bytes;
+};
+
+// One split item: {query, split index, first position, end position}.
+// One query record: {block-table row, context length, first split slot, splits}.
+struct DecodeArgs {
+  const uint8_t* k_layer;
+  const uint8_t* v_layer;
+  const void* q;                 // (n_queries, H, D)
+  void* out;                     // (n_queries, H, D)
+  const int32_t* block_tables;
+  int bt_stride;
+  const int4* items;
+  const int4* qinfo;
+  float* part_o;                 // (split slots, H, D) fp32 partial outputs
+  float2* part_ml;               // (split slots, H) running max (log2 units) and sum
+  unsigned int* counters;        // (n_queries, Hkv, n_hchunk), zero between launches
+  int n_items;
+  int num_heads;
+  int num_kv_heads;
+  int group;                     // num_heads / num_kv_heads
+  int n_hchunk;                  // ceil(group / 8): q-head chunks per KV head
+  int head_dim;
+  int page_size;
+  int num_pages;
+  float scale_log2;              // scale * log2(e)
+};
+
+struct FillArgs {
+  uint8_t* base;                 // first byte of the range to fill
+  size_t n_elems;
+  uint64_t seed;
+  uint64_t index0;               // global element index of base (for reproducibility)
+  float stddev;
+  int dtype;
+};
+
+// Launchers: return cudaSuccess or the launch error.
+cudaError_t launch_append(const AppendArgs& a, int elem_size, cudaStream_t s);
+cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
+cudaError_t launch_fill_normal(const FillArgs& a, cudaStream_t s);
+// kind: 0 = tensor-core kernel, 1 = CUDA-core kernel (selected by the host).
+cudaError_t launch_decode(const DecodeArgs& a, int dtype, int layout, cudaStream_t s);
+bool decode_uses_mma(int dtype, int head_dim, int page_size);
+
+// Device error word (per device): read and optionally clear.
+cudaError_t read_device_error(uint32_t* code, uint32_t* info, bool clear);
+
+}  // namespace kvc

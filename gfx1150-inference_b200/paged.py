@@ -1,0 +1,237 @@
+"""Batched decode over a paged KV pool (torch device buffers + libkvcache.so).
+
+The reference keeps one sequence in an unpaged pool and "batches" with a
+sequential Python loop (src/inference.py:435-447).  This module is the batched
+form of the same path: many sequences share one pool of fixed-size pages,
+addressed through int32 block tables, and one decode step per layer appends the
+new K/V row of every sequence and attends over its whole cached context
+(the per-token append of attention.hip:410-415 and the attention of
+attention.hip:35-123, for a batch).
+
+Buffers are torch CUDA tensors; work is enqueued on torch's current stream
+unless a stream is given.  KV-head sharding across GPUs is a matter of
+building each rank's pool with its own ``num_kv_heads`` slice (see
+``shard_heads``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+import kvcache_ffi as ffi
+
+_TORCH_CODE = {torch.float16: ffi.DTYPE_F16, torch.bfloat16: ffi.DTYPE_BF16,
+               torch.float32: ffi.DTYPE_F32}
+
+
+def _sp(stream) -> Optional[int]:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream) or None
+
+
+def _i32(t: torch.Tensor) -> int:
+    if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError("block tables / rows / positions must be contiguous int32 CUDA tensors")
+    return int(t.data_ptr())
+
+
+def _dev(t: torch.Tensor, name: str, dtype: torch.dtype, numel: int) -> int:
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous {dtype} CUDA tensor")
+    if t.numel() < numel:
+        raise ValueError(f"{name} buffer is smaller than expected dimensions.")
+    return int(t.data_ptr())
+
+
+@dataclass
+class PlanInfo:
+    n_queries: int
+    n_items: int
+    n_ctas: int
+    scratch_bytes: int
+
+
+class DecodePlan:
+    """Split-K work list for one batch of queries (see kvc_plan_decode)."""
+
+    def __init__(self):
+        h = ctypes.c_void_p()
+        ffi.check(ffi.lib.kvc_plan_create(ctypes.byref(h)))
+        self.handle = h
+        self.n_queries = 0
+        self.num_heads = 0
+        self.ctx_lens: Optional[np.ndarray] = None
+
+    def info(self) -> PlanInfo:
+        n_items, n_ctas = ctypes.c_int(), ctypes.c_int()
+        scratch = ctypes.c_size_t()
+        ffi.check(ffi.lib.kvc_plan_info(self.handle, ctypes.byref(n_items), ctypes.byref(n_ctas),
+                                        ctypes.byref(scratch)))
+        return PlanInfo(self.n_queries, n_items.value, n_ctas.value, scratch.value)
+
+    def close(self):
+        if self.handle is not None:
+            ffi.check(ffi.lib.kvc_plan_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class PagedKVCache:
+    """Paged K/V pool for ``num_layers`` layers on one GPU."""
+
+    def __init__(self, num_layers: int, num_pages: int, page_size: int, num_kv_heads: int,
+                 head_dim: int, dtype: torch.dtype = torch.float16, device: int = 0):
+        if dtype not in _TORCH_CODE:
+            raise ValueError(f"unsupported KV storage dtype {dtype}")
+        h = ctypes.c_void_p()
+        ffi.check(ffi.lib.kvc_pool_create(num_layers, num_pages, page_size, num_kv_heads,
+                                          head_dim, _TORCH_CODE[dtype], device, ctypes.byref(h)))
+        self.handle = h
+        self.num_layers = num_layers
+        self.num_pages = num_pages
+        self.page_size = page_size
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.device = device
+
+    # -- synthetic contents ------------------------------------------------------
+    def fill_normal(self, seed: int, stddev: float = 1.0, layers=None, pages=None, stream=None):
+        l0, l1 = layers if layers is not None else (0, self.num_layers)
+        p0, p1 = pages if pages is not None else (0, self.num_pages)
+        ffi.check(ffi.lib.kvc_pool_fill_normal(self.handle, l0, l1, p0, p1, int(seed),
+                                               float(stddev), _sp(stream)))
+
+    def info(self):
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        lb, phb = ctypes.c_size_t(), ctypes.c_size_t()
+        ffi.check(ffi.lib.kvc_pool_info(self.handle, ctypes.byref(k), ctypes.byref(v),
+                                        ctypes.byref(lb), ctypes.byref(phb)))
+        return {"k": k.value, "v": v.value, "bytes_per_layer": lb.value,
+                "bytes_per_page_head": phb.value}
+
+    # -- plan / append / decode ---------------------------------------------------
+    def plan(self, ctx_lens: Sequence[int], num_heads: int, rows: Optional[Sequence[int]] = None,
+             plan: Optional[DecodePlan] = None, stream=None) -> DecodePlan:
+        """Plan attention for query i over positions [0, ctx_lens[i]) of block-table
+        row rows[i] (default i)."""
+        p = plan if plan is not None else DecodePlan()
+        ctx = np.ascontiguousarray(np.asarray(ctx_lens, dtype=np.int32))
+        r = None if rows is None else np.ascontiguousarray(np.asarray(rows, dtype=np.int32))
+        ffi.check(ffi.lib.kvc_plan_decode(p.handle, self.handle, ffi.np_ptr(r), ffi.np_ptr(ctx),
+                                          int(ctx.size), int(num_heads), _sp(stream)))
+        p.n_queries = int(ctx.size)
+        p.num_heads = int(num_heads)
+        p.ctx_lens = ctx
+        return p
+
+    def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor,
+               block_tables: torch.Tensor, positions: torch.Tensor,
+               rows: Optional[torch.Tensor] = None, stream=None):
+        n = int(positions.numel())
+        row_elems = self.num_kv_heads * self.head_dim
+        ffi.check(ffi.lib.kvc_append(
+            self.handle, layer, _dev(k_new, "k_new", self.dtype, n * row_elems),
+            _dev(v_new, "v_new", self.dtype, n * row_elems), _i32(block_tables),
+            int(block_tables.shape[-1]), None if rows is None else _i32(rows), _i32(positions), n,
+            _sp(stream)))
+
+    def decode(self, plan: DecodePlan, layer: int, q: torch.Tensor, out: torch.Tensor,
+               block_tables: torch.Tensor, scale: float, stream=None):
+        n = plan.n_queries * plan.num_heads * self.head_dim
+        ffi.check(ffi.lib.kvc_decode(
+            self.handle, plan.handle, layer, _dev(q, "q", self.dtype, n),
+            _dev(out, "out", self.dtype, n), _i32(block_tables), int(block_tables.shape[-1]),
+            float(scale), _sp(stream)))
+
+    def append_decode(self, plan: DecodePlan, layer: int, q: torch.Tensor, k_new: torch.Tensor,
+                      v_new: torch.Tensor, out: torch.Tensor, block_tables: torch.Tensor,
+                      scale: float, stream=None):
+        n = plan.n_queries * plan.num_heads * self.head_dim
+        nk = plan.n_queries * self.num_kv_heads * self.head_dim
+        ffi.check(ffi.lib.kvc_append_decode(
+            self.handle, plan.handle, layer, _dev(q, "q", self.dtype, n),
+            _dev(k_new, "k_new", self.dtype, nk), _dev(v_new, "v_new", self.dtype, nk),
+            _dev(out, "out", self.dtype, n), _i32(block_tables), int(block_tables.shape[-1]),
+            float(scale), _sp(stream)))
+
+    def decode_host(self, plan: DecodePlan, layer: int, h_q: torch.Tensor, h_k: torch.Tensor,
+                    h_v: torch.Tensor, h_out: torch.Tensor, block_tables: torch.Tensor,
+                    scale: float, stream=None):
+        """Reference-facing call: host (ideally pinned) buffers in, host result out."""
+        for name, t in (("q", h_q), ("k_new", h_k), ("v_new", h_v), ("out", h_out)):
+            if t.is_cuda or not t.is_contiguous() or t.dtype != self.dtype:
+                raise ValueError(f"{name} must be a contiguous {self.dtype} host tensor")
+        ffi.check(ffi.lib.kvc_decode_host(
+            self.handle, plan.handle, layer, int(h_q.data_ptr()), int(h_k.data_ptr()),
+            int(h_v.data_ptr()), int(h_out.data_ptr()), _i32(block_tables),
+            int(block_tables.shape[-1]), float(scale), _sp(stream)))
+
+    def gather(self, layer: int, block_tables: torch.Tensor, row: int, start: int, count: int,
+               stream=None):
+        k = torch.empty((count, self.num_kv_heads, self.head_dim), dtype=self.dtype,
+                        device=f"cuda:{self.device}")
+        v = torch.empty_like(k)
+        ffi.check(ffi.lib.kvc_gather(self.handle, layer, _i32(block_tables),
+                                     int(block_tables.shape[-1]), row, start, count,
+                                     int(k.data_ptr()), int(v.data_ptr()), _sp(stream)))
+        return k, v
+
+    def close(self):
+        if self.handle is not None:
+            ffi.check(ffi.lib.kvc_pool_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# -- layout helpers -------------------------------------------------------------------
+def pages_for(ctx_lens: Sequence[int], page_size: int) -> np.ndarray:
+    return np.array([(int(c) + page_size - 1) // page_size for c in ctx_lens], dtype=np.int64)
+
+
+def random_block_tables(ctx_lens: Sequence[int], page_size: int, seed: int):
+    """Block tables for sequences of the given lengths over a pool with exactly
+    the pages they need, assigned in a seeded random permutation (BASELINE
+    config 3: "paged fp16 pool of 16-token pages with a random page permutation").
+    Returns (table (n, max_pages) int32 numpy, total pages)."""
+    need = pages_for(ctx_lens, page_size)
+    total = int(need.sum())
+    perm = np.random.default_rng(seed).permutation(total).astype(np.int32)
+    width = int(need.max()) if len(need) else 1
+    table = np.full((len(need), max(1, width)), -1, dtype=np.int32)
+    o = 0
+    for i, n in enumerate(need):
+        table[i, :n] = perm[o:o + n]
+        o += int(n)
+    # unused tail entries point at page 0 (never read: beyond every context)
+    table[table < 0] = 0
+    return table, total
+
+
+def shard_heads(num_kv_heads: int, world: int, rank: int):
+    """KV heads [h0, h1) owned by `rank` when heads are split across `world` GPUs."""
+    if num_kv_heads % world != 0:
+        raise ValueError(f"{num_kv_heads} KV heads cannot be split evenly over {world} GPUs")
+    per = num_kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def default_scale(head_dim: int) -> float:
+    """1/sqrt(head_dim), the scale every caller passes (src/layer.py:181)."""
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,270 @@
+/*
+ * kvcache.h — C ABI of libkvcache.so, the B200 (sm_100a) KV-cache decode path.
+ *
+ * This library replaces the hot-path entry points of gfx1150-inference's pybind11
+ * `matmul_module` (src/python_bindings/bindings.cpp) and the HIP launchers behind
+ * them (src/kernels/attention.h).  Every function:
+ *   - takes plain pointers and sizes (no torch / numpy types),
+ *   - returns an int status (KVC_OK == 0), with a human-readable message available
+ *     from kvc_last_error() on the calling thread,
+ *   - maps the reference's C++ exception classes onto status codes:
+ *       std::invalid_argument -> KVC_ERR_INVALID_ARG   (Python ValueError)
+ *       std::out_of_range     -> KVC_ERR_OUT_OF_RANGE  (Python IndexError)
+ *       std::runtime_error    -> KVC_ERR_RUNTIME / KVC_ERR_CUDA / KVC_ERR_DEVICE
+ *                                                      (Python RuntimeError)
+ *
+ * Two families of entry points exist:
+ *   1. Reference-compatible process-wide pool ("kvc_cache_*", "kvc_gqa_attention*"):
+ *      same arguments, same validation order and same semantics as the reference's
+ *      DeviceKVCachePool singleton and its launchers.  Host-buffer variants copy in
+ *      and out like the reference; the *_device variant takes device pointers and a
+ *      cudaStream_t (passed as void*).
+ *   2. Handle-based paged pool for batched decode ("kvc_pool_*", "kvc_plan_*",
+ *      "kvc_append", "kvc_decode*", "kvc_gather"): many sequences, block tables of
+ *      fixed-size pages, one KV-head shard per GPU.  Device pointers + stream.
+ *   3. Host-streamed offload ("kvc_offload_*"): the --offload-kv-cpu / --kv-mmap-dir
+ *      modes.  KV lives in host memory; each call streams one layer to the GPU on a
+ *      copy stream, double-buffered, while the previous layer's attention runs.
+ *
+ * Numerics (all attention entry points): fp16 / bf16 / fp32 KV storage, fp32
+ * accumulation, online softmax, scores = (q . k) * scale with `scale` used exactly
+ * as given (0.0 gives all-equal scores, as in the reference kernel
+ * src/kernels/attention.hip:99), causal bound min(kv_len, start_pos + m + 1)
+ * (attention.hip:75), and an all-zero output row when no position is attended
+ * (attention.hip:115).
+ */
+#ifndef KVCACHE_H
+#define KVCACHE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KVC_API __attribute__((visibility("default")))
+#else
+#define KVC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define KVC_OK 0
+#define KVC_ERR_INVALID_ARG 1   /* reference: std::invalid_argument */
+#define KVC_ERR_OUT_OF_RANGE 2  /* reference: std::out_of_range */
+#define KVC_ERR_RUNTIME 3       /* reference: std::runtime_error (e.g. pool missing) */
+#define KVC_ERR_CUDA 4          /* reference: HIP_CHECK -> std::runtime_error */
+#define KVC_ERR_DEVICE 5        /* a kernel reported a bad page id or a wait limit */
+#define KVC_ERR_TIMEOUT 6       /* a host-side wait ran past its limit */
+
+/* ---- storage types --------------------------------------------------------- */
+#define KVC_DTYPE_F16 0
+#define KVC_DTYPE_BF16 1
+#define KVC_DTYPE_F32 2
+
+/* device error codes written by kernels (kvc_device_error) */
+#define KVC_DEVERR_NONE 0u
+#define KVC_DEVERR_BAD_PAGE 1u        /* block table entry outside [0, num_pages) */
+#define KVC_DEVERR_WAIT_LIMIT 2u      /* an mbarrier wait gave up after its limit */
+#define KVC_DEVERR_BAD_POSITION 3u    /* append position outside the block table */
+
+/* Library ABI version (bumped on any signature change). */
+KVC_API int kvc_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+KVC_API const char* kvc_last_error(void);
+
+/* Read (and optionally clear) the device-side error word of `device`.
+ * *code receives one of KVC_DEVERR_*, *info an auxiliary value (e.g. the bad page). */
+KVC_API int kvc_device_error(int device, int clear, uint32_t* code, uint32_t* info);
+
+/* Number of streaming multiprocessors of `device` (grid sizing helper). */
+KVC_API int kvc_device_sm_count(int device, int* out);
+
+/* ==== 1. Reference-compatible process-wide pool ============================ */
+
+/* Replaces init_device_kv_cache_fp16 (src/kernels/attention.h:27-32,
+ * attention.hip:286-296) behind matmul_module.kv_cache_init
+ * (src/python_bindings/bindings.cpp:468-472).  Allocates (or grows) the fp16
+ * pool for one sequence of up to max_seq_len positions in every layer.  Like the
+ * reference, memory is only reallocated when the new size exceeds the capacity
+ * and pool contents are not zeroed.  Fails with KVC_ERR_INVALID_ARG unless all
+ * dimensions are positive. */
+KVC_API int kvc_cache_init(int num_layers, int max_seq_len, int num_kv_heads, int head_dim);
+
+/* Extension of kvc_cache_init: storage dtype (KVC_DTYPE_*) and page size in
+ * positions (a multiple of 16; 0 selects 16). */
+KVC_API int kvc_cache_init_ex(int num_layers, int max_seq_len, int num_kv_heads, int head_dim,
+                      int dtype, int page_size);
+
+/* Replaces free_device_kv_cache_fp16 (attention.h:35, attention.hip:298-300)
+ * behind matmul_module.kv_cache_free (bindings.cpp:474-478). */
+KVC_API int kvc_cache_free(void);
+
+/* Storage dtype of the process-wide pool, or -1 if none is allocated. */
+KVC_API int kvc_cache_dtype(void);
+
+/* Replaces launch_gqa_attention_cached_fp16 (attention.h:41-54,
+ * attention.hip:302-374) behind matmul_module.gqa_attention_cached
+ * (bindings.cpp:480-514).  Host buffers in the pool's dtype:
+ *   h_Q (q_len, num_heads, head_dim), h_K_new / h_V_new (q_len, num_kv_heads,
+ *   head_dim), h_Out (q_len, num_heads, head_dim).
+ * Appends the q_len new rows at (layer_idx, start_pos) and attends over
+ * [0, start_pos + q_len).  Validation order and status codes follow
+ * attention.hip:316-329. */
+KVC_API int kvc_gqa_attention_cached(const void* h_Q, const void* h_K_new, const void* h_V_new,
+                             void* h_Out, int layer_idx, int q_len, int start_pos,
+                             int num_heads, int num_kv_heads, int head_dim, float scale,
+                             int causal);
+
+/* Replaces launch_gqa_attention_cached_fp16_device (attention.h:59-72,
+ * attention.hip:376-440): device pointers, work enqueued on `stream`
+ * (a cudaStream_t; NULL = legacy default stream), no host synchronisation. */
+KVC_API int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_new,
+                                    const void* d_V_new, void* d_Out, int layer_idx,
+                                    int q_len, int start_pos, int num_heads,
+                                    int num_kv_heads, int head_dim, float scale,
+                                    int causal, void* stream);
+
+/* Replaces launch_gqa_attention_fp16 (attention.h:10-23, attention.hip:228-284)
+ * behind matmul_module.gqa_attention (bindings.cpp:414-447): full K/V for one
+ * layer in host memory, token-major (kv_len, num_kv_heads, head_dim), fp16.
+ * Same validation as attention.hip:242-247. */
+KVC_API int kvc_gqa_attention(const void* h_Q, const void* h_K, const void* h_V, void* h_Out,
+                      int q_len, int kv_len, int num_heads, int num_kv_heads,
+                      int head_dim, int start_pos, float scale, int causal);
+
+/* kvc_gqa_attention with an explicit storage dtype (KVC_DTYPE_*). */
+KVC_API int kvc_gqa_attention_ex(const void* h_Q, const void* h_K, const void* h_V, void* h_Out,
+                         int q_len, int kv_len, int num_heads, int num_kv_heads,
+                         int head_dim, int start_pos, float scale, int causal,
+                         int dtype);
+
+/* Copy positions [start, start+count) of `layer_idx` out of the process-wide pool
+ * into host buffers laid out like the reference pool, (count, num_kv_heads,
+ * head_dim).  No reference counterpart: it exists so pool contents can be
+ * compared bit for bit with the reference's host-mode append (kv_cache.py:222-225). */
+KVC_API int kvc_cache_gather(int layer_idx, int start, int count, void* h_K_out, void* h_V_out);
+
+/* ==== 2. Paged pool for batched decode ==================================== */
+
+typedef struct kvc_pool kvc_pool_t;
+typedef struct kvc_plan kvc_plan_t;
+
+/* Create a paged pool on `device`: for every layer, num_pages pages, each holding
+ * page_size positions of num_kv_heads heads.  Storage is head-major inside a page
+ * (one contiguous page_size x head_dim block per head).  No reference counterpart
+ * beyond DeviceKVCachePool (attention.hip:168-214), which is the one-sequence,
+ * unpaged special case. */
+KVC_API int kvc_pool_create(int num_layers, int num_pages, int page_size, int num_kv_heads,
+                    int head_dim, int dtype, int device, kvc_pool_t** out);
+KVC_API int kvc_pool_destroy(kvc_pool_t* pool);
+
+/* Device base addresses and sizes of the pool (for tests and diagnostics). */
+KVC_API int kvc_pool_info(const kvc_pool_t* pool, void** k_base, void** v_base,
+                  size_t* bytes_per_layer, size_t* bytes_per_page_head);
+
+/* Fill pages [page_begin, page_end) of layers [layer_begin, layer_end) with
+ * seeded N(0, stddev^2) values (synthetic benchmark data), on `stream`. */
+KVC_API int kvc_pool_fill_normal(kvc_pool_t* pool, int layer_begin, int layer_end, int page_begin,
+                         int page_end, uint64_t seed, float stddev, void* stream);
+
+/* Append n token rows.  d_k_new / d_v_new: (n, num_kv_heads, head_dim) in the
+ * pool dtype.  Row i goes to sequence d_rows[i] (a block-table row; NULL means
+ * row 0 for every i) at position d_positions[i].  d_block_tables: int32
+ * (n_rows, bt_stride) page ids.  The fused, vectorised replacement of the
+ * reference's two blocking row copies (attention.hip:336-341, :410-415). */
+KVC_API int kvc_append(kvc_pool_t* pool, int layer, const void* d_k_new, const void* d_v_new,
+               const int32_t* d_block_tables, int bt_stride, const int32_t* d_rows,
+               const int32_t* d_positions, int n, void* stream);
+
+/* A decode plan: the split-K work list for one batch of queries, reused by every
+ * layer of a step.  The split of a query depends only on its context length. */
+KVC_API int kvc_plan_create(kvc_plan_t** out);
+KVC_API int kvc_plan_destroy(kvc_plan_t* plan);
+
+/* Build the plan on the host and upload it on `stream`.  Query i reads the block
+ * table row h_rows[i] (NULL: row i) over positions [0, h_ctx_lens[i]).  The
+ * queries' q rows are (num_heads, head_dim) at index i of the q buffer. */
+KVC_API int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const int32_t* h_rows,
+                    const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                    void* stream);
+
+/* Number of split items, CTAs and bytes of split scratch of the last plan. */
+KVC_API int kvc_plan_info(const kvc_plan_t* plan, int* n_items, int* n_ctas, size_t* scratch_bytes);
+
+/* Split-K GQA decode attention for one layer.  d_q, d_out: (n_queries,
+ * num_heads, head_dim) in the pool dtype.  Replaces gqa_online_softmax_kernel
+ * (attention.hip:35-123) for a batch of queries over a paged pool. */
+KVC_API int kvc_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int layer, const void* d_q,
+               void* d_out, const int32_t* d_block_tables, int bt_stride, float scale,
+               void* stream);
+
+/* Fused decode step for one layer on device buffers: appends row i of
+ * d_k_new / d_v_new ((n_queries, num_kv_heads, head_dim)) at position
+ * ctx_len[i]-1 of the query's block-table row (the plan's context lengths
+ * include the new token), then runs kvc_decode.  The batched counterpart of
+ * launch_gqa_attention_cached_fp16_device (attention.hip:376-440). */
+KVC_API int kvc_append_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int layer, const void* d_q,
+                      const void* d_k_new, const void* d_v_new, void* d_out,
+                      const int32_t* d_block_tables, int bt_stride, float scale, void* stream);
+
+/* Reference-facing batched call with HOST buffers: copies h_q, h_k_new, h_v_new
+ * to the device, appends and attends like kvc_append_decode, copies the result
+ * to h_out and waits for it, like launch_gqa_attention_cached_fp16
+ * (attention.hip:302-374) but for a batch of sequences. */
+KVC_API int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer, const void* h_q,
+                    const void* h_k_new, const void* h_v_new, void* h_out,
+                    const int32_t* d_block_tables, int bt_stride, float scale, void* stream);
+
+/* Copy positions [start, start+count) of block-table row `row` in `layer` into
+ * device buffers (count, num_kv_heads, head_dim) on `stream`. */
+KVC_API int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_tables, int bt_stride,
+               int row, int start, int count, void* d_k_out, void* d_v_out, void* stream);
+
+/* ==== 3. Host-streamed offload (--offload-kv-cpu / --kv-mmap-dir) ========== */
+
+typedef struct kvc_offload kvc_offload_t;
+
+/* Page-locked host memory for the offload pools. */
+KVC_API int kvc_host_alloc(size_t bytes, void** out);
+KVC_API int kvc_host_free(void* ptr);
+
+#define KVC_OFFLOAD_PINNED 1   /* h_k / h_v came from kvc_host_alloc */
+#define KVC_OFFLOAD_REGISTER 2 /* try cudaHostRegister on h_k / h_v */
+
+/* Attach host KV pools laid out as the reference's host arrays,
+ * (num_layers, max_seq_len, num_kv_heads, head_dim) (src/kv_cache.py:97, :133-135
+ * and the mmap arrays of :100-132).  The caller keeps ownership of h_k / h_v.
+ * When the memory is neither pinned nor registrable, copies go through pinned
+ * bounce buffers. */
+KVC_API int kvc_offload_create(void* h_k, void* h_v, int num_layers, int max_seq_len,
+                       int num_kv_heads, int head_dim, int dtype, int flags, int device,
+                       kvc_offload_t** out);
+KVC_API int kvc_offload_destroy(kvc_offload_t* off);
+
+/* Offload-mode attend, the replacement of KVCacheManager.attend's offload branch
+ * (src/kv_cache.py:219-239) plus launch_gqa_attention_fp16 (attention.hip:228-284):
+ * writes the q_len new rows into the host pools at (layer_idx, start_pos), makes
+ * rows [0, start_pos+q_len) of the layer resident on the GPU (reusing the copy
+ * prefetched during the previous call when it is still valid), attends, copies
+ * h_Out back, and starts prefetching the next layer.  Results are bit-identical
+ * to the GPU-resident pool's for the same inputs. */
+KVC_API int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const void* h_K_new,
+                       const void* h_V_new, void* h_Out, int layer_idx, int q_len,
+                       int start_pos, int num_heads, float scale, int causal);
+
+/* Discard prefetched layers (call after the host pools were written elsewhere). */
+KVC_API int kvc_offload_invalidate(kvc_offload_t* off);
+
+/* Cumulative host-to-device bytes and copy-engine time (ms) of the offload path,
+ * and how many attend calls found their layer already prefetched. */
+KVC_API int kvc_offload_stats(const kvc_offload_t* off, double* h2d_bytes, double* h2d_ms,
+                      int64_t* prefetch_hits, int64_t* attend_calls);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVCACHE_H */

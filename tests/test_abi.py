@@ -1,0 +1,86 @@
+"""The C ABI: libkvcache.so loads and exports every symbol include/kvcache.h
+declares; argument errors that need no GPU map to the reference's exception
+classes (CPU only, no compute calls)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import kvcache_ffi as ffi
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "kvcache.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^KVC_API\s+(?:const\s+)?\w+\s*\*?\s*(kvc_\w+)\s*\(", text,
+                                 flags=re.M)))
+
+
+def test_header_declares_the_reference_entry_points():
+    names = declared_symbols()
+    for required in ("kvc_cache_init", "kvc_cache_free", "kvc_gqa_attention_cached",
+                     "kvc_gqa_attention_cached_device", "kvc_gqa_attention",
+                     "kvc_offload_attend", "kvc_decode", "kvc_append", "kvc_last_error"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", ffi.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [n for n in declared_symbols() if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    extra = sorted(n for n in exported if n.startswith("kvc_") and n not in declared_symbols())
+    assert not extra, f"exported but not declared: {extra}"
+
+
+def test_ffi_binds_every_declared_symbol():
+    assert sorted(ffi.SIGNATURES) == declared_symbols()
+    for name in declared_symbols():
+        assert getattr(ffi.lib, name) is not None
+
+
+def test_version_and_no_error_initially():
+    assert ffi.lib.kvc_version() == 1
+
+
+def test_invalid_arguments_map_to_reference_exceptions():
+    # init_device_kv_cache_fp16 rejects non-positive dims with invalid_argument
+    # (attention.hip:292-294) -> ValueError
+    with pytest.raises(ValueError, match="positive"):
+        ffi.check(ffi.lib.kvc_cache_init(0, 16, 2, 32))
+    h = ctypes.c_void_p()
+    with pytest.raises(ValueError, match="page_size"):
+        ffi.check(ffi.lib.kvc_pool_create(1, 4, 10, 2, 64, ffi.DTYPE_F16, 0, ctypes.byref(h)))
+    with pytest.raises(ValueError, match="head_dim"):
+        ffi.check(ffi.lib.kvc_pool_create(1, 4, 16, 2, 300, ffi.DTYPE_F16, 0, ctypes.byref(h)))
+    # gqa_attention checks (attention.hip:242-247) run before any device work
+    with pytest.raises(ValueError, match="head_dim"):
+        ffi.check(ffi.lib.kvc_gqa_attention(None, None, None, None, 1, 1, 4, 2, 512, 0, 0.0, 1))
+    with pytest.raises(ValueError, match="divisible"):
+        ffi.check(ffi.lib.kvc_gqa_attention(None, None, None, None, 1, 1, 5, 2, 64, 0, 0.0, 1))
+    # the cached path without a pool: runtime_error (attention.hip:317-319)
+    ffi.lib.kvc_cache_free()
+    with pytest.raises(RuntimeError, match="not initialized"):
+        ffi.check(ffi.lib.kvc_gqa_attention_cached(None, None, None, None, 0, 1, 0, 4, 2, 32,
+                                                   0.0, 1))
+    assert "not initialized" in ffi.last_error()
+
+
+def test_status_code_mapping():
+    with pytest.raises(IndexError):
+        ffi.check(ffi.KVC_ERR_OUT_OF_RANGE)
+    with pytest.raises(ffi.KVCacheDeviceError):
+        ffi.check(ffi.KVC_ERR_DEVICE)
+    with pytest.raises(TimeoutError):
+        ffi.check(ffi.KVC_ERR_TIMEOUT)
+    with pytest.raises(RuntimeError):
+        ffi.check(ffi.KVC_ERR_CUDA)
+    ffi.check(ffi.KVC_OK)

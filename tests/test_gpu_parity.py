@@ -1,0 +1,410 @@
+"""CUDA parity tests (B200): every entry point against the pinned oracle.
+
+Tolerances (BASELINE north star and the reference's own tests):
+  fp32 storage                 max-abs <= 1e-5
+  fp16 storage, fp32 accumulate max-abs <= 2e-3 * max(1, max|ref|)
+                               (test_layer.py:179 uses 2e-3, test_full_model.py:104/124 1e-3)
+  pool contents, offload vs resident, fused vs separate calls: bit-exact.
+"""
+
+from __future__ import annotations
+
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+import cases
+import gqa_ref
+from conftest import HAS_GPU
+
+pytestmark = pytest.mark.gpu
+
+if HAS_GPU:
+    import torch
+
+    import kvcache_ffi as ffi
+    import matmul_module
+    import paged
+    from kv_cache import KVCacheManager
+
+G = cases.load_golden() if HAS_GPU else {}
+
+
+def _fp16_tol(ref):
+    return 2e-3 * max(1.0, float(np.max(np.abs(ref.astype(np.float32)))))
+
+
+def _maxerr(a, b):
+    return float(np.max(np.abs(a.astype(np.float32) - b.astype(np.float32))))
+
+
+@pytest.fixture(autouse=True)
+def _clean(cuda_device):
+    yield
+    KVCacheManager._active_gpu_instance = False
+    matmul_module.kv_cache_free()
+    code, info = ffi.device_error(0, clear=True)
+    assert code == 0, f"device error word left set: {code} {info}"
+
+
+# ---------------------------------------------------------------------------
+# host full-KV entry (matmul_module.gqa_attention, attention.hip:228-284)
+# ---------------------------------------------------------------------------
+def test_reference_layer_cases_gqa_attention():
+    """tests/test_layer.py:155-184 through the drop-in gqa_attention."""
+    for i, c in enumerate(cases.layer_cases()):
+        out = np.zeros_like(c["Q"])
+        matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out, c["q_len"], c["kv_len"], 16, 4,
+                                    64, c["start_pos"], c["scale"], True)
+        assert _maxerr(out, G[f"layer{i}_out"]) < 2e-3
+
+
+@pytest.mark.parametrize("name", list(cases.EDGE_CASES))
+def test_edge_cases_gqa_attention(name):
+    c = cases.edge_case(name)
+    ref = G[f"{name}_out"]
+    out = np.zeros_like(c["Q"])
+    H, D = c["Q"].shape[1], c["Q"].shape[2]
+    Hkv = c["K"].shape[1]
+    matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out, c["q_len"], c["kv_len"], H, Hkv, D,
+                                c["start_pos"], c["scale"], c["causal"])
+    if c["Q"].dtype == np.float32:
+        assert _maxerr(out, ref) <= 1e-5
+    else:
+        assert _maxerr(out, ref) <= _fp16_tol(ref)
+
+
+def test_scale_zero_follows_the_kernel():
+    """scale = 0 gives equal scores (attention.hip:99): output = mean of V."""
+    c = cases.edge_case("scale_custom")
+    out = np.zeros_like(c["Q"])
+    matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out, 1, c["kv_len"], 8, 2, 64,
+                                c["start_pos"], 0.0, True)
+    expect = gqa_ref.online_softmax_attention(c["Q"], c["K"], c["V"], c["start_pos"], 0.0)
+    assert _maxerr(out, expect) <= 2e-3
+
+
+def test_empty_context_gives_zeros():
+    """kv_len = 0: nothing attended -> zero rows (attention.hip:115)."""
+    q = np.ones((2, 4, 32), np.float16)
+    out = np.full_like(q, 7)
+    k = np.zeros((0, 2, 32), np.float16)
+    matmul_module.gqa_attention(q, k, k, out, 2, 0, 4, 2, 32, 0, 0.2, False)
+    assert not out.any()
+
+
+# ---------------------------------------------------------------------------
+# GPU-resident pool (kv_cache_init / gqa_attention_cached / KVCacheManager)
+# ---------------------------------------------------------------------------
+def test_gpu_kv_cache_manager_reference_sequence():
+    """tests/test_full_model.py:78-129 with the drop-in KVCacheManager."""
+    c = cases.kv_manager_case()
+    L, H, Hkv, D = c["num_layers"], c["num_heads"], c["num_kv_heads"], c["head_dim"]
+    with KVCacheManager(L, c["max_seq_len"], Hkv, D) as kv:
+        for l in range(L):
+            out = np.zeros((4, H, D), np.float16)
+            kv.attend(c["Q"][l, :4], c["K"][l, :4], c["V"][l, :4], out, layer_idx=l, q_len=4,
+                      start_pos=0, num_heads=H, scale=c["scale"], causal=True)
+            assert _maxerr(out, G[f"kvm_prefill_l{l}"]) < 1e-3
+        for pos in (4, 5):
+            for l in range(L):
+                out = np.zeros((1, H, D), np.float16)
+                kv.attend(c["Q"][l, pos:pos + 1], c["K"][l, pos:pos + 1], c["V"][l, pos:pos + 1],
+                          out, layer_idx=l, q_len=1, start_pos=pos, num_heads=H,
+                          scale=c["scale"], causal=True)
+                assert _maxerr(out, G[f"kvm_decode_l{l}_p{pos}"]) < 1e-3
+        assert kv.current_seq_len == 6
+        # pool contents are bit-exact with the reference's host-mode append
+        for l in range(L):
+            k, v = matmul_module.kv_cache_gather(l, 0, 6)
+            np.testing.assert_array_equal(k, c["K"][l, :6])
+            np.testing.assert_array_equal(v, c["V"][l, :6])
+
+
+def test_config1_fp32_pool_within_1e5():
+    """fp32 pool, 511 cached + 1 appended, max-abs 1e-5."""
+    c = cases.config1_case()
+    P, H, Hkv, D = c["kv_len"], 32, 4, 64
+    matmul_module.kv_cache_init_ex(1, P, Hkv, D, dtype=np.float32)
+    q_pre = np.zeros((P - 1, H, D), np.float32)  # prefill rows (outputs unused)
+    out_pre = np.zeros_like(q_pre)
+    matmul_module.gqa_attention_cached(q_pre, c["K"][:P - 1], c["V"][:P - 1], out_pre, 0, P - 1,
+                                       0, H, Hkv, D, c["scale"], True)
+    out = np.zeros((1, H, D), np.float32)
+    matmul_module.gqa_attention_cached(c["Q"], c["K"][P - 1:], c["V"][P - 1:], out, 0, 1, P - 1,
+                                       H, Hkv, D, c["scale"], True)
+    assert _maxerr(out, G["config1_out_f32"]) <= 1e-5
+    k, v = matmul_module.kv_cache_gather(0, 0, P)
+    np.testing.assert_array_equal(k, c["K"])
+    np.testing.assert_array_equal(v, c["V"])
+
+
+def test_cached_prefill_matches_host_attention_bit_exact():
+    """The cached path and the full-KV host path share kernels and splits."""
+    c = cases.edge_case("split_boundary_1025")
+    H, Hkv, D, P = 8, 2, 128, c["kv_len"]
+    matmul_module.kv_cache_init(1, 2048, Hkv, D)
+    rng = np.random.default_rng(5)
+    qp = (rng.standard_normal((P - 1, H, D), dtype=np.float32) * 0.5).astype(np.float16)
+    outp = np.zeros_like(qp)
+    matmul_module.gqa_attention_cached(qp, c["K"][:P - 1], c["V"][:P - 1], outp, 0, P - 1, 0, H,
+                                       Hkv, D, c["scale"], True)
+    out = np.zeros_like(c["Q"])
+    matmul_module.gqa_attention_cached(c["Q"], c["K"][P - 1:], c["V"][P - 1:], out, 0, 1, P - 1,
+                                       H, Hkv, D, c["scale"], True)
+    assert _maxerr(out, G["split_boundary_1025_out"]) <= _fp16_tol(G["split_boundary_1025_out"])
+    out2 = np.zeros_like(c["Q"])
+    matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out2, 1, P, H, Hkv, D, P - 1, c["scale"])
+    np.testing.assert_array_equal(out, out2)
+    # prefill row m of the cached call == a single decode query at position m
+    outp2 = np.zeros_like(qp[:3])
+    matmul_module.gqa_attention(qp[600:603], c["K"][:603], c["V"][:603], outp2, 3, 603, H, Hkv,
+                                D, 600, c["scale"])
+    np.testing.assert_array_equal(outp[600:603], outp2)
+
+
+def test_validation_matches_reference_exception_classes():
+    matmul_module.kv_cache_init(2, 16, 2, 32)
+    q = np.zeros((1, 4, 32), np.float16)
+    kn = np.zeros((1, 2, 32), np.float16)
+    out = np.zeros_like(q)
+    with pytest.raises(IndexError, match="layer_idx"):
+        matmul_module.gqa_attention_cached(q, kn, kn, out, 2, 1, 0, 4, 2, 32)
+    with pytest.raises(IndexError, match="max_seq_len"):
+        matmul_module.gqa_attention_cached(q, kn, kn, out, 0, 1, 16, 4, 2, 32)
+    with pytest.raises(IndexError, match="max_seq_len"):
+        matmul_module.gqa_attention_cached(q, kn, kn, out, 0, 1, -1, 4, 2, 32)
+    with pytest.raises(ValueError, match="mismatch"):
+        matmul_module.gqa_attention_cached(q, kn, kn, out, 0, 1, 0, 4, 1, 32)
+    with pytest.raises(ValueError, match="FP16"):
+        matmul_module.gqa_attention_cached(q.astype(np.float32), kn, kn, out, 0, 1, 0, 4, 2, 32)
+    with pytest.raises(ValueError, match="C-contiguous"):
+        matmul_module.gqa_attention_cached(np.zeros((1, 4, 64), np.float16)[:, :, ::2], kn, kn,
+                                           out, 0, 1, 0, 4, 2, 32)
+    ro = out.copy()
+    ro.flags.writeable = False
+    with pytest.raises(ValueError, match="writeable"):
+        matmul_module.gqa_attention_cached(q, kn, kn, ro, 0, 1, 0, 4, 2, 32)
+    with pytest.raises(ValueError, match="smaller"):
+        matmul_module.gqa_attention_cached(q, kn, kn, out[:, :2], 0, 1, 0, 4, 2, 32)
+    # grow-only re-init keeps working; free + call -> RuntimeError
+    matmul_module.kv_cache_init(1, 8, 2, 32)
+    matmul_module.gqa_attention_cached(q, kn, kn, out, 0, 1, 0, 4, 2, 32)
+    matmul_module.kv_cache_free()
+    with pytest.raises(RuntimeError, match="not initialized"):
+        matmul_module.gqa_attention_cached(q, kn, kn, out, 0, 1, 0, 4, 2, 32)
+
+
+# ---------------------------------------------------------------------------
+# offload modes: bit-identical to the resident pool
+# ---------------------------------------------------------------------------
+def _run_sequence(kv, c, chunk=None):
+    """Prefill 8 positions (optionally chunked) then decode 3, over all layers."""
+    L, H, D = c["L"], c["H"], c["D"]
+    outs = []
+    pos = 0
+    spans = [(0, 8)] if chunk is None else [(s, min(8, s + chunk)) for s in range(0, 8, chunk)]
+    spans += [(8, 9), (9, 10), (10, 11)]
+    for s, e in spans:
+        for l in range(L):
+            out = np.zeros((e - s, H, D), np.float16)
+            kv.attend(c["Q"][l, s:e], c["K"][l, s:e], c["V"][l, s:e], out, layer_idx=l,
+                      q_len=e - s, start_pos=s, num_heads=H, scale=c["scale"], causal=True)
+            outs.append((l, s, e, out))
+        pos = e
+    assert kv.current_seq_len == pos
+    return outs
+
+
+def _seq_case():
+    rng = np.random.default_rng(77)
+    L, T, H, Hkv, D = 3, 11, 8, 2, 64
+    return dict(L=L, H=H, Hkv=Hkv, D=D, scale=0.125,
+                Q=(rng.standard_normal((L, T, H, D), dtype=np.float32) * 0.5).astype(np.float16),
+                K=(rng.standard_normal((L, T, Hkv, D), dtype=np.float32) * 0.5).astype(np.float16),
+                V=(rng.standard_normal((L, T, Hkv, D), dtype=np.float32) * 0.5).astype(np.float16))
+
+
+def _by_position(outs):
+    rows = {}
+    for l, s, e, out in outs:
+        for i in range(e - s):
+            rows[(l, s + i)] = out[i]
+    return rows
+
+
+def test_offload_cpu_and_mmap_bit_identical_to_resident():
+    c = _seq_case()
+    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"]) as kv:
+        gpu = _by_position(_run_sequence(kv, c))
+    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], offload_to_cpu=True) as kv:
+        cpu = _by_position(_run_sequence(kv, c))
+        st = kv.offload_stats()
+        assert st["attend_calls"] == 4 * c["L"] and st["prefetch_hits"] >= 3 * c["L"] - 1
+        assert st["h2d_bytes"] > 0
+        np.testing.assert_array_equal(kv._k_host[:, :11], c["K"])  # host append, bit-exact
+    with tempfile.TemporaryDirectory() as d:
+        with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], mmap_dir=d) as kv:
+            mm = _by_position(_run_sequence(kv, c))
+    for key in gpu:
+        np.testing.assert_array_equal(cpu[key], gpu[key], err_msg=str(key))
+        np.testing.assert_array_equal(mm[key], gpu[key], err_msg=str(key))
+    for (l, p), row in gpu.items():
+        ref = gqa_ref.ref_gqa_attention(c["Q"][l, p:p + 1], c["K"][l, :p + 1], c["V"][l, :p + 1],
+                                        p, c["scale"])[0]
+        assert _maxerr(row, ref) < 2e-3
+
+
+def test_chunked_prefill_bit_identical():
+    """test_phase5_scale.py:199-206 (full vs chunked prefill) at the attention level."""
+    c = _seq_case()
+    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"]) as kv:
+        full = _by_position(_run_sequence(kv, c))
+        kv.reset()
+        chunked = _by_position(_run_sequence(kv, c, chunk=3))
+    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], offload_to_cpu=True) as kv:
+        off_chunked = _by_position(_run_sequence(kv, c, chunk=2))
+    for key in full:
+        np.testing.assert_array_equal(chunked[key], full[key])
+        np.testing.assert_array_equal(off_chunked[key], full[key])
+
+
+# ---------------------------------------------------------------------------
+# paged batched decode
+# ---------------------------------------------------------------------------
+def _ragged_pool(page_size=16, dtype=None, seed=3):
+    dtype = dtype or torch.float16
+    c = cases.ragged_case()
+    n, H, Hkv, D = len(c["ctx"]), c["H"], c["Hkv"], c["D"]
+    table, total = paged.random_block_tables(c["ctx"], page_size, seed)
+    pool = paged.PagedKVCache(1, total + 3, page_size, Hkv, D, dtype=dtype)
+    bt = torch.from_numpy(table).cuda()
+    for i, ctx in enumerate(c["ctx"]):
+        k = torch.from_numpy(c["ks"][i]).cuda().to(dtype)
+        v = torch.from_numpy(c["vs"][i]).cuda().to(dtype)
+        pos = torch.arange(ctx, dtype=torch.int32, device="cuda")
+        rows = torch.full((ctx,), i, dtype=torch.int32, device="cuda")
+        pool.append(0, k, v, bt, pos, rows)
+    torch.cuda.synchronize()
+    return c, pool, bt
+
+
+def test_paged_ragged_batch_decode_and_pool_bit_exact():
+    c, pool, bt = _ragged_pool()
+    plan = pool.plan(c["ctx"], c["H"])
+    q = torch.from_numpy(c["q"]).cuda()
+    out = torch.zeros_like(q)
+    pool.decode(plan, 0, q, out, bt, c["scale"])
+    res = out.cpu().numpy()
+    assert _maxerr(res, G["ragged_out"]) <= _fp16_tol(G["ragged_out"])
+    for i, ctx in enumerate(c["ctx"]):
+        k, v = pool.gather(0, bt, i, 0, ctx)
+        np.testing.assert_array_equal(k.cpu().numpy(), c["ks"][i])
+        np.testing.assert_array_equal(v.cpu().numpy(), c["vs"][i])
+    # one batched call == one call per sequence (the reference's sequential batch)
+    for i, ctx in enumerate(c["ctx"]):
+        p1 = pool.plan([ctx], c["H"], rows=[i])
+        o1 = torch.zeros_like(q[i:i + 1])
+        pool.decode(p1, 0, q[i:i + 1].contiguous(), o1, bt, c["scale"])
+        assert torch.equal(o1[0], out[i])
+
+
+@pytest.mark.parametrize("page_size", [32, 64])
+def test_page_size_does_not_change_results(page_size):
+    c, pool16, bt16 = _ragged_pool(16)
+    c, poolp, btp = _ragged_pool(page_size, seed=11)
+    q = torch.from_numpy(c["q"]).cuda()
+    o16, op = torch.zeros_like(q), torch.zeros_like(q)
+    pool16.decode(pool16.plan(c["ctx"], c["H"]), 0, q, o16, bt16, c["scale"])
+    poolp.decode(poolp.plan(c["ctx"], c["H"]), 0, q, op, btp, c["scale"])
+    assert torch.equal(o16, op)
+
+
+def test_append_decode_fused_equals_separate_and_host_call():
+    rng = np.random.default_rng(9)
+    H, Hkv, D, ps = 32, 8, 128, 16
+    ctx = [1000, 1, 2049, 17, 512]
+    table, total = paged.random_block_tables(ctx, ps, 4)
+    pool = paged.PagedKVCache(2, total, ps, Hkv, D)
+    pool.fill_normal(seed=1)
+    bt = torch.from_numpy(table).cuda()
+    n = len(ctx)
+    q = torch.from_numpy(rng.standard_normal((n, H, D), dtype=np.float32)).half().cuda()
+    kn = torch.from_numpy(rng.standard_normal((n, Hkv, D), dtype=np.float32)).half().cuda()
+    vn = torch.from_numpy(rng.standard_normal((n, Hkv, D), dtype=np.float32)).half().cuda()
+    plan = pool.plan(ctx, H)
+    o_fused = torch.zeros_like(q)
+    pool.append_decode(plan, 1, q, kn, vn, o_fused, bt, 0.088)
+    pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32, device="cuda")
+    rows = torch.arange(n, dtype=torch.int32, device="cuda")
+    pool.append(1, kn, vn, bt, pos, rows)
+    o_sep = torch.zeros_like(q)
+    pool.decode(plan, 1, q, o_sep, bt, 0.088)
+    assert torch.equal(o_fused, o_sep)
+    hq, hk, hv = q.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    ho = torch.zeros_like(hq).pin_memory()
+    pool.decode_host(plan, 1, hq, hk, hv, ho, bt, 0.088)
+    assert torch.equal(ho, o_fused.cpu())
+    # against the oracle, from the gathered pool contents
+    for i, c in enumerate(ctx):
+        k, v = pool.gather(1, bt, i, 0, c)
+        assert torch.equal(k[c - 1], kn[i]) and torch.equal(v[c - 1], vn[i])
+        ref = gqa_ref.ref_gqa_attention(q[i:i + 1].cpu().numpy(), k.cpu().numpy(),
+                                        v.cpu().numpy(), c - 1, 0.088)
+        assert _maxerr(o_fused[i:i + 1].cpu().numpy(), ref) <= _fp16_tol(ref)
+
+
+def test_bf16_pool_against_fp32_reference():
+    rng = np.random.default_rng(12)
+    H, Hkv, D, ps = 16, 2, 128, 16
+    ctx = [700, 33]
+    table, total = paged.random_block_tables(ctx, ps, 2)
+    pool = paged.PagedKVCache(1, total, ps, Hkv, D, dtype=torch.bfloat16)
+    bt = torch.from_numpy(table).cuda()
+    ks = [torch.from_numpy(rng.standard_normal((c, Hkv, D), dtype=np.float32)).bfloat16().cuda()
+          for c in ctx]
+    vs = [torch.from_numpy(rng.standard_normal((c, Hkv, D), dtype=np.float32)).bfloat16().cuda()
+          for c in ctx]
+    for i, c in enumerate(ctx):
+        pool.append(0, ks[i], vs[i], bt, torch.arange(c, dtype=torch.int32, device="cuda"),
+                    torch.full((c,), i, dtype=torch.int32, device="cuda"))
+    q = torch.from_numpy(rng.standard_normal((2, H, D), dtype=np.float32)).bfloat16().cuda()
+    out = torch.zeros_like(q)
+    pool.decode(pool.plan(ctx, H), 0, q, out, bt, 0.09)
+    for i, c in enumerate(ctx):
+        ref = gqa_ref.ref_gqa_attention(q[i:i + 1].float().cpu().numpy(),
+                                        ks[i].float().cpu().numpy(), vs[i].float().cpu().numpy(),
+                                        c - 1, 0.09, out_dtype=np.float32)
+        assert _maxerr(out[i:i + 1].float().cpu().numpy(), ref) < 2e-2
+
+
+def test_head_dim_80_uses_cuda_core_path():
+    rng = np.random.default_rng(13)
+    H, Hkv, D, P = 8, 2, 80, 333
+    Q = (rng.standard_normal((1, H, D), dtype=np.float32) * 0.5).astype(np.float16)
+    K = (rng.standard_normal((P, Hkv, D), dtype=np.float32) * 0.5).astype(np.float16)
+    V = (rng.standard_normal((P, Hkv, D), dtype=np.float32) * 0.5).astype(np.float16)
+    out = np.zeros_like(Q)
+    matmul_module.gqa_attention(Q, K, V, out, 1, P, H, Hkv, D, P - 1, 0.11)
+    ref = gqa_ref.ref_gqa_attention(Q, K, V, P - 1, 0.11)
+    assert _maxerr(out, ref) <= 2e-3
+
+
+def test_bad_block_table_is_reported_and_context_survives():
+    H, Hkv, D, ps = 8, 2, 64, 16
+    pool = paged.PagedKVCache(1, 8, ps, Hkv, D)
+    pool.fill_normal(seed=2)
+    bt = torch.tensor([[0, 1, 99, 3]], dtype=torch.int32, device="cuda")  # 99 >= num_pages
+    q = torch.ones((1, H, D), dtype=torch.float16, device="cuda")
+    out = torch.zeros_like(q)
+    pool.decode(pool.plan([60], H), 0, q, out, bt, 0.1)
+    torch.cuda.synchronize()
+    code, info = ffi.device_error(0, clear=True)
+    assert code == 1 and info == 99  # KVC_DEVERR_BAD_PAGE
+    bt[0, 2] = 2
+    pool.decode(pool.plan([60], H), 0, q, out, bt, 0.1)
+    torch.cuda.synchronize()
+    assert ffi.device_error(0, clear=True) == (0, 0)
+    assert torch.isfinite(out).all()
