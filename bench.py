@@ -87,60 +87,100 @@ def load_peaks():
 # clocks sampling (nvidia-smi during the timed region)
 # ---------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of one GPU, sampled every 20 ms by a
+    thread while the timed region runs (read-only NVML queries; nvidia-smi
+    polling when NVML is unavailable)."""
 
-    def __init__(self, gpu_index: int):
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, gpu_index: int, interval_s: float = 0.02):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.interval = interval_s
+        self.samples = []   # (sm_mhz, reasons bitmask)
+        self.sm_max = 0.0
+        self._stop = threading.Event()
         self.thread = None
+        self.proc = None
 
     def start(self):
         try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = self._nvml_handle(pynvml)
+            self.sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((float(mhz), int(rs)))
+                    except Exception:
+                        pass
+                    self._stop.wait(self.interval)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+        except Exception:
+            self._start_smi()
+
+    def _nvml_handle(self, pynvml):
+        """NVML handle of the CUDA device (matched by PCI address, since NVML
+        numbers every GPU of the machine, not only the visible ones)."""
+        try:
+            import torch
+
+            p = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _start_smi(self):
+        fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
+                ["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        bits = [0x8, 0x40, 0x20, 0x4]
+
+        def read():
+            for line in self.proc.stdout:
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    mask = sum(b for b, v in zip(bits, parts[2:6]) if v.lower() == "active")
+                    self.samples.append((float(parts[0]), mask))
+                    self.sm_max = max(self.sm_max, float(parts[1]))
+                except (ValueError, IndexError):
+                    continue
+
+        self.thread = threading.Thread(target=read, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = max(smax, float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = sorted(n for n, b in self.REASONS.items()
+                         if any(m & b for _, m in self.samples))
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples),
+                "sm_max_mhz": self.sm_max, "reasons": reasons, "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------------------------
@@ -210,12 +250,14 @@ def run_b200(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg["layers"] = args.layers  # profiling subset only (the bench line names it)
     L, H, Hkv, D, B = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["batch"]
     cached = cached_lengths(cfg)
     ctx = cached + 1                                  # context includes the appended token
-    table, total_pages = paged.random_block_tables(ctx, PAGE, cfg["seed"] + 17 * rank)
-    pool = paged.PagedKVCache(L, total_pages, PAGE, Hkv, D, dtype=torch.float16,
+    table, total_pages = paged.random_block_tables(ctx, args.page_size, cfg["seed"] + 17 * rank)
+    pool = paged.PagedKVCache(L, total_pages, args.page_size, Hkv, D, dtype=torch.float16,
                               device=local_rank)
     pool.fill_normal(seed=1000 + rank, stddev=1.0)
     bt = torch.from_numpy(table).to(dev)
@@ -233,15 +275,13 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     def step(events=None):
+        # one fused launch per layer: append each sequence's new row + attend
         for l in range(L):
             if events is not None:
                 events[l][0].record(stream)
-            pool.append(l, kn[l], vn[l], bt, pos, rows, stream=stream)
+            pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=stream)
             if events is not None:
                 events[l][1].record(stream)
-            pool.decode(plan, l, q[l], out[l], bt, scale, stream=stream)
-            if events is not None:
-                events[l][2].record(stream)
 
     for _ in range(args.warmup):
         step()
@@ -251,7 +291,7 @@ def run_b200(args, rank, world, local_rank):
         raise RuntimeError(f"device error {code} ({info}) during warm-up")
 
     # per-launch events for every layer of every timed step
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)]
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
            for _ in range(args.steps)]
     sampler = ClockSampler(local_rank) if not args.no_clocks else None
     if world > 1:
@@ -259,7 +299,6 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if sampler:
         sampler.start()
-        time.sleep(0.3)
     t_start = torch.cuda.Event(enable_timing=True)
     t_stop = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
@@ -271,8 +310,7 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.barrier()
     elapsed_ms = t_start.elapsed_time(t_stop)
-    dec_ms = [evs[s][l][1].elapsed_time(evs[s][l][2]) for s in range(args.steps) for l in range(L)]
-    app_ms = [evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(args.steps) for l in range(L)]
+    dec_ms = [evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(args.steps) for l in range(L)]
     code, info = ffi.device_error(local_rank)
     if code:
         raise RuntimeError(f"device error {code} ({info}) during timing")
@@ -334,7 +372,7 @@ def run_b200(args, rank, world, local_rank):
 
     peak, peak_kind = load_peaks()
     dec_avg_ms = float(np.mean(dec_ms))
-    dec_bytes = (kv_read + qo) / L                      # per launch (one layer)
+    dec_bytes = (kv_read + appended + qo) / L           # per launch (one layer)
     achieved = dec_bytes / (dec_avg_ms / 1e3) / 1e9
     res = {
         "metric": METRIC,
@@ -352,26 +390,26 @@ def run_b200(args, rank, world, local_rank):
         "dtype": "f16 storage, f32 accumulate",
         "data": "synthetic: seeded N(0,1) K/V/q, random page permutation",
         "config": {
-            "workload": f"{cfg['workload']} (BASELINE config {args.config})",
+            "workload": f"{cfg['workload']} (BASELINE config {args.config})"
+                        + (f" [profiling subset: {L} layers]" if args.layers else ""),
             "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D,
             "sequences_per_gpu": B, "global_batch": B * world,
             "cached_len": (f"U[{cfg['lens'][1]},{cfg['lens'][2]}] seed {cfg['seed']}"
                            if cfg["lens"][0] == "uniform" else int(cfg["lens"][1])),
-            "ctx_tokens_per_gpu": int(ctx.sum()), "page_size": PAGE,
-            "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * PAGE * D * 2 / 1e9, 2),
+            "ctx_tokens_per_gpu": int(ctx.sum()), "page_size": args.page_size,
+            "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * args.page_size * D * 2 / 1e9, 2),
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
             "parallelism": f"sequence-sharded x{world} (independent batches, no collective)",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "decode_mma_kernel",
+            "bound": "hbm", "kernel": "decode_mma_kernel (append fused)",
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
             "unit": "GB/s", "frac": round(achieved / peak, 4),
             "bytes_per_launch": int(dec_bytes), "avg_launch_us": round(dec_avg_ms * 1e3, 2),
             "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
-            "append_avg_us": round(float(np.mean(app_ms)) * 1e3, 2),
         },
-        "gpu_launches": 2 * L * args.steps,
+        "gpu_launches": L * args.steps,
         "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
     }
     if e2e:
@@ -441,11 +479,14 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: run this many layers instead of the config's")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

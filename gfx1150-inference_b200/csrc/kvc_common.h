@@ -53,10 +53,15 @@ struct kvc_plan {
   int n_queries = 0, n_items = 0, n_slots = 0;
   int num_heads = 0, num_kv_heads = 0, group = 0, n_hchunk = 0;
   int head_dim = 0, page_size = 0, max_ctx = 0;
+  bool rows_distinct = true;   // every query has its own block-table row
   kvc::PoolGeom pool_geom;
-  std::vector<int4> items, qinfo;
-  std::vector<int32_t> rows, positions;
-  kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters;
+  std::vector<int4> items, qinfo, item_pairs;
+  std::vector<int32_t> rows, positions, sched_off;
+  std::vector<int4> sched_recs;   // 3 per scheduled unit
+  std::vector<int32_t> merge_queries;
+  int n_sched_ctas = 0;
+  kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters, d_sched_off,
+      d_sched_units, d_merge;
   kvc::HostBuf h_stage;
   cudaEvent_t upload_done = nullptr;
 
@@ -68,6 +73,9 @@ struct kvc_plan {
     d_part_o.release();
     d_part_ml.release();
     d_counters.release();
+    d_sched_off.release();
+    d_sched_units.release();
+    d_merge.release();
     h_stage.release();
     if (upload_done) cudaEventDestroy(upload_done);
     upload_done = nullptr;
@@ -83,6 +91,12 @@ int do_append(kvc_pool* pool, int layer, const void* d_k_new, const void* d_v_ne
               int pos0, int n, cudaStream_t s);
 int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, void* d_out,
               const int32_t* d_bt, int bt_stride, float scale, cudaStream_t s);
+int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
+                    void* d_out, const int32_t* d_bt, int bt_stride, float scale,
+                    const void* d_k_new, const void* d_v_new, cudaStream_t s);
+int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
+                       const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
+                       int bt_stride, float scale, cudaStream_t s);
 // Plan for q_len queries m = 0..q_len-1 of one sequence (block-table row 0)
 // whose context is min(kv_len, start_pos + m + 1) if causal, else kv_len
 // (attention.hip:75).

@@ -8,14 +8,16 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
 #include <mutex>
+#include <queue>
 #include <string>
 #include <vector>
 
-#include "../../include/kvcache.h"
+#include "kvcache.h"
 #include "kvc_common.h"
 #include "kvc_internal.h"
 
@@ -353,8 +355,20 @@ extern "C" int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_ta
 // ============================================================================
 namespace kvc {
 
+// Positions per split: kSplitTokens rounded up to whole pages.  KVC_SPLIT_TOKENS
+// overrides it for tuning (changes the summation order, so results may differ
+// in the last bits between settings; every mode of one setting still agrees).
 int split_tokens_for(int page_size) {
-  return ((kSplitTokens + page_size - 1) / page_size) * page_size;
+  static int base = [] {
+    const char* e = getenv("KVC_SPLIT_TOKENS");
+    int v = e ? atoi(e) : kSplitTokens;
+    if (v < kSlab) v = kSlab;
+    return v;
+  }();
+  int c = ((base + page_size - 1) / page_size) * page_size;
+  while (c / page_size > kMaxSplitPages) c -= page_size;
+  if (c > kMaxSplitPages * kSlab) c = (kMaxSplitPages * kSlab / page_size) * page_size;
+  return c < page_size ? page_size : c;
 }
 
 // Build the split list on the host.  ctx_of(i) / row_of(i) describe query i.
@@ -389,6 +403,58 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   std::stable_sort(p->items.begin(), p->items.end(), [](const int4& x, const int4& y) {
     return (x.w - x.z) > (y.w - y.z);
   });
+  // Each kernel work item is {split record, its query's record}: one 32-byte load.
+  p->item_pairs.resize(2 * p->items.size());
+  for (size_t k = 0; k < p->items.size(); ++k) {
+    p->item_pairs[2 * k] = p->items[k];
+    p->item_pairs[2 * k + 1] = p->qinfo[p->items[k].x];
+  }
+  // Persistent schedule: units (item x KV head x q-head chunk) onto warps of
+  // kPersistWarps-warp CTAs (one per SM), longest first onto the least-loaded
+  // warp, so every warp streams about the same number of positions.  Cost of
+  // a unit = its positions + a fixed per-unit overhead.  Each unit is stored as
+  // a self-contained 3 x int4 record in its warp's list.
+  {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    const int group = num_heads / g.num_kv_heads;
+    const int nhc = (group + 7) / 8;
+    const int per_item = g.num_kv_heads * nhc;
+    const int n_units = static_cast<int>(p->items.size()) * per_item;
+    const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
+    const int n_bins = n_ctas * kPersistWarps;
+    std::vector<std::vector<int>> lists(n_bins);
+    using Load = std::pair<int64_t, int>;
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int b = 0; b < n_bins; ++b) heap.push({0, b});
+    for (int k = 0; k < static_cast<int>(p->items.size()); ++k) {
+      const int64_t cost = (p->items[k].w - p->items[k].z) + 64;
+      for (int r = 0; r < per_item; ++r) {
+        Load top = heap.top();
+        heap.pop();
+        lists[top.second].push_back(k * per_item + r);
+        heap.push({top.first + cost, top.second});
+      }
+    }
+    p->sched_off.assign(1, 0);
+    p->sched_recs.clear();
+    for (auto& l : lists) {
+      for (int u : l) {
+        const int k = u / per_item;
+        const int kvh = (u / nhc) % g.num_kv_heads;
+        const int hc = u % nhc;
+        const int4 it = p->items[k];
+        p->sched_recs.push_back(it);
+        p->sched_recs.push_back(p->qinfo[it.x]);
+        p->sched_recs.push_back(make_int4(kvh, hc, kvh * group + hc * 8, std::min(8, group - hc * 8)));
+      }
+      p->sched_off.push_back(static_cast<int32_t>(p->sched_recs.size() / 3));
+    }
+    p->n_sched_ctas = n_units > 0 ? n_ctas : 0;
+    p->merge_queries.clear();
+    for (int i = 0; i < n_queries; ++i)
+      if (p->qinfo[i].w > 1) p->merge_queries.push_back(i);
+  }
   p->n_queries = n_queries;
   p->n_items = static_cast<int>(p->items.size());
   p->n_slots = slot;
@@ -400,10 +466,15 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->page_size = g.page_size;
   p->max_ctx = max_ctx;
   p->device = device;
+  {
+    std::vector<int32_t> r(p->rows);
+    std::sort(r.begin(), r.end());
+    p->rows_distinct = std::adjacent_find(r.begin(), r.end()) == r.end();
+  }
 
   cudaError_t e;
   // device buffers (grow-only)
-  const size_t items_b = sizeof(int4) * std::max<size_t>(1, p->items.size());
+  const size_t items_b = sizeof(int4) * std::max<size_t>(1, p->item_pairs.size());
   const size_t qinfo_b = sizeof(int4) * std::max(1, n_queries);
   const size_t rows_b = sizeof(int32_t) * std::max(1, n_queries);
   const size_t po_b = sizeof(float) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads * g.head_dim);
@@ -419,7 +490,13 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
       return cuda_error(e, "cudaMemsetAsync(counters)");
   }
   // upload through pinned staging; wait for the previous upload to leave it
-  const size_t stage_b = items_b + qinfo_b + 2 * rows_b;
+  const size_t soff_b = (sizeof(int32_t) * p->sched_off.size() + 15) / 16 * 16;
+  const size_t sun_b = sizeof(int4) * std::max<size_t>(1, p->sched_recs.size());
+  if ((e = p->d_sched_off.ensure(soff_b)) || (e = p->d_sched_units.ensure(sun_b)))
+    return cuda_error(e, "plan schedule buffers");
+  const size_t mq_b = sizeof(int32_t) * std::max<size_t>(1, p->merge_queries.size());
+  if ((e = p->d_merge.ensure(mq_b))) return cuda_error(e, "plan merge list");
+  const size_t stage_b = items_b + qinfo_b + 2 * rows_b + soff_b + sun_b + mq_b;
   if (p->upload_done) {
     if ((e = cudaEventSynchronize(p->upload_done))) return cuda_error(e, "plan upload wait");
   } else if ((e = cudaEventCreateWithFlags(&p->upload_done, cudaEventDisableTiming))) {
@@ -427,14 +504,24 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   }
   if ((e = p->h_stage.ensure(stage_b))) return cuda_error(e, "cudaMallocHost(plan)");
   uint8_t* h = static_cast<uint8_t*>(p->h_stage.ptr);
-  memcpy(h, p->items.data(), sizeof(int4) * p->items.size());
+  memcpy(h, p->item_pairs.data(), sizeof(int4) * p->item_pairs.size());
   memcpy(h + items_b, p->qinfo.data(), sizeof(int4) * n_queries);
   memcpy(h + items_b + qinfo_b, p->rows.data(), sizeof(int32_t) * n_queries);
   memcpy(h + items_b + qinfo_b + rows_b, p->positions.data(), sizeof(int32_t) * n_queries);
-  if ((e = cudaMemcpyAsync(p->d_items.ptr, h, sizeof(int4) * p->items.size(), cudaMemcpyHostToDevice, s)) ||
+  uint8_t* hs = h + items_b + qinfo_b + 2 * rows_b;
+  memcpy(hs, p->sched_off.data(), sizeof(int32_t) * p->sched_off.size());
+  if (!p->sched_recs.empty()) memcpy(hs + soff_b, p->sched_recs.data(), sizeof(int4) * p->sched_recs.size());
+  uint8_t* hm = hs + soff_b + sun_b;
+  if (!p->merge_queries.empty()) memcpy(hm, p->merge_queries.data(), sizeof(int32_t) * p->merge_queries.size());
+  if ((e = cudaMemcpyAsync(p->d_items.ptr, h, sizeof(int4) * p->item_pairs.size(), cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(p->d_qinfo.ptr, h + items_b, sizeof(int4) * n_queries, cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(p->d_rows.ptr, h + items_b + qinfo_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(p->d_pos.ptr, h + items_b + qinfo_b + rows_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)))
+      (e = cudaMemcpyAsync(p->d_pos.ptr, h + items_b + qinfo_b + rows_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(p->d_sched_off.ptr, hs, soff_b, cudaMemcpyHostToDevice, s)) ||
+      (!p->sched_recs.empty() &&
+       (e = cudaMemcpyAsync(p->d_sched_units.ptr, hs + soff_b, sizeof(int4) * p->sched_recs.size(), cudaMemcpyHostToDevice, s))) ||
+      (!p->merge_queries.empty() &&
+       (e = cudaMemcpyAsync(p->d_merge.ptr, hm, sizeof(int32_t) * p->merge_queries.size(), cudaMemcpyHostToDevice, s))))
     return cuda_error(e, "plan upload");
   if ((e = cudaEventRecord(p->upload_done, s))) return cuda_error(e, "cudaEventRecord(plan)");
   p->pool_geom = g;
@@ -444,6 +531,13 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
 
 int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, void* d_out,
               const int32_t* d_bt, int bt_stride, float scale, cudaStream_t s) {
+  return do_decode_fused(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, nullptr, nullptr,
+                         s);
+}
+
+int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
+                    void* d_out, const int32_t* d_bt, int bt_stride, float scale,
+                    const void* d_k_new, const void* d_v_new, cudaStream_t s) {
   const PoolGeom& g = pool->g;
   if (!plan || !plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
   if (layer < 0 || layer >= g.num_layers)
@@ -470,6 +564,13 @@ int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, 
   a.part_o = static_cast<float*>(plan->d_part_o.ptr);
   a.part_ml = static_cast<float2*>(plan->d_part_ml.ptr);
   a.counters = static_cast<unsigned*>(plan->d_counters.ptr);
+  a.sched_off = static_cast<const int32_t*>(plan->d_sched_off.ptr);
+  a.sched_recs = static_cast<const int4*>(plan->d_sched_units.ptr);
+  a.n_sched_ctas = plan->n_sched_ctas;
+  a.merge_queries = static_cast<const int32_t*>(plan->d_merge.ptr);
+  a.n_merge_queries = static_cast<int>(plan->merge_queries.size());
+  a.k_new = static_cast<const uint8_t*>(d_k_new);
+  a.v_new = static_cast<const uint8_t*>(d_v_new);
   a.n_items = plan->n_items;
   a.num_heads = plan->num_heads;
   a.num_kv_heads = g.num_kv_heads;
@@ -490,6 +591,29 @@ int plan_queries(kvc_plan* plan, const PoolGeom& g, int q_len, int num_heads, in
       plan, g, q_len, num_heads,
       [&](int m) { return causal ? std::max(0, std::min(kv_len, start_pos + m + 1)) : kv_len; },
       [](int) { return 0; }, device, s);
+}
+
+// Decode step with one new row per query at position ctx - 1: fused into the
+// attention kernel when every query has its own block-table row (a decode
+// batch), else a separate append launch first (several queries of one
+// sequence read each other's new rows).
+int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
+                       const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
+                       int bt_stride, float scale, cudaStream_t s) {
+  if (!d_k_new || !d_v_new) return set_error(KVC_ERR_INVALID_ARG, "K/V rows must not be null.");
+  if ((reinterpret_cast<uintptr_t>(d_k_new) | reinterpret_cast<uintptr_t>(d_v_new)) & 15u)
+    return set_error(KVC_ERR_INVALID_ARG, "K/V row buffers must be 16-byte aligned.");
+  if (plan->rows_distinct) {
+    for (int32_t c : plan->positions)
+      if (c < 0) return set_error(KVC_ERR_INVALID_ARG, "a query with an empty context has no new row.");
+    return do_decode_fused(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, d_k_new, d_v_new,
+                           s);
+  }
+  int rc = do_append(pool, layer, d_k_new, d_v_new, d_bt, bt_stride,
+                     static_cast<const int32_t*>(plan->d_rows.ptr),
+                     static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
+  if (rc) return rc;
+  return do_decode(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, s);
 }
 
 }  // namespace kvc
@@ -548,11 +672,8 @@ extern "C" int kvc_append_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int l
   if (!plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
   cudaSetDevice(pool->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = do_append(pool, layer, d_k_new, d_v_new, d_block_tables, bt_stride,
-                     static_cast<const int32_t*>(plan->d_rows.ptr),
-                     static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
-  if (rc) return rc;
-  return do_decode(pool, plan, layer, d_q, d_out, d_block_tables, bt_stride, scale, s);
+  return append_then_decode(pool, plan, layer, d_q, d_k_new, d_v_new, d_out, d_block_tables,
+                            bt_stride, scale, s);
 }
 
 extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
@@ -582,11 +703,8 @@ extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int lay
       (e = cudaMemcpyAsync(d_k, h_k_new, kb, cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(d_v, h_v_new, kb, cudaMemcpyHostToDevice, s)))
     return cuda_error(e, "cudaMemcpyAsync(H2D)");
-  int rc = do_append(pool, layer, d_k, d_v, d_block_tables, bt_stride,
-                     static_cast<const int32_t*>(plan->d_rows.ptr),
-                     static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
-  if (rc) return rc;
-  rc = do_decode(pool, plan, layer, d_q, d_out, d_block_tables, bt_stride, scale, s);
+  int rc = append_then_decode(pool, plan, layer, d_q, d_k, d_v, d_out, d_block_tables, bt_stride,
+                              scale, s);
   if (rc) return rc;
   if ((e = cudaMemcpyAsync(h_out, d_out, qb, cudaMemcpyDeviceToHost, s)))
     return cuda_error(e, "cudaMemcpyAsync(D2H)");
@@ -705,10 +823,13 @@ int cached_attend(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_le
                   int q_len, int start_pos, int num_heads, float scale, bool causal,
                   cudaStream_t s) {
   const int kv_len = start_pos + q_len;
-  int rc = do_append(pool, layer_idx, d_Kn, d_Vn, d_bt, bt_len, nullptr, nullptr, start_pos,
-                     q_len, s);
+  int rc = plan_queries(plan, pool->g, q_len, num_heads, start_pos, kv_len, causal, pool->device,
+                        s);
   if (rc) return rc;
-  rc = plan_queries(plan, pool->g, q_len, num_heads, start_pos, kv_len, causal, pool->device, s);
+  if (q_len == 1)  // a decode step: the row append runs inside the attention kernel
+    return append_then_decode(pool, plan, layer_idx, d_Q, d_Kn, d_Vn, d_Out, d_bt, bt_len, scale,
+                              s);
+  rc = do_append(pool, layer_idx, d_Kn, d_Vn, d_bt, bt_len, nullptr, nullptr, start_pos, q_len, s);
   if (rc) return rc;
   return do_decode(pool, plan, layer_idx, d_Q, d_Out, d_bt, bt_len, scale, s);
 }

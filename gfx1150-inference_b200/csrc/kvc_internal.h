@@ -45,6 +45,11 @@ __host__ __device__ __forceinline__ size_t unit_offset(int layout, int t, int u,
 // only on the context length, never on the storage mode, batch composition or
 // GPU count, so resident, offloaded and sharded runs add in the same order.
 constexpr int kSplitTokens = 512;
+// Upper bound on pages per split the kernels accept (split tokens are capped at
+// kMaxSplitPages * 16).
+constexpr int kMaxSplitPages = 64;
+// Warps per CTA of the persistent decode kernel (one CTA per SM).
+constexpr int kPersistWarps = 8;
 
 struct PoolGeom {
   int num_layers = 0;
@@ -105,11 +110,27 @@ struct DecodeArgs {
   void* out;                     // (n_queries, H, D)
   const int32_t* block_tables;
   int bt_stride;
-  const int4* items;
+  const int4* items;             // 2 per item: {query, split, tb, te}, {row, ctx, slot0, splits}
   const int4* qinfo;
   float* part_o;                 // (split slots, H, D) fp32 partial outputs
   float2* part_ml;               // (split slots, H) running max (log2 units) and sum
   unsigned int* counters;        // (n_queries, Hkv, n_hchunk), zero between launches
+  // Fused append (decode steps): when non-null, query i's new K/V row, (n_queries,
+  // Hkv, D), is written at position ctx_i - 1 of its block-table row by the CTA
+  // that owns that position, which also uses it in place of the slab's stale row.
+  // Only valid when every query has its own block-table row.
+  const uint8_t* k_new;
+  const uint8_t* v_new;
+  // Persistent schedule: warp w (= CTA * kPersistWarps + warp) processes unit
+  // records sched_recs[3 * (sched_off[w] .. sched_off[w+1]))], each 3 x int4:
+  // {query, split, first pos, end pos}, {bt row, ctx, split slot0, n_splits},
+  // {KV head, q-head chunk, first q-head, q-heads in chunk}.
+  const int32_t* sched_off;
+  const int4* sched_recs;
+  int n_sched_ctas;
+  // queries with more than one split (merged by merge_splits_kernel)
+  const int32_t* merge_queries;
+  int n_merge_queries;
   int n_items;
   int num_heads;
   int num_kv_heads;

@@ -17,6 +17,8 @@
 // memory with bulk copies, and serves all q-heads of the group from the same
 // tile; splits are merged by the last CTA of a query to finish.
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "kvc_device.cuh"
 #include "kvc_internal.h"
@@ -178,7 +180,7 @@ cudaError_t launch_fill_normal(const FillArgs& a, cudaStream_t s) {
 // =====================================================================================
 constexpr int kMergeChunk = 128;
 // Bytes reserved at the start of dynamic shared memory for the mbarriers.
-constexpr int kBarBytes = 128;
+constexpr int kBarBytes = 256;
 
 __device__ __forceinline__ size_t merge_smem_bytes(int head_dim) {
   return (8 * kMergeChunk + 8 * static_cast<size_t>(head_dim) + 16) * sizeof(float);
@@ -241,6 +243,44 @@ __device__ void merge_splits(const DecodeArgs& a, float* sm, int query, int spli
   for (int i = threadIdx.x; i < nh * D; i += blockDim.x) out[i] = from_f32<T>(acc[i] * st[8 + i / D]);
 }
 
+// Fused append, global half: lanes of one warp copy query `query`'s new K and V
+// row of head `kvh` into the pool at position pos (16-byte units).
+__device__ __forceinline__ void append_row_to_pool(const DecodeArgs& a, int layout, int es,
+                                                   int query, int kvh, int pos,
+                                                   const int32_t* bt_row, int lane) {
+  const int U = a.head_dim * es / 16;
+  const int slot = pos / a.page_size;
+  const int phys = bt_row[slot];
+  if (phys < 0 || phys >= a.num_pages) return;  // reported by the slab loader
+  const int t = pos - slot * a.page_size;
+  const size_t page_head = static_cast<size_t>(a.page_size) * a.head_dim * es;
+  const size_t dst = (static_cast<size_t>(phys) * a.num_kv_heads + kvh) * page_head;
+  const size_t src = (static_cast<size_t>(query) * a.num_kv_heads + kvh) * U * 16;
+  uint8_t* kl = const_cast<uint8_t*>(a.k_layer);
+  uint8_t* vl = const_cast<uint8_t*>(a.v_layer);
+  for (int x = lane; x < 2 * U; x += 32) {
+    const int u = x % U;
+    const uint8_t* sp = (x < U ? a.k_new : a.v_new) + src + static_cast<size_t>(u) * 16;
+    uint8_t* dp = (x < U ? kl : vl) + dst + unit_offset(layout, t, u, U) * 16;
+    *reinterpret_cast<uint4*>(dp) = *reinterpret_cast<const uint4*>(sp);
+  }
+}
+
+// Fused append, shared half: overwrite row t of a staged K/V slab pair with the
+// new row (the bulk copy may have fetched the pool's previous contents).
+__device__ __forceinline__ void patch_slab_row(const DecodeArgs& a, int layout, int es, uint8_t* st,
+                                               int slab_bytes, int query, int kvh, int t, int tid,
+                                               int nthreads) {
+  const int U = a.head_dim * es / 16;
+  const size_t src = (static_cast<size_t>(query) * a.num_kv_heads + kvh) * U * 16;
+  for (int x = tid; x < 2 * U; x += nthreads) {
+    const int u = x % U;
+    const uint8_t* sp = (x < U ? a.k_new : a.v_new) + src + static_cast<size_t>(u) * 16;
+    *reinterpret_cast<uint4*>(st + (x < U ? 0 : slab_bytes) + unit_offset(layout, t, u, U) * 16) =
+        *reinterpret_cast<const uint4*>(sp);
+  }
+}
+
 // Publish this CTA's partial and let the last CTA of (query, KV head, head chunk)
 // merge.  Classic threadfence reduction: no CTA ever waits for another.
 template <typename T>
@@ -292,8 +332,9 @@ __global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a)
   b /= a.n_hchunk;
   const int kvh = b % a.num_kv_heads;
   b /= a.num_kv_heads;
-  const int4 it = a.items[b];
-  const int4 qi = a.qinfo[it.x];
+  // Item record: {query, split, first pos, end pos}, {bt row, ctx, split slot, splits}.
+  const int4 it = a.items[2 * b];
+  const int4 qi = a.items[2 * b + 1];
   const int query = it.x, split = it.y, tb = it.z, te = it.w;
   const int hq0 = kvh * a.group + hc * 8;
   const int nh = min(8, a.group - hc * 8);
@@ -338,18 +379,33 @@ __global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a)
   const size_t page_stride = static_cast<size_t>(a.num_kv_heads) * ps * D * 2;
   const uint64_t policy = l2_policy_evict_first();
 
-  // Physical page of slab j, or -1 if the block table entry is out of range.
-  auto slab_page = [&](int j) -> int {
-    const int phys = bt_row[j / slabs_per_page];
-    return (phys >= 0 && phys < a.num_pages) ? phys : -1;
+  // The split's page ids, two per lane, read once (a split spans at most
+  // kMaxSplitPages pages).  Out-of-range entries become -1 and are reported;
+  // their slabs are skipped.
+  const int pg0 = tb / ps;
+  const int npages = (te + ps - 1) / ps - pg0;
+  int my_page0 = -1, my_page1 = -1;
+  if (lane < npages) {
+    const int v = bt_row[pg0 + lane];
+    my_page0 = (v >= 0 && v < a.num_pages) ? v : -1;
+    if (my_page0 < 0) report_error(1u, static_cast<uint32_t>(v));
+  }
+  if (lane + 32 < npages) {
+    const int v = bt_row[pg0 + lane + 32];
+    my_page1 = (v >= 0 && v < a.num_pages) ? v : -1;
+    if (my_page1 < 0) report_error(1u, static_cast<uint32_t>(v));
+  }
+  auto slab_page = [&](int j) -> int {  // all lanes (j is warp-uniform)
+    const int idx = j / slabs_per_page - pg0;
+    const int v0 = __shfl_sync(0xffffffffu, my_page0, idx & 31);
+    const int v1 = __shfl_sync(0xffffffffu, my_page1, idx & 31);
+    return idx < 32 ? v0 : v1;
   };
-  auto issue = [&](int i) {  // lane 0 only
+  auto issue = [&](int i, int phys) {  // lane 0 only
     const int j = sb0 + warp + i * NW;
     const int s = i % NS;
     const uint32_t bar = smem_u32(&bars[s]);
-    const int phys = slab_page(j);
     if (phys < 0) {
-      report_error(1u, static_cast<uint32_t>(bt_row[j / slabs_per_page]));
       mbar_arrive(bar);
       return;
     }
@@ -361,13 +417,20 @@ __global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a)
     bulk_g2s(dst + SLAB_BYTES, a.v_layer + off, SLAB_BYTES, bar, policy);
   };
 
-  int issued = 0;
-  if (lane == 0) {
-    const int first = min(NS, nslabs);
-    for (int i = 0; i < first; ++i) issue(i);
+  const int first = min(NS, nslabs);
+  for (int i = 0; i < first; ++i) {
+    const int phys = slab_page(sb0 + warp + i * NW);
+    if (lane == 0) issue(i, phys);
   }
-  issued = min(NS, nslabs);
+  int issued = first;
   __syncwarp();
+
+  // Fused append: this split holds the query's last position.
+  const int ctx = qi.y;
+  const bool owns_new = a.k_new != nullptr && ctx > 0 && te == ctx;
+  const int new_slab = (ctx - 1) / kSlab;
+  if (owns_new && hc == 0 && warp == 0)
+    append_row_to_pool(a, kLayoutCore, 2, query, kvh, ctx - 1, bt_row, lane);
 
   float m_run = kNegBig, l_run = 0.f;
   float o[MT][4];
@@ -400,27 +463,54 @@ __global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a)
         }
         __syncwarp();
       }
+      if (owns_new && j == new_slab) {
+        patch_slab_row(a, kLayoutCore, 2, st, SLAB_BYTES, query, kvh, (ctx - 1) - j * kSlab, lane,
+                       32);
+        __syncwarp();
+      }
       const uint32_t kbase = smem_u32(st);
       const uint32_t vbase = kbase + SLAB_BYTES;
 
-      float sc[2][4];
+      // S = Q . K^T for the slab's two 8-position tiles.  Four independent
+      // accumulator chains (tile x even/odd k-chunk) instead of two serial
+      // ones, so consecutive mma.sync do not wait on each other.
+      float sc[2][2][4];
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int k2 = 0; k2 < D / 32; ++k2) {
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, r0, r1, r2, r3);
-          Mma<T>::run(sc[nt], qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, r0, r1);
-          Mma<T>::run(sc[nt], qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, r2, r3);
+        for (int par = 0; par < 2; ++par)
+          sc[nt][par][0] = sc[nt][par][1] = sc[nt][par][2] = sc[nt][par][3] = 0.f;
+#pragma unroll
+      for (int k2 = 0; k2 < D / 32; ++k2) {
+        uint32_t r[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, r[nt][0],
+                  r[nt][1], r[nt][2], r[nt][3]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          Mma<T>::run(sc[nt][0], qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, r[nt][0], r[nt][1]);
+          Mma<T>::run(sc[nt][1], qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, r[nt][2], r[nt][3]);
         }
       }
+      // V^T fragments of the first m-tiles, loaded before the softmax so their
+      // shared-memory latency overlaps the shuffles and exponentials.
+      constexpr int VPRE = MT < 8 ? MT : 8;
+      const int jm = lane >> 3;
+      uint32_t vf[VPRE][4];
+#pragma unroll
+      for (int mt = 0; mt < VPRE; ++mt)
+        ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, vf[mt][0],
+                  vf[mt][1], vf[mt][2], vf[mt][3]);
+
       // Lane (gid, tig) holds scores of q-head gid for positions 2tig, 2tig+1,
       // 8+2tig, 9+2tig of the slab.
       const int t0 = 2 * tig;
       const bool v0 = t0 < valid, v1 = t0 + 1 < valid, v2 = t0 + 8 < valid, v3 = t0 + 9 < valid;
-      const float x0 = sc[0][0] * a.scale_log2, x1 = sc[0][1] * a.scale_log2;
-      const float x2 = sc[1][0] * a.scale_log2, x3 = sc[1][1] * a.scale_log2;
+      const float x0 = (sc[0][0][0] + sc[0][1][0]) * a.scale_log2;
+      const float x1 = (sc[0][0][1] + sc[0][1][1]) * a.scale_log2;
+      const float x2 = (sc[1][0][0] + sc[1][1][0]) * a.scale_log2;
+      const float x3 = (sc[1][0][1] + sc[1][1][1]) * a.scale_log2;
       float mx = fmaxf(fmaxf(v0 ? x0 : kNegBig, v1 ? x1 : kNegBig),
                        fmaxf(v2 ? x2 : kNegBig, v3 ? x3 : kNegBig));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -439,23 +529,28 @@ __global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a)
       // lives in lanes (2tig)*4 and (2tig+1)*4.
       const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * tig) * 4);
       const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * tig + 1) * 4);
-      const int jm = lane >> 3;
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         o[mt][0] *= a_lo;
         o[mt][1] *= a_hi;
         o[mt][2] *= a_lo;
         o[mt][3] *= a_hi;
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, r0, r1, r2, r3);
-        Mma<T>::run(o[mt], r0, r1, r2, r3, pb0, pb1);
+        if (mt < VPRE) {
+          Mma<T>::run(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], pb0, pb1);
+        } else {
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, r0, r1,
+                    r2, r3);
+          Mma<T>::run(o[mt], r0, r1, r2, r3, pb0, pb1);
+        }
       }
     }
     __syncwarp();
     if (i + NS < nslabs) {
+      const int phys = slab_page(sb0 + warp + (i + NS) * NW);
       if (lane == 0) {
         fence_proxy_async();
-        issue(i + NS);
+        issue(i + NS, phys);
       }
       issued = i + NS + 1;
     }
@@ -517,6 +612,479 @@ __global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a)
 }
 
 // =====================================================================================
+// Persistent tensor-core decode kernel (16-bit storage, head_dim multiple of 32).
+//
+// One CTA of NW warps per SM; every warp is an independent streaming engine.
+// The host assigns whole split units (one split of one query for one KV head
+// and <= 8 of its q-heads) to warps, longest first onto the least-loaded warp,
+// so all warps stream about the same number of positions.  A warp walks its
+// list in order: its producer side keeps NS slabs (16 positions of K and V,
+// one bulk copy each) in flight in the warp's shared-memory ring, running into
+// the next unit before the current one is finished, and prefetches the next
+// unit's page ids one unit ahead; its consumer side does the math of a slab
+// as soon as it lands (S = Q K^T, online softmax, O^T += V^T P^T, mma.sync
+// m16n8k16) and, at the end of a unit, writes the output or the split's
+// partial state (the last split of a query to finish merges all of them).
+// There is no CTA-wide synchronisation after start-up.
+// =====================================================================================
+constexpr int kPersistBarBytes = 1024;   // NW * NS mbarriers
+constexpr int kPersistMetaBytes = 8192;  // NW * NS stage records (4 x int4 each)
+
+template <int D>
+constexpr int persist_stages() {
+  // ~192 KiB of ring per CTA, at most 12 stages per warp
+  return (196608 / (kPersistWarps * 2 * kSlab * D * 2)) > 12
+             ? 12
+             : (196608 / (kPersistWarps * 2 * kSlab * D * 2));
+}
+
+template <typename T, int D, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int SLAB_BYTES = kSlab * D * 2;
+  constexpr int STAGE_BYTES = 2 * SLAB_BYTES;
+  constexpr int KC = D / 16;
+  constexpr int MT = D / 16;
+  constexpr int U = D / 8;
+  static_assert(NW * NS * 8 <= kPersistBarBytes, "mbarrier block too small");
+  static_assert(NW * NS * 64 <= kPersistMetaBytes, "stage record block too small");
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int ps = a.page_size;
+  const int spp = ps / kSlab;  // slabs per page
+  const int H = a.num_heads;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * NS;
+  int4* meta = reinterpret_cast<int4*>(smem + kPersistBarBytes) + warp * NS * 4;
+  uint8_t* stages = smem + kPersistBarBytes + kPersistMetaBytes + warp * NS * STAGE_BYTES;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  const int gw = blockIdx.x * NW + warp;
+  const int ub = a.sched_off[gw];
+  const int ue = a.sched_off[gw + 1];
+  const size_t page_stride = static_cast<size_t>(a.num_kv_heads) * ps * D * 2;
+  const uint64_t policy = l2_policy_evict_first();
+
+  // Unit record r (3 x int4): {query, split, tb, te}, {bt row, ctx, slot0, n_splits},
+  // {kvh, hc, hq0, nh}.
+  auto load_pages = [&](const int4& r0, const int4& r1, int& pg0, int& page0, int& page1) {
+    pg0 = r0.z / ps;
+    const int npages = (r0.w + ps - 1) / ps - pg0;
+    const int32_t* bt_row = a.block_tables + static_cast<size_t>(r1.x) * a.bt_stride;
+    page0 = page1 = -1;
+    if (lane < npages) {
+      const int v = bt_row[pg0 + lane];
+      page0 = (v >= 0 && v < a.num_pages) ? v : -1;
+      if (page0 < 0) report_error(1u, static_cast<uint32_t>(v));
+    }
+    if (lane + 32 < npages) {
+      const int v = bt_row[pg0 + lane + 32];
+      page1 = (v >= 0 && v < a.num_pages) ? v : -1;
+      if (page1 < 0) report_error(1u, static_cast<uint32_t>(v));
+    }
+  };
+
+  // ---------------- producer ----------------
+  // p_*: the unit being issued.  n_*: the next unit of the list, fetched while
+  // the current one streams (its record when the current unit's first slab is
+  // issued, its page ids one slab later), so unit switches never wait on memory.
+  // pq: Q fragments of the unit the producer started last, taken over by the
+  // consumer when it reaches that unit.
+  int p_pos = ub;
+  int4 p_r0 = make_int4(0, 0, 0, 0), p_r1 = p_r0, p_r2 = p_r0;
+  int p_j = 0, p_end = 0, p_pg0 = 0, p_page0 = -1, p_page1 = -1;
+  int4 n_r0 = p_r0, n_r1 = p_r0, n_r2 = p_r0;
+  int n_pg0 = 0, n_page0 = -1, n_page1 = -1;
+  int n_state = 0;  // 0: nothing fetched, 1: record fetched, 2: record and page ids fetched
+  uint32_t pq[KC][2];
+  int pq_pos = -1;
+  auto load_q = [&](const int4& r0, const int4& r2, uint32_t (&q)[KC][2]) {
+    const T* qrow = reinterpret_cast<const T*>(a.q) + (static_cast<size_t>(r0.x) * H + r2.z + gid) * D;
+#pragma unroll
+    for (int kc = 0; kc < KC; ++kc) {
+      q[kc][0] = gid < r2.w ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * tig) : 0u;
+      q[kc][1] = gid < r2.w ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 8 + 2 * tig) : 0u;
+    }
+  };
+  auto fetch_next_record = [&]() {
+    if (p_pos + 1 >= ue) return;
+    const int4* rec = a.sched_recs + static_cast<size_t>(p_pos + 1) * 3;
+    n_r0 = rec[0];
+    n_r1 = rec[1];
+    n_r2 = rec[2];
+    n_state = 1;
+  };
+  auto fetch_next_pages = [&]() {
+    load_pages(n_r0, n_r1, n_pg0, n_page0, n_page1);
+    n_state = 2;
+  };
+  auto start_unit = [&]() {
+    p_j = p_r0.z / kSlab;
+    p_end = (p_r0.w + kSlab - 1) / kSlab;
+    load_q(p_r0, p_r2, pq);
+    pq_pos = p_pos;
+    if (p_j >= p_end && p_r1.w == 1) {
+      // empty context (nothing to attend): the output row is zero (attention.hip:115)
+      T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(p_r0.x) * H + p_r2.z) * D;
+      for (int x = lane; x < p_r2.w * D; x += 32) out[x] = from_f32<T>(0.f);
+    }
+  };
+  if (p_pos < ue) {
+    const int4* rec = a.sched_recs + static_cast<size_t>(p_pos) * 3;
+    p_r0 = rec[0];
+    p_r1 = rec[1];
+    p_r2 = rec[2];
+    load_pages(p_r0, p_r1, p_pg0, p_page0, p_page1);
+    start_unit();
+  }
+  int issued = 0;
+  auto p_issue = [&]() {  // all lanes; lane 0 issues the bulk copies
+    while (p_j >= p_end) {  // current unit fully issued: move to the next one
+      if (p_pos + 1 >= ue) {
+        p_pos = ue;
+        return;
+      }
+      if (n_state == 0) fetch_next_record();
+      if (n_state == 1) fetch_next_pages();
+      ++p_pos;
+      p_r0 = n_r0;
+      p_r1 = n_r1;
+      p_r2 = n_r2;
+      p_pg0 = n_pg0;
+      p_page0 = n_page0;
+      p_page1 = n_page1;
+      n_state = 0;
+      start_unit();
+    }
+    const int idx = p_j / spp - p_pg0;
+    const int v0 = __shfl_sync(0xffffffffu, p_page0, idx & 31);
+    const int v1 = __shfl_sync(0xffffffffu, p_page1, idx & 31);
+    const int phys = idx < 32 ? v0 : v1;
+    const int s = issued % NS;
+    if (lane < 4) {
+      int4 m = lane == 0 ? p_r0 : lane == 1 ? p_r1 : lane == 2 ? p_r2 : make_int4(phys, p_j, p_pos, 0);
+      meta[s * 4 + lane] = m;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t bar = smem_u32(&bars[s]);
+      if (phys < 0) {
+        mbar_arrive(bar);
+      } else {
+        const size_t off = static_cast<size_t>(phys) * page_stride +
+                           static_cast<size_t>(p_r2.x) * ps * D * 2 +
+                           static_cast<size_t>(p_j % spp) * SLAB_BYTES;
+        mbar_arrive_expect_tx(bar, STAGE_BYTES);
+        const uint32_t dst = smem_u32(stages + s * STAGE_BYTES);
+        bulk_g2s(dst, a.k_layer + off, SLAB_BYTES, bar, policy);
+        bulk_g2s(dst + SLAB_BYTES, a.v_layer + off, SLAB_BYTES, bar, policy);
+      }
+    }
+    ++p_j;
+    ++issued;
+    if (n_state == 0) fetch_next_record();
+    else if (n_state == 1) fetch_next_pages();
+  };
+#pragma unroll 1
+  for (int k = 0; k < NS; ++k) p_issue();
+
+  // ---------------- consumer ----------------
+  int consumed = 0, waited = 0;
+  int cur = -1;  // list position of the unit being consumed
+  int4 c_r0 = make_int4(0, 0, 0, 0), c_r1 = c_r0, c_r2 = c_r0;
+  uint32_t qa[KC][2];
+  float m_run = kNegBig, l_run = 0.f;
+  float o[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+  // End of a unit: the output row, or the split's partial state.
+  auto finalize = [&]() {
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    const int query = c_r0.x, split = c_r0.y;
+    const int slot0 = c_r1.z, n_splits = c_r1.w;
+    const int hq0 = c_r2.z, nh = c_r2.w;
+    // q-heads 2tig, 2tig+1 of this lane's O^T columns: their sums live in lanes 8tig, 8tig+4
+    const float l_lo = __shfl_sync(0xffffffffu, l_run, (2 * tig) * 4);
+    const float l_hi = __shfl_sync(0xffffffffu, l_run, (2 * tig + 1) * 4);
+    const int h_lo = 2 * tig, h_hi = 2 * tig + 1;
+    if (n_splits == 1) {
+      const float i_lo = l_lo > 0.f ? 1.0f / l_lo : 0.f;
+      const float i_hi = l_hi > 0.f ? 1.0f / l_hi : 0.f;
+      T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(query) * H + hq0) * D;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        if (h_lo < nh) {
+          out[h_lo * D + 16 * mt + gid] = from_f32<T>(o[mt][0] * i_lo);
+          out[h_lo * D + 16 * mt + gid + 8] = from_f32<T>(o[mt][2] * i_lo);
+        }
+        if (h_hi < nh) {
+          out[h_hi * D + 16 * mt + gid] = from_f32<T>(o[mt][1] * i_hi);
+          out[h_hi * D + 16 * mt + gid + 8] = from_f32<T>(o[mt][3] * i_hi);
+        }
+      }
+      return;
+    }
+    const size_t slot = static_cast<size_t>(slot0 + split) * H + hq0;
+    float* po = a.part_o + slot * D;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      if (h_lo < nh) {
+        po[h_lo * D + 16 * mt + gid] = o[mt][0];
+        po[h_lo * D + 16 * mt + gid + 8] = o[mt][2];
+      }
+      if (h_hi < nh) {
+        po[h_hi * D + 16 * mt + gid] = o[mt][1];
+        po[h_hi * D + 16 * mt + gid + 8] = o[mt][3];
+      }
+    }
+    if (tig == 0 && gid < nh) a.part_ml[slot + gid] = make_float2(m_run, l_run);
+  };
+
+  constexpr int K2 = D / 32;
+  constexpr bool kAllFragsFirst = D <= 128;  // registers allow holding a whole slab
+  bool dead = false;  // a wait ran past its limit: stop computing
+#pragma unroll 1
+  while (consumed < issued && !dead) {
+    const int s = consumed % NS;
+    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), static_cast<uint32_t>(consumed / NS) & 1u);
+    if (__any_sync(0xffffffffu, !ok)) {
+      if (lane == 0) report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, static_cast<uint32_t>(consumed));
+      dead = true;
+      break;
+    }
+    waited = consumed + 1;
+    const int4 r3 = meta[s * 4 + 3];  // {phys, slab, list position}
+    if (r3.z != cur) {
+      if (cur >= 0) finalize();
+      cur = r3.z;
+      c_r0 = meta[s * 4 + 0];
+      c_r1 = meta[s * 4 + 1];
+      c_r2 = meta[s * 4 + 2];
+      if (pq_pos == cur) {
+#pragma unroll
+        for (int kc = 0; kc < KC; ++kc) {
+          qa[kc][0] = pq[kc][0];
+          qa[kc][1] = pq[kc][1];
+        }
+      } else {
+        load_q(c_r0, c_r2, qa);
+      }
+      m_run = kNegBig;
+      l_run = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      const int ctx = c_r1.y;
+      if (a.k_new != nullptr && ctx > 0 && c_r0.w == ctx && c_r2.y == 0)
+        append_row_to_pool(a, kLayoutCore, 2, c_r0.x, c_r2.x, ctx - 1,
+                           a.block_tables + static_cast<size_t>(c_r1.x) * a.bt_stride, lane);
+    }
+    const int j = r3.y;
+    const int te = c_r0.w, ctx = c_r1.y;
+    const bool have = r3.x >= 0;
+    const int valid = min(kSlab, te - j * kSlab);
+    uint8_t* st = stages + s * STAGE_BYTES;
+    const uint32_t kbase = smem_u32(st);
+    const uint32_t vbase = kbase + SLAB_BYTES;
+    const int jm = lane >> 3;
+    if (have) {
+      if (valid < kSlab) {
+        // positions past the context may hold anything: clear them
+        const int nunits = (kSlab - valid) * U;
+        for (int x = lane; x < 2 * nunits; x += 32) {
+          const int kv = x / nunits, r = x - kv * nunits;
+          const int tt = valid + r / U, uu = r - (r / U) * U;
+          *reinterpret_cast<uint4*>(st + kv * SLAB_BYTES + unit_offset(kLayoutCore, tt, uu, U) * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      if (a.k_new != nullptr && ctx > 0 && te == ctx && j == (ctx - 1) / kSlab) {
+        patch_slab_row(a, kLayoutCore, 2, st, SLAB_BYTES, c_r0.x, c_r2.x, (ctx - 1) - j * kSlab,
+                       lane, 32);
+        __syncwarp();
+      }
+    }
+    // K and V fragments of the slab (all of them when registers allow, so the
+    // stage can be refilled before the math; otherwise K first, V after S).
+    uint32_t kf[K2][2][4];
+    uint32_t vf[kAllFragsFirst ? MT : 1][4];
+    float sc[2][2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int par = 0; par < 2; ++par)
+        sc[nt][par][0] = sc[nt][par][1] = sc[nt][par][2] = sc[nt][par][3] = 0.f;
+    if (have) {
+#pragma unroll
+      for (int k2 = 0; k2 < K2; ++k2)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, kf[k2][nt][0],
+                  kf[k2][nt][1], kf[k2][nt][2], kf[k2][nt][3]);
+      if constexpr (kAllFragsFirst) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, vf[mt][0],
+                    vf[mt][1], vf[mt][2], vf[mt][3]);
+      }
+#pragma unroll
+      for (int k2 = 0; k2 < K2; ++k2)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          Mma<T>::run(sc[nt][0], qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, kf[k2][nt][0], kf[k2][nt][1]);
+          Mma<T>::run(sc[nt][1], qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, kf[k2][nt][2],
+                      kf[k2][nt][3]);
+        }
+    }
+    uint32_t vlate[kAllFragsFirst ? 1 : MT][4];
+    if constexpr (!kAllFragsFirst) {
+      if (have) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16,
+                    vlate[mt][0], vlate[mt][1], vlate[mt][2], vlate[mt][3]);
+      }
+    }
+    // Every fragment has landed in registers (the XOR reads one register of
+    // each ldmatrix, so it waits for all of them): the stage can be refilled.
+    {
+      uint32_t dep = 0;
+      if (have) {
+        if constexpr (kAllFragsFirst) {
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) dep ^= vf[mt][0];
+        } else {
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) dep ^= vlate[mt][0];
+        }
+      }
+      asm volatile("" ::"r"(dep));
+    }
+    __syncwarp();
+    ++consumed;
+    if (lane == 0) fence_proxy_async();
+    p_issue();
+    if (!have) continue;
+
+    const int t0 = 2 * tig;
+    const bool v0 = t0 < valid, v1 = t0 + 1 < valid, v2 = t0 + 8 < valid, v3 = t0 + 9 < valid;
+    const float x0 = (sc[0][0][0] + sc[0][1][0]) * a.scale_log2;
+    const float x1 = (sc[0][0][1] + sc[0][1][1]) * a.scale_log2;
+    const float x2 = (sc[1][0][0] + sc[1][1][0]) * a.scale_log2;
+    const float x3 = (sc[1][0][1] + sc[1][1][1]) * a.scale_log2;
+    float mx = fmaxf(fmaxf(v0 ? x0 : kNegBig, v1 ? x1 : kNegBig),
+                     fmaxf(v2 ? x2 : kNegBig, v3 ? x3 : kNegBig));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float alpha = fast_exp2(m_run - m_new);
+    const float p0 = v0 ? fast_exp2(x0 - m_new) : 0.f;
+    const float p1 = v1 ? fast_exp2(x1 - m_new) : 0.f;
+    const float p2 = v2 ? fast_exp2(x2 - m_new) : 0.f;
+    const float p3 = v3 ? fast_exp2(x3 - m_new) : 0.f;
+    l_run = l_run * alpha + ((p0 + p1) + (p2 + p3));
+    m_run = m_new;
+    const uint32_t pb0 = Mma<T>::pack(p0, p1);
+    const uint32_t pb1 = Mma<T>::pack(p2, p3);
+    const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * tig) * 4);
+    const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * tig + 1) * 4);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      o[mt][0] *= a_lo;
+      o[mt][1] *= a_hi;
+      o[mt][2] *= a_lo;
+      o[mt][3] *= a_hi;
+      if constexpr (kAllFragsFirst) {
+        Mma<T>::run(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], pb0, pb1);
+      } else {
+        Mma<T>::run(o[mt], vlate[mt][0], vlate[mt][1], vlate[mt][2], vlate[mt][3], pb0, pb1);
+      }
+    }
+  }
+  if (cur >= 0 && !dead) finalize();
+  // Bounded waits for copies still landing in this warp's ring (none unless a
+  // wait gave up above).
+  for (int k = waited; k < issued; ++k)
+    (void)mbar_wait_bounded(smem_u32(&bars[k % NS]), static_cast<uint32_t>(k / NS) & 1u);
+  // The split merge (a programmatic dependent launch) may start being scheduled.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// =====================================================================================
+// Split merge of the persistent path: one warp per (query with several splits,
+// q-head), lanes over head dims.  Runs as a programmatic dependent launch after
+// decode_persistent_kernel and waits for it (griddepcontrol.wait) before
+// reading the partial states:
+//   M = max_k M_k,  L = sum_k L_k 2^(M_k - M),  out = sum_k O_k 2^(M_k - M) / L
+// with the splits added in index order (the result does not depend on timing).
+// =====================================================================================
+template <typename T, int EPL>
+__global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * 4 + warp;
+  if (h >= a.num_heads) return;
+  const int query = a.merge_queries[blockIdx.x];
+  const int4 qi = a.qinfo[query];
+  const int slot0 = qi.z, n = qi.w;
+  const int H = a.num_heads, D = a.head_dim;
+  const float2* ml = a.part_ml + static_cast<size_t>(slot0) * H + h;
+  const float* po = a.part_o + (static_cast<size_t>(slot0) * H + h) * D + lane;
+  float mx = kNegBig;
+  for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(&ml[static_cast<size_t>(k) * H]).x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  float acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+  for (int k0 = 0; k0 < n; k0 += 32) {
+    const int kn = min(32, n - k0);
+    float w = 0.f;
+    if (lane < kn) {
+      const float2 v = __ldcg(&ml[static_cast<size_t>(k0 + lane) * H]);
+      w = fast_exp2(v.x - mx);
+      sum += v.y * w;
+    }
+    int kk = 0;
+    for (; kk + 4 <= kn; kk += 4) {  // four splits' loads in flight at once
+      float v[4][EPL];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e)
+          v[u][e] = __ldcg(po + static_cast<size_t>(k0 + kk + u) * H * D + 32 * e);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float wk = __shfl_sync(0xffffffffu, w, kk + u);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] += v[u][e] * wk;
+      }
+    }
+    for (; kk < kn; ++kk) {
+      const float wk = __shfl_sync(0xffffffffu, w, kk);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e)
+        acc[e] += __ldcg(po + static_cast<size_t>(k0 + kk) * H * D + 32 * e) * wk;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+  T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(query) * H + h) * D + lane;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) out[32 * e] = from_f32<T>(acc[e] * inv);
+}
+
+// =====================================================================================
 // CUDA-core split-K decode kernel: fp32 storage (linear layout) and 16-bit head
 // dims the tensor-core kernel does not cover.  One warp per q-head of the chunk,
 // lanes over head dims (element d = lane + 32 e, like attention.hip:65-73), the
@@ -537,8 +1105,8 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
   b /= a.n_hchunk;
   const int kvh = b % a.num_kv_heads;
   b /= a.num_kv_heads;
-  const int4 it = a.items[b];
-  const int4 qi = a.qinfo[it.x];
+  const int4 it = a.items[2 * b];
+  const int4 qi = a.items[2 * b + 1];
   const int query = it.x, split = it.y, tb = it.z, te = it.w;
   const int hq0 = kvh * a.group + hc * 8;
   const int nh = min(8, a.group - hc * 8);
@@ -573,17 +1141,29 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
   const size_t page_stride = static_cast<size_t>(a.num_kv_heads) * ps * D * ES;
   const uint64_t policy = l2_policy_evict_first();
 
-  auto slab_page = [&](int j) -> int {
-    const int phys = bt_row[j / slabs_per_page];
-    return (phys >= 0 && phys < a.num_pages) ? phys : -1;
-  };
+  // The split's page ids, read once into shared memory.
+  __shared__ int s_pages[kMaxSplitPages];
+  const int pg0 = tb / ps;
+  const int npages = (te + ps - 1) / ps - pg0;
+  if (threadIdx.x < kMaxSplitPages) {
+    int v = -1;
+    if (static_cast<int>(threadIdx.x) < npages) {
+      v = bt_row[pg0 + threadIdx.x];
+      if (v < 0 || v >= a.num_pages) {
+        report_error(1u, static_cast<uint32_t>(v));
+        v = -1;
+      }
+    }
+    s_pages[threadIdx.x] = v;
+  }
+  __syncthreads();
+  auto slab_page = [&](int j) -> int { return s_pages[j / slabs_per_page - pg0]; };
   auto issue = [&](int i) {  // thread 0 only
     const int j = sb0 + i;
     const int s = i % NS;
     const uint32_t bar = smem_u32(&bars[s]);
     const int phys = slab_page(j);
     if (phys < 0) {
-      report_error(1u, static_cast<uint32_t>(bt_row[j / slabs_per_page]));
       mbar_arrive(bar);
       return;
     }
@@ -598,6 +1178,12 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
   if (threadIdx.x == 0)
     for (int i = 0; i < min(NS, nslabs); ++i) issue(i);
   int issued = min(NS, nslabs);
+
+  const int ctx = qi.y;
+  const bool owns_new = a.k_new != nullptr && ctx > 0 && te == ctx;
+  const int new_slab = (ctx - 1) / kSlab;
+  if (owns_new && hc == 0 && warp == 0)
+    append_row_to_pool(a, layout, ES, query, kvh, ctx - 1, bt_row, lane);
 
   float m_run = kNegBig, l_run = 0.f;
   __shared__ int s_abort;
@@ -616,6 +1202,11 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
     consumed = i + 1;
     const uint8_t* st = region + s * stage_bytes;
     const int valid = min(kSlab, te - j * kSlab);
+    if (owns_new && j == new_slab) {
+      patch_slab_row(a, layout, ES, const_cast<uint8_t*>(st), slab_bytes, query, kvh,
+                     (ctx - 1) - j * kSlab, threadIdx.x, blockDim.x);
+      __syncthreads();
+    }
     if (active && slab_page(j) >= 0) {
       for (int t = 0; t < valid; ++t) {
         float dot = 0.f;
@@ -692,31 +1283,91 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
 // =====================================================================================
 namespace {
 
-constexpr int kNW = 4;
-
-template <int D>
-constexpr int mma_stages() {
-  return D <= 128 ? 3 : 2;
-}
-
-template <typename T, int D>
-cudaError_t run_mma(const DecodeArgs& a, cudaStream_t s) {
-  constexpr int NS = mma_stages<D>();
-  constexpr size_t stage_region = static_cast<size_t>(kNW) * NS * 2 * kSlab * D * 2;
-  const size_t combine = (2 * kNW * 8 + static_cast<size_t>(kNW) * 8 * (D + 4)) * sizeof(float);
+template <typename T, int D, int NW, int NS>
+cudaError_t run_mma_cfg(const DecodeArgs& a, cudaStream_t s) {
+  constexpr size_t stage_region = static_cast<size_t>(NW) * NS * 2 * kSlab * D * 2;
+  const size_t combine = (2 * NW * 8 + static_cast<size_t>(NW) * 8 * (D + 4)) * sizeof(float);
   const size_t merge = (8 * kMergeChunk + 8 * static_cast<size_t>(D) + 16) * sizeof(float);
-  static_assert(kNW * NS * sizeof(uint64_t) <= kBarBytes, "mbarrier block too small");
+  static_assert(NW * NS * sizeof(uint64_t) <= kBarBytes, "mbarrier block too small");
   size_t smem = stage_region;
   if (combine > smem) smem = combine;
   if (merge > smem) smem = merge;
   smem += kBarBytes;
-  auto kern = decode_mma_kernel<T, D, kNW, NS>;
+  auto kern = decode_mma_kernel<T, D, NW, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const unsigned grid = static_cast<unsigned>(a.n_items) * a.num_kv_heads * a.n_hchunk;
-  kern<<<grid, kNW * 32, smem, s>>>(a);
+  kern<<<grid, NW * 32, smem, s>>>(a);
   return cudaGetLastError();
+}
+
+// Tuning knob for head_dim 128: KVC_DECODE_VARIANT="<warps>x<stages>" picks one of
+// the compiled (warps per CTA, stages per warp) shapes; default 4x3.
+int decode_variant_128() {
+  static int v = [] {
+    const char* e = getenv("KVC_DECODE_VARIANT");
+    if (!e) return 43;
+    if (strncmp(e, "legacy", 6) == 0) e += 6;
+    int nw = 0, ns = 0;
+    if (sscanf(e, "%dx%d", &nw, &ns) != 2) return 43;
+    return nw * 10 + ns;
+  }();
+  return v;
+}
+
+template <typename T, int D, int NW>
+cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
+  constexpr int NS = persist_stages<D>();
+  const size_t smem =
+      kPersistBarBytes + kPersistMetaBytes + static_cast<size_t>(NW) * NS * 2 * kSlab * D * 2;
+  auto kern = decode_persistent_kernel<T, D, NW, NS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  if (a.n_sched_ctas <= 0) return cudaSuccess;
+  kern<<<a.n_sched_ctas, NW * 32, smem, s>>>(a);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (a.n_merge_queries <= 0) return cudaSuccess;
+  // merge as a programmatic dependent launch: scheduled while the decode grid drains
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.n_merge_queries), (a.num_heads + 3) / 4, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a);
+}
+
+bool use_legacy_decode() {
+  static bool v = [] {
+    const char* e = getenv("KVC_DECODE_VARIANT");
+    return e != nullptr && strncmp(e, "legacy", 6) == 0;
+  }();
+  return v;
+}
+
+template <typename T, int D>
+cudaError_t run_mma(const DecodeArgs& a, cudaStream_t s) {
+  if (!use_legacy_decode() && a.sched_off != nullptr) return run_persistent<T, D, kPersistWarps>(a, s);
+  if constexpr (D == 128) {
+    switch (decode_variant_128()) {
+      case 42: return run_mma_cfg<T, D, 4, 2>(a, s);
+      case 45: return run_mma_cfg<T, D, 4, 5>(a, s);
+      case 23: return run_mma_cfg<T, D, 2, 3>(a, s);
+      case 24: return run_mma_cfg<T, D, 2, 4>(a, s);
+      case 26: return run_mma_cfg<T, D, 2, 6>(a, s);
+      case 82: return run_mma_cfg<T, D, 8, 2>(a, s);
+      case 83: return run_mma_cfg<T, D, 8, 3>(a, s);
+      default: return run_mma_cfg<T, D, 4, 3>(a, s);
+    }
+  } else {
+    return run_mma_cfg<T, D, 4, (D <= 128 ? 3 : 2)>(a, s);
+  }
 }
 
 template <typename T, int EPL>

@@ -20,7 +20,7 @@
 #include <mutex>
 #include <vector>
 
-#include "../../include/kvcache.h"
+#include "kvcache.h"
 #include "kvc_common.h"
 #include "kvc_internal.h"
 
