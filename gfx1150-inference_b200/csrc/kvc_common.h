@@ -54,6 +54,7 @@ struct kvc_plan {
   int num_heads = 0, num_kv_heads = 0, group = 0, n_hchunk = 0;
   int head_dim = 0, page_size = 0, max_ctx = 0;
   bool rows_distinct = true;   // every query has its own block-table row
+  int flags = 0;               // KVC_PLAN_*
   kvc::PoolGeom pool_geom;
   std::vector<int4> items, qinfo, item_pairs;
   std::vector<int32_t> rows, positions, sched_off;

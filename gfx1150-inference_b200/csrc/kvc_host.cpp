@@ -567,6 +567,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.sched_off = static_cast<const int32_t*>(plan->d_sched_off.ptr);
   a.sched_recs = static_cast<const int4*>(plan->d_sched_units.ptr);
   a.n_sched_ctas = plan->n_sched_ctas;
+  a.early_prefetch = (plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0;
   a.merge_queries = static_cast<const int32_t*>(plan->d_merge.ptr);
   a.n_merge_queries = static_cast<int>(plan->merge_queries.size());
   a.k_new = static_cast<const uint8_t*>(d_k_new);
@@ -643,6 +644,13 @@ extern "C" int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const i
       plan, pool->g, n_queries, num_heads, [&](int i) { return h_ctx_lens[i]; },
       [&](int i) { return h_rows ? h_rows[i] : i; }, pool->device,
       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvc_plan_set_flags(kvc_plan_t* plan, int flags) {
+  if (!plan) return set_error(KVC_ERR_INVALID_ARG, "plan must not be null.");
+  if (flags & ~KVC_PLAN_KV_STABLE) return set_error(KVC_ERR_INVALID_ARG, "unknown plan flags %d.", flags);
+  plan->flags = flags;
+  return KVC_OK;
 }
 
 extern "C" int kvc_plan_info(const kvc_plan_t* plan, int* n_items, int* n_ctas,

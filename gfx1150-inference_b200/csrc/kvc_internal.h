@@ -128,6 +128,10 @@ struct DecodeArgs {
   const int32_t* sched_off;
   const int4* sched_recs;
   int n_sched_ctas;
+  // Block tables and KV pages are not written by the kernel launched just before
+  // (plan flag KVC_PLAN_KV_STABLE): the decode kernel may start streaming them
+  // before that kernel's results are visible.
+  int early_prefetch;
   // queries with more than one split (merged by merge_splits_kernel)
   const int32_t* merge_queries;
   int n_merge_queries;

@@ -724,15 +724,18 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     load_pages(n_r0, n_r1, n_pg0, n_page0, n_page1);
     n_state = 2;
   };
+  bool dep_ready = false;  // the preceding kernel's results are visible (griddepcontrol.wait)
   auto start_unit = [&]() {
     p_j = p_r0.z / kSlab;
     p_end = (p_r0.w + kSlab - 1) / kSlab;
-    load_q(p_r0, p_r2, pq);
-    pq_pos = p_pos;
-    if (p_j >= p_end && p_r1.w == 1) {
-      // empty context (nothing to attend): the output row is zero (attention.hip:115)
-      T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(p_r0.x) * H + p_r2.z) * D;
-      for (int x = lane; x < p_r2.w * D; x += 32) out[x] = from_f32<T>(0.f);
+    // An empty context still gets one slab without data, so the consumer
+    // finalizes the unit and writes its zero row (attention.hip:115).
+    if (p_end <= p_j) p_end = p_j + 1;
+    if (dep_ready) {  // q may come from the preceding kernel
+      load_q(p_r0, p_r2, pq);
+      pq_pos = p_pos;
+    } else {
+      pq_pos = -1;
     }
   };
   if (p_pos < ue) {
@@ -765,7 +768,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     const int idx = p_j / spp - p_pg0;
     const int v0 = __shfl_sync(0xffffffffu, p_page0, idx & 31);
     const int v1 = __shfl_sync(0xffffffffu, p_page1, idx & 31);
-    const int phys = idx < 32 ? v0 : v1;
+    const int phys = p_r0.w > p_r0.z ? (idx < 32 ? v0 : v1) : -1;
     const int s = issued % NS;
     if (lane < 4) {
       int4 m = lane == 0 ? p_r0 : lane == 1 ? p_r1 : lane == 2 ? p_r2 : make_int4(phys, p_j, p_pos, 0);
@@ -791,8 +794,20 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     if (n_state == 0) fetch_next_record();
     else if (n_state == 1) fetch_next_pages();
   };
+  // Prologue: fill the ring.  Before griddepcontrol.wait only the plan, the
+  // block tables and KV pages are read, and only when the caller declared them
+  // stable across the preceding launch (KVC_PLAN_KV_STABLE); q, the new rows
+  // and every write come after it.
+  if (!a.early_prefetch) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    dep_ready = true;
+  }
 #pragma unroll 1
   for (int k = 0; k < NS; ++k) p_issue();
+  if (!dep_ready) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    dep_ready = true;
+  }
 
   // ---------------- consumer ----------------
   int consumed = 0, waited = 0;
@@ -1029,6 +1044,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
 template <typename T, int EPL>
 __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the next decode launch may start filling its ring while the merge runs
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + warp;
   if (h >= a.num_heads) return;
@@ -1326,8 +1343,21 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   if (a.n_sched_ctas <= 0) return cudaSuccess;
-  kern<<<a.n_sched_ctas, NW * 32, smem, s>>>(a);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    // programmatic dependent launch: the ring prologue may overlap the tail of
+    // the preceding kernel (see griddepcontrol.wait in the kernel)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.n_sched_ctas), 1, 1);
+    cfg.blockDim = dim3(NW * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if ((e = cudaLaunchKernelEx(&cfg, kern, a)) != cudaSuccess) return e;
+  }
   if (a.n_merge_queries <= 0) return cudaSuccess;
   // merge as a programmatic dependent launch: scheduled while the decode grid drains
   cudaLaunchConfig_t cfg = {};
@@ -1335,9 +1365,6 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   cfg.blockDim = dim3(128, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a);

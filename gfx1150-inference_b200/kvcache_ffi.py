@@ -36,6 +36,8 @@ DTYPE_F16 = 0
 DTYPE_BF16 = 1
 DTYPE_F32 = 2
 
+PLAN_KV_STABLE = 1
+
 OFFLOAD_PINNED = 1
 OFFLOAD_REGISTER = 2
 
@@ -78,6 +80,7 @@ SIGNATURES = {
     "kvc_plan_create": (_c_int, [ctypes.POINTER(_vp)]),
     "kvc_plan_destroy": (_c_int, [_vp]),
     "kvc_plan_decode": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
+    "kvc_plan_set_flags": (_c_int, [_vp, _c_int]),
     "kvc_plan_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
                                ctypes.POINTER(_c_size)]),
     "kvc_decode": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_float, _vp]),

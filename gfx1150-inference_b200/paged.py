@@ -68,6 +68,12 @@ class DecodePlan:
         self.num_heads = 0
         self.ctx_lens: Optional[np.ndarray] = None
 
+    def set_kv_stable(self, stable: bool = True) -> None:
+        """Declare that block tables and KV pages are not written by the kernel
+        launched right before each decode (lets the kernel start streaming KV
+        early; see KVC_PLAN_KV_STABLE)."""
+        ffi.check(ffi.lib.kvc_plan_set_flags(self.handle, ffi.PLAN_KV_STABLE if stable else 0))
+
     def info(self) -> PlanInfo:
         n_items, n_ctas = ctypes.c_int(), ctypes.c_int()
         scratch = ctypes.c_size_t()

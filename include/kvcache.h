@@ -191,6 +191,14 @@ KVC_API int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const int3
                     const int32_t* h_ctx_lens, int n_queries, int num_heads,
                     void* stream);
 
+/* Plan flags.  KVC_PLAN_KV_STABLE: the block tables and KV pages the plan reads
+ * are not written by the kernel launched immediately before each decode on the
+ * stream (e.g. they change only through host copies or earlier steps), so the
+ * decode kernel may start streaming KV pages before that kernel's results are
+ * visible (programmatic dependent launch).  Without it, the kernel waits first. */
+#define KVC_PLAN_KV_STABLE 1
+KVC_API int kvc_plan_set_flags(kvc_plan_t* plan, int flags);
+
 /* Number of split items, CTAs and bytes of split scratch of the last plan. */
 KVC_API int kvc_plan_info(const kvc_plan_t* plan, int* n_items, int* n_ctas, size_t* scratch_bytes);
 
