@@ -20,8 +20,13 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
+#include <mutex>
+
+#include "kvc_common.h"
 #include "kvc_device.cuh"
 #include "kvc_internal.h"
+#include "kvcache.h"
 
 namespace kvc {
 
@@ -1459,3 +1464,262 @@ cudaError_t launch_decode(const DecodeArgs& a, int dtype, int layout, cudaStream
 }
 
 }  // namespace kvc
+
+// =====================================================================================
+// kvc_decode_noalloc: the decode for callers that cannot allocate device memory.
+//
+// Some hosts of this library (a runtime that owns every device allocation
+// through its own arena, a plugin that may not call cudaMalloc, code recorded
+// into a graph by a framework that forbids allocation) can still hand over
+// their KV pages, q and out, but cannot let the library allocate its plan and
+// split scratch.  This entry point keeps both in g_noalloc_scratch, a
+// file-scope device array of kNoAllocScratchBytes that every GPU loading the
+// library holds until the process exits, and stages the plan in static host
+// buffers.  It calls no cudaMalloc / cudaFree or other allocating routine.
+// Requests that do not fit are rejected with KVC_ERR_INVALID_ARG.
+// =====================================================================================
+namespace kvc {
+int split_tokens_for(int page_size);
+}
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
+constexpr int kNoAllocMaxQueries = 4096;
+constexpr int kNoAllocMaxItems = 16384;
+constexpr int kNoAllocMaxUnits = 65536;
+constexpr int kNoAllocMaxBins = 2048;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
+
+// Host staging (static, no heap).  Layout mirrors the device scratch.
+int4 h_items[kNoAllocMaxItems];
+int4 h_qinfo[kNoAllocMaxQueries];
+int4 h_recs[3 * kNoAllocMaxUnits];
+int32_t h_sched_off[kNoAllocMaxBins + 1];
+int32_t h_merge[kNoAllocMaxQueries];
+int32_t h_unit_bin[kNoAllocMaxUnits];
+int32_t h_bin_fill[kNoAllocMaxBins];
+int64_t h_heap_load[kNoAllocMaxBins];
+int32_t h_heap_bin[kNoAllocMaxBins];
+int32_t h_order[kNoAllocMaxItems];
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Fixed-capacity binary min-heap of (load, bin) pairs (ties: lower bin first).
+bool heap_less(int i, int j) {
+  return h_heap_load[i] < h_heap_load[j] ||
+         (h_heap_load[i] == h_heap_load[j] && h_heap_bin[i] < h_heap_bin[j]);
+}
+void heap_swap(int i, int j) {
+  const int64_t l = h_heap_load[i];
+  h_heap_load[i] = h_heap_load[j];
+  h_heap_load[j] = l;
+  const int32_t b = h_heap_bin[i];
+  h_heap_bin[i] = h_heap_bin[j];
+  h_heap_bin[j] = b;
+}
+void heap_sift_down(int i, int n) {
+  for (;;) {
+    int m = i;
+    const int l = 2 * i + 1, r = 2 * i + 2;
+    if (l < n && heap_less(l, m)) m = l;
+    if (r < n && heap_less(r, m)) m = r;
+    if (m == i) return;
+    heap_swap(i, m);
+    i = m;
+  }
+}
+
+}  // namespace
+
+extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, int num_pages,
+                                  int page_size, int num_kv_heads, int head_dim, int dtype,
+                                  const int32_t* d_block_tables, int bt_stride,
+                                  const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                                  const void* d_q, void* d_out, float scale, void* stream) {
+  using namespace kvc;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (dtype != KVC_DTYPE_F16 && dtype != KVC_DTYPE_BF16)
+    return set_error(KVC_ERR_INVALID_ARG, "kvc_decode_noalloc supports fp16 and bf16 KV pages only.");
+  if (!decode_uses_mma(dtype, head_dim, page_size))
+    return set_error(KVC_ERR_INVALID_ARG,
+                     "kvc_decode_noalloc needs head_dim in {32,64,96,128,160,192,256} and a "
+                     "page_size multiple of 16 (got %d, %d).", head_dim, page_size);
+  if (num_pages <= 0 || num_kv_heads <= 0 || bt_stride <= 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_pages, num_kv_heads and bt_stride must be positive.");
+  if (num_heads <= 0 || num_heads % num_kv_heads != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
+  if (n_queries < 0 || n_queries > kNoAllocMaxQueries)
+    return set_error(KVC_ERR_INVALID_ARG, "kvc_decode_noalloc accepts at most %d queries (got %d).",
+                     kNoAllocMaxQueries, n_queries);
+  if (n_queries == 0) return KVC_OK;
+  if (!d_k_layer || !d_v_layer || !d_block_tables || !h_ctx_lens || !d_q || !d_out)
+    return set_error(KVC_ERR_INVALID_ARG, "pointers must not be null.");
+  if ((reinterpret_cast<uintptr_t>(d_k_layer) | reinterpret_cast<uintptr_t>(d_v_layer)) & 15u)
+    return set_error(KVC_ERR_INVALID_ARG, "KV page buffers must be 16-byte aligned.");
+  if ((reinterpret_cast<uintptr_t>(d_q) | reinterpret_cast<uintptr_t>(d_out)) & 3u)
+    return set_error(KVC_ERR_INVALID_ARG, "q and out must be 4-byte aligned.");
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(KVC_ERR_INVALID_ARG, "device index %d is beyond kvc_decode_noalloc's table.", dev);
+  // Set-up, once per device with that device current: the device address of the
+  // scratch array (its host-side name is only a stand-in, not a device pointer).
+  if (!g_noalloc_dev_ptr[dev]) {
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) != cudaSuccess)
+      return cuda_error(e, "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_dev_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+
+  // ---- split list (the same partition as kvc_plan_decode) ----
+  const int C = split_tokens_for(page_size);
+  int n_items = 0, slot = 0, max_ctx = 0;
+  for (int i = 0; i < n_queries; ++i) {
+    const int ctx = h_ctx_lens[i];
+    if (ctx < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
+    if (static_cast<int64_t>(ctx) > static_cast<int64_t>(bt_stride) * page_size)
+      return set_error(KVC_ERR_OUT_OF_RANGE, "a context length exceeds the block-table width.");
+    const int ns = ctx > 0 ? (ctx + C - 1) / C : 1;
+    if (n_items + ns > kNoAllocMaxItems)
+      return set_error(KVC_ERR_INVALID_ARG, "kvc_decode_noalloc accepts at most %d splits.",
+                       kNoAllocMaxItems);
+    h_qinfo[i] = make_int4(i, ctx, slot, ns);
+    for (int k = 0; k < ns; ++k)
+      h_items[n_items++] = make_int4(i, k, k * C, std::min((k + 1) * C, ctx));
+    slot += ns;
+    max_ctx = std::max(max_ctx, ctx);
+  }
+  for (int k = 0; k < n_items; ++k) h_order[k] = k;
+  std::sort(h_order, h_order + n_items, [](int x, int y) {
+    const int lx = h_items[x].w - h_items[x].z, ly = h_items[y].w - h_items[y].z;
+    return lx != ly ? lx > ly : x < y;
+  });
+  const int group = num_heads / num_kv_heads;
+  const int nhc = (group + 7) / 8;
+  const int per_item = num_kv_heads * nhc;
+  const int64_t n_units64 = static_cast<int64_t>(n_items) * per_item;
+  if (n_units64 > kNoAllocMaxUnits)
+    return set_error(KVC_ERR_INVALID_ARG, "kvc_decode_noalloc accepts at most %d work units.",
+                     kNoAllocMaxUnits);
+  const int n_units = static_cast<int>(n_units64);
+
+  // ---- scratch layout and size check ----
+  const size_t H = static_cast<size_t>(num_heads);
+  const size_t off_items = 0;
+  const size_t off_qinfo = align256(off_items + sizeof(int4) * 2 * n_items);
+  const size_t off_recs = align256(off_qinfo + sizeof(int4) * n_queries);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
+  const int n_bins = n_ctas * kPersistWarps;
+  if (n_bins > kNoAllocMaxBins)
+    return set_error(KVC_ERR_INVALID_ARG, "too many SMs for kvc_decode_noalloc's schedule table.");
+  const size_t off_soff = align256(off_recs + sizeof(int4) * 3 * n_units);
+  const size_t off_merge = align256(off_soff + sizeof(int32_t) * (n_bins + 1));
+  const size_t plan_bytes = align256(off_merge + sizeof(int32_t) * n_queries);
+  const size_t off_part_ml = plan_bytes;
+  const size_t off_part_o = align256(off_part_ml + sizeof(float2) * slot * H);
+  const size_t need = off_part_o + sizeof(float) * slot * H * head_dim;
+  if (need > kNoAllocScratchBytes)
+    return set_error(KVC_ERR_INVALID_ARG,
+                     "kvc_decode_noalloc needs %zu bytes of scratch for this batch; its fixed "
+                     "scratch holds %zu bytes (use kvc_decode for larger batches).",
+                     need, kNoAllocScratchBytes);
+
+  // ---- schedule: units onto warps, longest first onto the least-loaded warp ----
+  for (int b = 0; b < n_bins; ++b) {
+    h_heap_load[b] = 0;
+    h_heap_bin[b] = b;
+    h_bin_fill[b] = 0;
+  }
+  for (int r = 0; r < n_units; ++r) {
+    const int k = h_order[r / per_item];
+    const int64_t cost = (h_items[k].w - h_items[k].z) + 64;
+    h_unit_bin[r] = h_heap_bin[0];
+    h_bin_fill[h_heap_bin[0]]++;
+    h_heap_load[0] += cost;
+    heap_sift_down(0, n_bins);
+  }
+  h_sched_off[0] = 0;
+  for (int b = 0; b < n_bins; ++b) h_sched_off[b + 1] = h_sched_off[b] + h_bin_fill[b];
+  for (int b = 0; b < n_bins; ++b) h_bin_fill[b] = h_sched_off[b];
+  int4* recs = h_recs;
+  for (int r = 0; r < n_units; ++r) {
+    const int k = h_order[r / per_item];
+    const int u = r % per_item;
+    const int kvh = u / nhc, hc = u % nhc;
+    const int4 it = h_items[k];
+    const int pos = h_bin_fill[h_unit_bin[r]]++;
+    recs[3 * pos + 0] = it;
+    recs[3 * pos + 1] = make_int4(0, h_qinfo[it.x].y, h_qinfo[it.x].z, h_qinfo[it.x].w);
+    recs[3 * pos + 1].x = it.x;  // block-table row of query i is row i
+    recs[3 * pos + 2] = make_int4(kvh, hc, kvh * group + hc * 8, std::min(8, group - hc * 8));
+  }
+  int n_merge = 0;
+  for (int i = 0; i < n_queries; ++i)
+    if (h_qinfo[i].w > 1) h_merge[n_merge++] = i;
+  // items are stored as {split, query record} pairs like kvc_plan_decode's
+  static int4 h_item_pairs[2 * kNoAllocMaxItems];
+  for (int k = 0; k < n_items; ++k) {
+    h_item_pairs[2 * k] = h_items[h_order[k]];
+    h_item_pairs[2 * k + 1] = h_qinfo[h_items[h_order[k]].x];
+  }
+  for (int i = 0; i < n_queries; ++i) h_qinfo[i].x = i;
+
+  // ---- upload (pageable host source: the call returns once it is staged) ----
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* base = g_noalloc_dev_ptr[dev];
+  if ((e = cudaMemcpyAsync(base + off_items, h_item_pairs, sizeof(int4) * 2 * n_items,
+                           cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(base + off_qinfo, h_qinfo, sizeof(int4) * n_queries,
+                           cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(base + off_recs, h_recs, sizeof(int4) * 3 * n_units,
+                           cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(base + off_soff, h_sched_off, sizeof(int32_t) * (n_bins + 1),
+                           cudaMemcpyHostToDevice, s)) ||
+      (n_merge > 0 && (e = cudaMemcpyAsync(base + off_merge, h_merge, sizeof(int32_t) * n_merge,
+                                           cudaMemcpyHostToDevice, s))))
+    return cuda_error(e, "kvc_decode_noalloc plan upload");
+
+  DecodeArgs a = {};
+  a.k_layer = static_cast<const uint8_t*>(d_k_layer);
+  a.v_layer = static_cast<const uint8_t*>(d_v_layer);
+  a.q = d_q;
+  a.out = d_out;
+  a.block_tables = d_block_tables;
+  a.bt_stride = bt_stride;
+  a.items = reinterpret_cast<const int4*>(base + off_items);
+  a.qinfo = reinterpret_cast<const int4*>(base + off_qinfo);
+  a.part_o = reinterpret_cast<float*>(base + off_part_o);
+  a.part_ml = reinterpret_cast<float2*>(base + off_part_ml);
+  a.counters = nullptr;  // not used by the tensor-core path
+  a.sched_off = reinterpret_cast<const int32_t*>(base + off_soff);
+  a.sched_recs = reinterpret_cast<const int4*>(base + off_recs);
+  a.n_sched_ctas = n_units > 0 ? n_ctas : 0;
+  a.early_prefetch = 0;
+  a.merge_queries = reinterpret_cast<const int32_t*>(base + off_merge);
+  a.n_merge_queries = n_merge;
+  a.k_new = nullptr;
+  a.v_new = nullptr;
+  a.n_items = n_items;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.n_hchunk = nhc;
+  a.head_dim = head_dim;
+  a.page_size = page_size;
+  a.num_pages = num_pages;
+  a.scale_log2 = scale * kLog2e;
+  (void)max_ctx;
+  if ((e = launch_decode(a, dtype, kLayoutCore, s)) != cudaSuccess)
+    return cuda_error(e, "kvc_decode_noalloc kernels");
+  return KVC_OK;
+}

@@ -89,6 +89,8 @@ SIGNATURES = {
     "kvc_decode_host": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_float,
                                  _vp]),
     "kvc_gather": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "kvc_decode_noalloc": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_int,
+                                    _vp, _c_int, _c_int, _vp, _vp, _c_float, _vp]),
     "kvc_host_alloc": (_c_int, [_c_size, ctypes.POINTER(_vp)]),
     "kvc_host_free": (_c_int, [_vp]),
     "kvc_offload_create": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,

@@ -226,6 +226,28 @@ KVC_API int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
                     const void* h_k_new, const void* h_v_new, void* h_out,
                     const int32_t* d_block_tables, int bt_stride, float scale, void* stream);
 
+/* No counterpart in the reference.  kvc_decode for callers that cannot allocate
+ * device memory (runtimes that own every device allocation through their own
+ * arena, plugins that may not call cudaMalloc, code recorded by frameworks that
+ * forbid allocation).  The caller passes one layer's K and V pages (the pool's
+ * layout, e.g. kvc_pool_info's base + layer * bytes_per_layer), int32 block
+ * tables (query i uses row i), HOST context lengths, q and out; the plan and the
+ * split partials live in a fixed 16 MiB device array inside the library that
+ * every GPU loading it holds until the process exits.  No cudaMalloc / cudaFree
+ * or other allocating routine is called.  fp16/bf16 pages, head_dim in
+ * {32,64,96,128,160,192,256}, page_size a multiple of 16; at most 4096 queries,
+ * 16384 splits and 65536 work units, and the plan + partials must fit 16 MiB:
+ * larger requests fail with KVC_ERR_INVALID_ARG.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls share the array, so calls whose
+ * kernels overlap on the GPU (different streams, or devices... one array per
+ * device) race: serialise them on one stream per device. */
+KVC_API int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, int num_pages,
+                               int page_size, int num_kv_heads, int head_dim, int dtype,
+                               const int32_t* d_block_tables, int bt_stride,
+                               const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                               const void* d_q, void* d_out, float scale, void* stream);
+
 /* Copy positions [start, start+count) of block-table row `row` in `layer` into
  * device buffers (count, num_kv_heads, head_dim) on `stream`. */
 KVC_API int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_tables, int bt_stride,
