@@ -57,11 +57,11 @@ struct kvc_plan {
   int flags = 0;               // KVC_PLAN_*
   kvc::PoolGeom pool_geom;
   std::vector<int4> items, qinfo, item_pairs;
-  std::vector<int32_t> rows, positions, sched_off;
+  std::vector<int32_t> rows, positions;
   std::vector<int4> sched_recs;   // 3 per scheduled unit
   std::vector<int32_t> merge_queries;
-  int n_sched_ctas = 0;
-  kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters, d_sched_off,
+  int n_sched_ctas = 0, n_units = 0;
+  kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters, d_queue,
       d_sched_units, d_merge;
   kvc::HostBuf h_stage;
   cudaEvent_t upload_done = nullptr;
@@ -74,7 +74,7 @@ struct kvc_plan {
     d_part_o.release();
     d_part_ml.release();
     d_counters.release();
-    d_sched_off.release();
+    d_queue.release();
     d_sched_units.release();
     d_merge.release();
     h_stage.release();

@@ -409,11 +409,9 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
     p->item_pairs[2 * k] = p->items[k];
     p->item_pairs[2 * k + 1] = p->qinfo[p->items[k].x];
   }
-  // Persistent schedule: units (item x KV head x q-head chunk) onto warps of
-  // kPersistWarps-warp CTAs (one per SM), longest first onto the least-loaded
-  // warp, so every warp streams about the same number of positions.  Cost of
-  // a unit = its positions + a fixed per-unit overhead.  Each unit is stored as
-  // a self-contained 3 x int4 record in its warp's list.
+  // Persistent schedule: units (item x KV head x q-head chunk) stored longest
+  // first (items are sorted by length); the kernel hands them out dynamically.
+  // Each unit is a self-contained 3 x int4 record.
   {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -422,34 +420,17 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
     const int per_item = g.num_kv_heads * nhc;
     const int n_units = static_cast<int>(p->items.size()) * per_item;
     const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
-    const int n_bins = n_ctas * kPersistWarps;
-    std::vector<std::vector<int>> lists(n_bins);
-    using Load = std::pair<int64_t, int>;
-    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-    for (int b = 0; b < n_bins; ++b) heap.push({0, b});
-    for (int k = 0; k < static_cast<int>(p->items.size()); ++k) {
-      const int64_t cost = (p->items[k].w - p->items[k].z) + 64;
-      for (int r = 0; r < per_item; ++r) {
-        Load top = heap.top();
-        heap.pop();
-        lists[top.second].push_back(k * per_item + r);
-        heap.push({top.first + cost, top.second});
-      }
-    }
-    p->sched_off.assign(1, 0);
     p->sched_recs.clear();
-    for (auto& l : lists) {
-      for (int u : l) {
-        const int k = u / per_item;
-        const int kvh = (u / nhc) % g.num_kv_heads;
-        const int hc = u % nhc;
-        const int4 it = p->items[k];
+    for (int k = 0; k < static_cast<int>(p->items.size()); ++k) {
+      const int4 it = p->items[k];
+      for (int r = 0; r < per_item; ++r) {
+        const int kvh = r / nhc, hc = r % nhc;
         p->sched_recs.push_back(it);
         p->sched_recs.push_back(p->qinfo[it.x]);
         p->sched_recs.push_back(make_int4(kvh, hc, kvh * group + hc * 8, std::min(8, group - hc * 8)));
       }
-      p->sched_off.push_back(static_cast<int32_t>(p->sched_recs.size() / 3));
     }
+    p->n_units = n_units;
     p->n_sched_ctas = n_units > 0 ? n_ctas : 0;
     p->merge_queries.clear();
     for (int i = 0; i < n_queries; ++i)
@@ -490,10 +471,12 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
       return cuda_error(e, "cudaMemsetAsync(counters)");
   }
   // upload through pinned staging; wait for the previous upload to leave it
-  const size_t soff_b = (sizeof(int32_t) * p->sched_off.size() + 15) / 16 * 16;
+  const size_t soff_b = 0;
   const size_t sun_b = sizeof(int4) * std::max<size_t>(1, p->sched_recs.size());
-  if ((e = p->d_sched_off.ensure(soff_b)) || (e = p->d_sched_units.ensure(sun_b)))
+  if ((e = p->d_sched_units.ensure(sun_b)) || (e = p->d_queue.ensure(256)))
     return cuda_error(e, "plan schedule buffers");
+  // the unit counter starts at zero (the merge kernel re-arms it after each launch)
+  if ((e = cudaMemsetAsync(p->d_queue.ptr, 0, 256, s))) return cuda_error(e, "cudaMemsetAsync(queue)");
   const size_t mq_b = sizeof(int32_t) * std::max<size_t>(1, p->merge_queries.size());
   if ((e = p->d_merge.ensure(mq_b))) return cuda_error(e, "plan merge list");
   const size_t stage_b = items_b + qinfo_b + 2 * rows_b + soff_b + sun_b + mq_b;
@@ -509,7 +492,6 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   memcpy(h + items_b + qinfo_b, p->rows.data(), sizeof(int32_t) * n_queries);
   memcpy(h + items_b + qinfo_b + rows_b, p->positions.data(), sizeof(int32_t) * n_queries);
   uint8_t* hs = h + items_b + qinfo_b + 2 * rows_b;
-  memcpy(hs, p->sched_off.data(), sizeof(int32_t) * p->sched_off.size());
   if (!p->sched_recs.empty()) memcpy(hs + soff_b, p->sched_recs.data(), sizeof(int4) * p->sched_recs.size());
   uint8_t* hm = hs + soff_b + sun_b;
   if (!p->merge_queries.empty()) memcpy(hm, p->merge_queries.data(), sizeof(int32_t) * p->merge_queries.size());
@@ -517,7 +499,6 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
       (e = cudaMemcpyAsync(p->d_qinfo.ptr, h + items_b, sizeof(int4) * n_queries, cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(p->d_rows.ptr, h + items_b + qinfo_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(p->d_pos.ptr, h + items_b + qinfo_b + rows_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(p->d_sched_off.ptr, hs, soff_b, cudaMemcpyHostToDevice, s)) ||
       (!p->sched_recs.empty() &&
        (e = cudaMemcpyAsync(p->d_sched_units.ptr, hs + soff_b, sizeof(int4) * p->sched_recs.size(), cudaMemcpyHostToDevice, s))) ||
       (!p->merge_queries.empty() &&
@@ -564,8 +545,9 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.part_o = static_cast<float*>(plan->d_part_o.ptr);
   a.part_ml = static_cast<float2*>(plan->d_part_ml.ptr);
   a.counters = static_cast<unsigned*>(plan->d_counters.ptr);
-  a.sched_off = static_cast<const int32_t*>(plan->d_sched_off.ptr);
   a.sched_recs = static_cast<const int4*>(plan->d_sched_units.ptr);
+  a.n_units = plan->n_units;
+  a.queue = static_cast<unsigned*>(plan->d_queue.ptr);
   a.n_sched_ctas = plan->n_sched_ctas;
   a.early_prefetch = (plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0;
   a.merge_queries = static_cast<const int32_t*>(plan->d_merge.ptr);

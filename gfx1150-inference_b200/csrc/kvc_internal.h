@@ -121,12 +121,14 @@ struct DecodeArgs {
   // Only valid when every query has its own block-table row.
   const uint8_t* k_new;
   const uint8_t* v_new;
-  // Persistent schedule: warp w (= CTA * kPersistWarps + warp) processes unit
-  // records sched_recs[3 * (sched_off[w] .. sched_off[w+1]))], each 3 x int4:
+  // Persistent schedule: n_units unit records, longest first, each 3 x int4:
   // {query, split, first pos, end pos}, {bt row, ctx, split slot0, n_splits},
-  // {KV head, q-head chunk, first q-head, q-heads in chunk}.
-  const int32_t* sched_off;
+  // {KV head, q-head chunk, first q-head, q-heads in chunk}.  Warp w of the grid
+  // starts with unit w and takes further units from *queue (zero between
+  // launches; the merge kernel re-arms it).
   const int4* sched_recs;
+  int n_units;
+  unsigned int* queue;
   int n_sched_ctas;
   // Block tables and KV pages are not written by the kernel launched just before
   // (plan flag KVC_PLAN_KV_STABLE): the decode kernel may start streaming them

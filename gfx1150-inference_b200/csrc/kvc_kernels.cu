@@ -1,9 +1,13 @@
 // CUDA kernels of the B200 KV-cache decode path (sm_100a):
-//   append_kernel      fused, vectorised scatter of new K/V rows into the paged pool
-//   decode_mma_kernel  split-K flash-decoding GQA attention, 16-bit storage, tensor cores
-//   decode_simt_kernel split-K GQA attention on CUDA cores (fp32 storage, odd head dims)
-//   gather_kernel      pool -> token-major rows (bit-exact pool checks)
-//   fill_normal_kernel seeded N(0, s^2) synthetic pool contents
+//   append_kernel             fused, vectorised scatter of new K/V rows into the paged pool
+//   decode_persistent_kernel  split-K flash-decoding GQA attention, 16-bit storage: one
+//                             CTA per SM, warps streaming KV slabs through bulk-copy rings,
+//                             tensor-core math, the row append fused in
+//   merge_splits_kernel       merge of the split partials (programmatic dependent launch)
+//   decode_simt_kernel        split-K GQA attention on CUDA cores (fp32 storage, other
+//                             head dims), splits merged by the last CTA of a query
+//   gather_kernel             pool -> token-major rows (bit-exact pool checks)
+//   fill_normal_kernel        seeded N(0, s^2) synthetic pool contents
 //
 // The attention computes, for every query m and q-head h, exactly the quantity of
 // gfx1150-inference's gqa_online_softmax_kernel (src/kernels/attention.hip:35-123):
@@ -12,10 +16,10 @@
 //   out = sum_j softmax(score)_j * v_j over j < ctx        (attention.hip:75-113)
 //   out = 0 when nothing is attended                       (attention.hip:115)
 // with fp32 accumulation.  The work is organised the B200 way instead of one
-// wave per (m, h) scanning every position: each CTA owns one KV head of one
-// split of one query, streams that head's 16-position slabs once through shared
-// memory with bulk copies, and serves all q-heads of the group from the same
-// tile; splits are merged by the last CTA of a query to finish.
+// wave per (m, h) scanning every position: a query's context is cut into splits
+// of fixed length; each split of one KV head is streamed from HBM once, 16
+// positions at a time through shared memory, and serves all q-heads of the
+// group from the same tile; the splits' partial softmax states are then merged.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -307,316 +311,6 @@ __device__ void finish_split(const DecodeArgs& a, float* sm, int query, int kvh,
 }
 
 // =====================================================================================
-// Tensor-core split-K decode kernel (16-bit storage, head_dim multiple of 32).
-//
-// CTA = (split item, KV head, chunk of <= 8 q-heads); NW warps.  Warp w streams
-// slabs w, w+NW, ... of the split through its own NS-deep ring of shared-memory
-// stages (one bulk copy per K slab and per V slab, completion on an mbarrier).
-// Per 16-position slab and warp:
-//   S  = Q . K^T       mma m16n8k16: A = Q (rows = q-heads, zero-padded to 16),
-//                      B = K^T fragments by ldmatrix from the core-matrix layout
-//   online softmax on the S fragments (max over the 4 lanes of a row: 2 shuffles)
-//   O^T += V^T . P^T   mma m16n8k16: A = V^T by ldmatrix.trans, B = P^T taken
-//                      straight from the S accumulators (no shuffles)
-// so K and V of a KV head are read from HBM exactly once for all its q-heads.
-// =====================================================================================
-template <typename T, int D, int NW, int NS>
-__global__ void __launch_bounds__(NW * 32) decode_mma_kernel(const DecodeArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int SLAB_BYTES = kSlab * D * 2;     // one slab of K (or V)
-  constexpr int STAGE_BYTES = 2 * SLAB_BYTES;   // K slab + V slab
-  constexpr int KC = D / 16;                    // k-chunks of the QK product
-  constexpr int MT = D / 16;                    // m-tiles of the PV product
-  constexpr int U = D / 8;                      // 16-byte units per position
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gid = lane >> 2, tig = lane & 3;
-
-  int b = blockIdx.x;
-  const int hc = b % a.n_hchunk;
-  b /= a.n_hchunk;
-  const int kvh = b % a.num_kv_heads;
-  b /= a.num_kv_heads;
-  // Item record: {query, split, first pos, end pos}, {bt row, ctx, split slot, splits}.
-  const int4 it = a.items[2 * b];
-  const int4 qi = a.items[2 * b + 1];
-  const int query = it.x, split = it.y, tb = it.z, te = it.w;
-  const int hq0 = kvh * a.group + hc * 8;
-  const int nh = min(8, a.group - hc * 8);
-  const int ps = a.page_size;
-  const int slabs_per_page = ps / kSlab;
-
-  // Shared memory: [mbarriers (kBarBytes)] [NW x NS stages]; after the stream
-  // loop the stage region is reused for the warp combine and the split merge.
-  uint8_t* const region = smem + kBarBytes;
-  uint8_t* stages = region + warp * NS * STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * NS;
-  if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&bars[s]), 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-
-  // Q fragments: row gid of the A operand is q-head hq0 + gid (rows >= nh and the
-  // upper 8 rows are zero).
-  uint32_t qa[KC][2];
-  {
-    const T* qrow = reinterpret_cast<const T*>(a.q) +
-                    (static_cast<size_t>(query) * a.num_heads + hq0 + gid) * D;
-#pragma unroll
-    for (int kc = 0; kc < KC; ++kc) {
-      if (gid < nh) {
-        qa[kc][0] = *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * tig);
-        qa[kc][1] = *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 8 + 2 * tig);
-      } else {
-        qa[kc][0] = 0u;
-        qa[kc][1] = 0u;
-      }
-    }
-  }
-
-  const int sb0 = tb / kSlab;
-  const int sb1 = (te + kSlab - 1) / kSlab;
-  const int nslabs = (sb1 - sb0 > warp) ? (sb1 - sb0 - warp + NW - 1) / NW : 0;
-  const int32_t* bt_row = a.block_tables + static_cast<size_t>(qi.x) * a.bt_stride;
-  const size_t head_off = static_cast<size_t>(kvh) * ps * D * 2;
-  const size_t page_stride = static_cast<size_t>(a.num_kv_heads) * ps * D * 2;
-  const uint64_t policy = l2_policy_evict_first();
-
-  // The split's page ids, two per lane, read once (a split spans at most
-  // kMaxSplitPages pages).  Out-of-range entries become -1 and are reported;
-  // their slabs are skipped.
-  const int pg0 = tb / ps;
-  const int npages = (te + ps - 1) / ps - pg0;
-  int my_page0 = -1, my_page1 = -1;
-  if (lane < npages) {
-    const int v = bt_row[pg0 + lane];
-    my_page0 = (v >= 0 && v < a.num_pages) ? v : -1;
-    if (my_page0 < 0) report_error(1u, static_cast<uint32_t>(v));
-  }
-  if (lane + 32 < npages) {
-    const int v = bt_row[pg0 + lane + 32];
-    my_page1 = (v >= 0 && v < a.num_pages) ? v : -1;
-    if (my_page1 < 0) report_error(1u, static_cast<uint32_t>(v));
-  }
-  auto slab_page = [&](int j) -> int {  // all lanes (j is warp-uniform)
-    const int idx = j / slabs_per_page - pg0;
-    const int v0 = __shfl_sync(0xffffffffu, my_page0, idx & 31);
-    const int v1 = __shfl_sync(0xffffffffu, my_page1, idx & 31);
-    return idx < 32 ? v0 : v1;
-  };
-  auto issue = [&](int i, int phys) {  // lane 0 only
-    const int j = sb0 + warp + i * NW;
-    const int s = i % NS;
-    const uint32_t bar = smem_u32(&bars[s]);
-    if (phys < 0) {
-      mbar_arrive(bar);
-      return;
-    }
-    const size_t off = static_cast<size_t>(phys) * page_stride + head_off +
-                       static_cast<size_t>(j % slabs_per_page) * SLAB_BYTES;
-    mbar_arrive_expect_tx(bar, STAGE_BYTES);
-    const uint32_t dst = smem_u32(stages + s * STAGE_BYTES);
-    bulk_g2s(dst, a.k_layer + off, SLAB_BYTES, bar, policy);
-    bulk_g2s(dst + SLAB_BYTES, a.v_layer + off, SLAB_BYTES, bar, policy);
-  };
-
-  const int first = min(NS, nslabs);
-  for (int i = 0; i < first; ++i) {
-    const int phys = slab_page(sb0 + warp + i * NW);
-    if (lane == 0) issue(i, phys);
-  }
-  int issued = first;
-  __syncwarp();
-
-  // Fused append: this split holds the query's last position.
-  const int ctx = qi.y;
-  const bool owns_new = a.k_new != nullptr && ctx > 0 && te == ctx;
-  const int new_slab = (ctx - 1) / kSlab;
-  if (owns_new && hc == 0 && warp == 0)
-    append_row_to_pool(a, kLayoutCore, 2, query, kvh, ctx - 1, bt_row, lane);
-
-  float m_run = kNegBig, l_run = 0.f;
-  float o[MT][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-
-  int consumed = 0;
-  for (int i = 0; i < nslabs; ++i) {
-    const int s = i % NS;
-    const uint32_t parity = static_cast<uint32_t>(i / NS) & 1u;
-    const int j = sb0 + warp + i * NW;
-    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity);
-    if (__any_sync(0xffffffffu, !ok)) {
-      if (lane == 0) report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, static_cast<uint32_t>(j));
-      break;
-    }
-    consumed = i + 1;
-    uint8_t* st = stages + s * STAGE_BYTES;
-    const int valid = min(kSlab, te - j * kSlab);
-    if (slab_page(j) >= 0) {
-      if (valid < kSlab) {
-        // Positions past the context may hold anything (the pool is not zeroed):
-        // clear them so 0 * garbage never reaches the accumulators.
-        const int nunits = (kSlab - valid) * U;
-        for (int x = lane; x < 2 * nunits; x += 32) {
-          const int kv = x / nunits, r = x - kv * nunits;
-          const int t = valid + r / U, u = r - (r / U) * U;
-          *reinterpret_cast<uint4*>(st + kv * SLAB_BYTES + unit_offset(kLayoutCore, t, u, U) * 16) =
-              make_uint4(0, 0, 0, 0);
-        }
-        __syncwarp();
-      }
-      if (owns_new && j == new_slab) {
-        patch_slab_row(a, kLayoutCore, 2, st, SLAB_BYTES, query, kvh, (ctx - 1) - j * kSlab, lane,
-                       32);
-        __syncwarp();
-      }
-      const uint32_t kbase = smem_u32(st);
-      const uint32_t vbase = kbase + SLAB_BYTES;
-
-      // S = Q . K^T for the slab's two 8-position tiles.  Four independent
-      // accumulator chains (tile x even/odd k-chunk) instead of two serial
-      // ones, so consecutive mma.sync do not wait on each other.
-      float sc[2][2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int par = 0; par < 2; ++par)
-          sc[nt][par][0] = sc[nt][par][1] = sc[nt][par][2] = sc[nt][par][3] = 0.f;
-#pragma unroll
-      for (int k2 = 0; k2 < D / 32; ++k2) {
-        uint32_t r[2][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, r[nt][0],
-                  r[nt][1], r[nt][2], r[nt][3]);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          Mma<T>::run(sc[nt][0], qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, r[nt][0], r[nt][1]);
-          Mma<T>::run(sc[nt][1], qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, r[nt][2], r[nt][3]);
-        }
-      }
-      // V^T fragments of the first m-tiles, loaded before the softmax so their
-      // shared-memory latency overlaps the shuffles and exponentials.
-      constexpr int VPRE = MT < 8 ? MT : 8;
-      const int jm = lane >> 3;
-      uint32_t vf[VPRE][4];
-#pragma unroll
-      for (int mt = 0; mt < VPRE; ++mt)
-        ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, vf[mt][0],
-                  vf[mt][1], vf[mt][2], vf[mt][3]);
-
-      // Lane (gid, tig) holds scores of q-head gid for positions 2tig, 2tig+1,
-      // 8+2tig, 9+2tig of the slab.
-      const int t0 = 2 * tig;
-      const bool v0 = t0 < valid, v1 = t0 + 1 < valid, v2 = t0 + 8 < valid, v3 = t0 + 9 < valid;
-      const float x0 = (sc[0][0][0] + sc[0][1][0]) * a.scale_log2;
-      const float x1 = (sc[0][0][1] + sc[0][1][1]) * a.scale_log2;
-      const float x2 = (sc[1][0][0] + sc[1][1][0]) * a.scale_log2;
-      const float x3 = (sc[1][0][1] + sc[1][1][1]) * a.scale_log2;
-      float mx = fmaxf(fmaxf(v0 ? x0 : kNegBig, v1 ? x1 : kNegBig),
-                       fmaxf(v2 ? x2 : kNegBig, v3 ? x3 : kNegBig));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = fast_exp2(m_run - m_new);
-      const float p0 = v0 ? fast_exp2(x0 - m_new) : 0.f;
-      const float p1 = v1 ? fast_exp2(x1 - m_new) : 0.f;
-      const float p2 = v2 ? fast_exp2(x2 - m_new) : 0.f;
-      const float p3 = v3 ? fast_exp2(x3 - m_new) : 0.f;
-      l_run = l_run * alpha + ((p0 + p1) + (p2 + p3));
-      m_run = m_new;
-      const uint32_t pb0 = Mma<T>::pack(p0, p1);
-      const uint32_t pb1 = Mma<T>::pack(p2, p3);
-      // Columns 2tig, 2tig+1 of O^T belong to q-heads 2tig, 2tig+1, whose alpha
-      // lives in lanes (2tig)*4 and (2tig+1)*4.
-      const float a_lo = __shfl_sync(0xffffffffu, alpha, (2 * tig) * 4);
-      const float a_hi = __shfl_sync(0xffffffffu, alpha, (2 * tig + 1) * 4);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        o[mt][0] *= a_lo;
-        o[mt][1] *= a_hi;
-        o[mt][2] *= a_lo;
-        o[mt][3] *= a_hi;
-        if (mt < VPRE) {
-          Mma<T>::run(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], pb0, pb1);
-        } else {
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, r0, r1,
-                    r2, r3);
-          Mma<T>::run(o[mt], r0, r1, r2, r3, pb0, pb1);
-        }
-      }
-    }
-    __syncwarp();
-    if (i + NS < nslabs) {
-      const int phys = slab_page(sb0 + warp + (i + NS) * NW);
-      if (lane == 0) {
-        fence_proxy_async();
-        issue(i + NS, phys);
-      }
-      issued = i + NS + 1;
-    }
-  }
-  // Error path only: wait (bounded) for copies still in flight into this warp's
-  // stages before the shared memory is reused.
-  for (int i = consumed; i < issued; ++i)
-    (void)mbar_wait_bounded(smem_u32(&bars[i % NS]), static_cast<uint32_t>(i / NS) & 1u);
-
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-
-  // ---- combine the NW warps of the CTA (stage memory is free now) ----
-  __syncthreads();
-  constexpr int OS = D + 4;
-  float* wm = reinterpret_cast<float*>(region);   // [NW][8]
-  float* wl = wm + NW * 8;                      // [NW][8]
-  float* wo = wl + NW * 8;                      // [NW][8][OS]
-  if (tig == 0) {
-    wm[warp * 8 + gid] = m_run;
-    wl[warp * 8 + gid] = l_run;
-  }
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    wo[(warp * 8 + 2 * tig) * OS + 16 * mt + gid] = o[mt][0];
-    wo[(warp * 8 + 2 * tig + 1) * OS + 16 * mt + gid] = o[mt][1];
-    wo[(warp * 8 + 2 * tig) * OS + 16 * mt + gid + 8] = o[mt][2];
-    wo[(warp * 8 + 2 * tig + 1) * OS + 16 * mt + gid + 8] = o[mt][3];
-  }
-  __syncthreads();
-
-  const int n_splits = qi.w;
-  const int H = a.num_heads;
-  for (int idx = threadIdx.x; idx < nh * D; idx += NW * 32) {
-    const int h = idx / D, d = idx - (idx / D) * D;
-    float M = kNegBig;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * 8 + h]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float f = fast_exp2(wm[w * 8 + h] - M);
-      L += wl[w * 8 + h] * f;
-      O += wo[(w * 8 + h) * OS + d] * f;
-    }
-    if (n_splits == 1) {
-      reinterpret_cast<T*>(a.out)[(static_cast<size_t>(query) * H + hq0 + h) * D + d] =
-          from_f32<T>(L > 0.f ? O * (1.0f / L) : 0.f);
-    } else {
-      const size_t slot = static_cast<size_t>(qi.z + split) * H + hq0 + h;
-      a.part_o[slot * D + d] = O;
-      if (d == 0) a.part_ml[slot] = make_float2(M, L);
-    }
-  }
-  if (n_splits > 1) {
-    __syncthreads();  // the merge reuses the combine buffers
-    finish_split<T>(a, reinterpret_cast<float*>(region), query, kvh, hc, qi.z, n_splits, hq0, nh);
-  }
-}
-
-// =====================================================================================
 // Persistent tensor-core decode kernel (16-bit storage, head_dim multiple of 32).
 //
 // One CTA of NW warps per SM; every warp is an independent streaming engine.
@@ -671,8 +365,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
   __syncwarp();
 
   const int gw = blockIdx.x * NW + warp;
-  const int ub = a.sched_off[gw];
-  const int ue = a.sched_off[gw + 1];
+  const int W = gridDim.x * NW;
+  const int n_units = a.n_units;
   const size_t page_stride = static_cast<size_t>(a.num_kv_heads) * ps * D * 2;
   const uint64_t policy = l2_policy_evict_first();
 
@@ -696,17 +390,21 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
   };
 
   // ---------------- producer ----------------
-  // p_*: the unit being issued.  n_*: the next unit of the list, fetched while
-  // the current one streams (its record when the current unit's first slab is
-  // issued, its page ids one slab later), so unit switches never wait on memory.
-  // pq: Q fragments of the unit the producer started last, taken over by the
-  // consumer when it reaches that unit.
-  int p_pos = ub;
+  // Units are stored longest first.  Warp gw starts with unit gw and then takes
+  // the next free one from a global counter (dynamic list scheduling, so every
+  // SM keeps streaming until the whole list is done).  p_*: the unit being
+  // issued.  n_*: the next unit, fetched while the current one streams, one
+  // step per issued slab (counter ticket, then its record, then its page ids),
+  // so unit switches never wait on memory.  pq: Q fragments of the unit the
+  // producer started last, taken over by the consumer when it reaches it.
+  int p_pos = gw;
   int4 p_r0 = make_int4(0, 0, 0, 0), p_r1 = p_r0, p_r2 = p_r0;
   int p_j = 0, p_end = 0, p_pg0 = 0, p_page0 = -1, p_page1 = -1;
   int4 n_r0 = p_r0, n_r1 = p_r0, n_r2 = p_r0;
   int n_pg0 = 0, n_page0 = -1, n_page1 = -1;
-  int n_state = 0;  // 0: nothing fetched, 1: record fetched, 2: record and page ids fetched
+  int n_state = 0;  // 0: nothing, 1: ticket taken, 2: record fetched, 3: page ids fetched, 4: none left
+  int n_pos = -1;
+  unsigned n_ticket = 0;
   uint32_t pq[KC][2];
   int pq_pos = -1;
   auto load_q = [&](const int4& r0, const int4& r2, uint32_t (&q)[KC][2]) {
@@ -717,17 +415,26 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
       q[kc][1] = gid < r2.w ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 8 + 2 * tig) : 0u;
     }
   };
-  auto fetch_next_record = [&]() {
-    if (p_pos + 1 >= ue) return;
-    const int4* rec = a.sched_recs + static_cast<size_t>(p_pos + 1) * 3;
-    n_r0 = rec[0];
-    n_r1 = rec[1];
-    n_r2 = rec[2];
-    n_state = 1;
-  };
-  auto fetch_next_pages = [&]() {
-    load_pages(n_r0, n_r1, n_pg0, n_page0, n_page1);
-    n_state = 2;
+  // One step of the background fetch of the next unit.
+  auto next_step = [&]() {
+    if (n_state == 0) {
+      if (lane == 0) n_ticket = atomicAdd(a.queue, 1u);  // used one step later
+      n_state = 1;
+    } else if (n_state == 1) {
+      n_pos = W + static_cast<int>(__shfl_sync(0xffffffffu, n_ticket, 0));
+      if (n_pos >= n_units) {
+        n_state = 4;
+        return;
+      }
+      const int4* rec = a.sched_recs + static_cast<size_t>(n_pos) * 3;
+      n_r0 = rec[0];
+      n_r1 = rec[1];
+      n_r2 = rec[2];
+      n_state = 2;
+    } else if (n_state == 2) {
+      load_pages(n_r0, n_r1, n_pg0, n_page0, n_page1);
+      n_state = 3;
+    }
   };
   bool dep_ready = false;  // the preceding kernel's results are visible (griddepcontrol.wait)
   auto start_unit = [&]() {
@@ -743,7 +450,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
       pq_pos = -1;
     }
   };
-  if (p_pos < ue) {
+  if (p_pos < n_units) {
     const int4* rec = a.sched_recs + static_cast<size_t>(p_pos) * 3;
     p_r0 = rec[0];
     p_r1 = rec[1];
@@ -754,13 +461,13 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
   int issued = 0;
   auto p_issue = [&]() {  // all lanes; lane 0 issues the bulk copies
     while (p_j >= p_end) {  // current unit fully issued: move to the next one
-      if (p_pos + 1 >= ue) {
-        p_pos = ue;
+      if (p_pos >= n_units) return;
+      while (n_state < 3) next_step();
+      if (n_state == 4) {
+        p_pos = n_units;
         return;
       }
-      if (n_state == 0) fetch_next_record();
-      if (n_state == 1) fetch_next_pages();
-      ++p_pos;
+      p_pos = n_pos;
       p_r0 = n_r0;
       p_r1 = n_r1;
       p_r2 = n_r2;
@@ -796,8 +503,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     }
     ++p_j;
     ++issued;
-    if (n_state == 0) fetch_next_record();
-    else if (n_state == 1) fetch_next_pages();
+    next_step();
   };
   // Prologue: fill the ring.  Before griddepcontrol.wait only the plan, the
   // block tables and KV pages are read, and only when the caller declared them
@@ -1049,8 +755,16 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
 template <typename T, int EPL>
 __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The decode grid has finished: re-arm its unit counter for the next launch,
+  // visibly to the whole device before the next launch may start.
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    *a.queue = 0u;
+    __threadfence();
+  }
+  __syncthreads();
   // the next decode launch may start filling its ring while the merge runs
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (a.n_merge_queries == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + warp;
   if (h >= a.num_heads) return;
@@ -1305,39 +1019,6 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
 // =====================================================================================
 namespace {
 
-template <typename T, int D, int NW, int NS>
-cudaError_t run_mma_cfg(const DecodeArgs& a, cudaStream_t s) {
-  constexpr size_t stage_region = static_cast<size_t>(NW) * NS * 2 * kSlab * D * 2;
-  const size_t combine = (2 * NW * 8 + static_cast<size_t>(NW) * 8 * (D + 4)) * sizeof(float);
-  const size_t merge = (8 * kMergeChunk + 8 * static_cast<size_t>(D) + 16) * sizeof(float);
-  static_assert(NW * NS * sizeof(uint64_t) <= kBarBytes, "mbarrier block too small");
-  size_t smem = stage_region;
-  if (combine > smem) smem = combine;
-  if (merge > smem) smem = merge;
-  smem += kBarBytes;
-  auto kern = decode_mma_kernel<T, D, NW, NS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  const unsigned grid = static_cast<unsigned>(a.n_items) * a.num_kv_heads * a.n_hchunk;
-  kern<<<grid, NW * 32, smem, s>>>(a);
-  return cudaGetLastError();
-}
-
-// Tuning knob for head_dim 128: KVC_DECODE_VARIANT="<warps>x<stages>" picks one of
-// the compiled (warps per CTA, stages per warp) shapes; default 4x3.
-int decode_variant_128() {
-  static int v = [] {
-    const char* e = getenv("KVC_DECODE_VARIANT");
-    if (!e) return 43;
-    if (strncmp(e, "legacy", 6) == 0) e += 6;
-    int nw = 0, ns = 0;
-    if (sscanf(e, "%dx%d", &nw, &ns) != 2) return 43;
-    return nw * 10 + ns;
-  }();
-  return v;
-}
-
 template <typename T, int D, int NW>
 cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   constexpr int NS = persist_stages<D>();
@@ -1363,10 +1044,11 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
     cfg.numAttrs = 1;
     if ((e = cudaLaunchKernelEx(&cfg, kern, a)) != cudaSuccess) return e;
   }
-  if (a.n_merge_queries <= 0) return cudaSuccess;
-  // merge as a programmatic dependent launch: scheduled while the decode grid drains
+  // merge (and counter re-arm) as a programmatic dependent launch: scheduled while
+  // the decode grid drains
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(a.n_merge_queries), (a.num_heads + 3) / 4, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(a.n_merge_queries > 0 ? a.n_merge_queries : 1),
+                     a.n_merge_queries > 0 ? (a.num_heads + 3) / 4 : 1, 1);
   cfg.blockDim = dim3(128, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
@@ -1375,31 +1057,9 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   return cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a);
 }
 
-bool use_legacy_decode() {
-  static bool v = [] {
-    const char* e = getenv("KVC_DECODE_VARIANT");
-    return e != nullptr && strncmp(e, "legacy", 6) == 0;
-  }();
-  return v;
-}
-
 template <typename T, int D>
 cudaError_t run_mma(const DecodeArgs& a, cudaStream_t s) {
-  if (!use_legacy_decode() && a.sched_off != nullptr) return run_persistent<T, D, kPersistWarps>(a, s);
-  if constexpr (D == 128) {
-    switch (decode_variant_128()) {
-      case 42: return run_mma_cfg<T, D, 4, 2>(a, s);
-      case 45: return run_mma_cfg<T, D, 4, 5>(a, s);
-      case 23: return run_mma_cfg<T, D, 2, 3>(a, s);
-      case 24: return run_mma_cfg<T, D, 2, 4>(a, s);
-      case 26: return run_mma_cfg<T, D, 2, 6>(a, s);
-      case 82: return run_mma_cfg<T, D, 8, 2>(a, s);
-      case 83: return run_mma_cfg<T, D, 8, 3>(a, s);
-      default: return run_mma_cfg<T, D, 4, 3>(a, s);
-    }
-  } else {
-    return run_mma_cfg<T, D, 4, (D <= 128 ? 3 : 2)>(a, s);
-  }
+  return run_persistent<T, D, kPersistWarps>(a, s);
 }
 
 template <typename T, int EPL>
@@ -1488,7 +1148,6 @@ constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
 constexpr int kNoAllocMaxQueries = 4096;
 constexpr int kNoAllocMaxItems = 16384;
 constexpr int kNoAllocMaxUnits = 65536;
-constexpr int kNoAllocMaxBins = 2048;
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -1500,40 +1159,11 @@ uint8_t* g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
 int4 h_items[kNoAllocMaxItems];
 int4 h_qinfo[kNoAllocMaxQueries];
 int4 h_recs[3 * kNoAllocMaxUnits];
-int32_t h_sched_off[kNoAllocMaxBins + 1];
 int32_t h_merge[kNoAllocMaxQueries];
-int32_t h_unit_bin[kNoAllocMaxUnits];
-int32_t h_bin_fill[kNoAllocMaxBins];
-int64_t h_heap_load[kNoAllocMaxBins];
-int32_t h_heap_bin[kNoAllocMaxBins];
 int32_t h_order[kNoAllocMaxItems];
+int4 h_item_pairs[2 * kNoAllocMaxItems];
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
-
-// Fixed-capacity binary min-heap of (load, bin) pairs (ties: lower bin first).
-bool heap_less(int i, int j) {
-  return h_heap_load[i] < h_heap_load[j] ||
-         (h_heap_load[i] == h_heap_load[j] && h_heap_bin[i] < h_heap_bin[j]);
-}
-void heap_swap(int i, int j) {
-  const int64_t l = h_heap_load[i];
-  h_heap_load[i] = h_heap_load[j];
-  h_heap_load[j] = l;
-  const int32_t b = h_heap_bin[i];
-  h_heap_bin[i] = h_heap_bin[j];
-  h_heap_bin[j] = b;
-}
-void heap_sift_down(int i, int n) {
-  for (;;) {
-    int m = i;
-    const int l = 2 * i + 1, r = 2 * i + 2;
-    if (l < n && heap_less(l, m)) m = l;
-    if (r < n && heap_less(r, m)) m = r;
-    if (m == i) return;
-    heap_swap(i, m);
-    i = m;
-  }
-}
 
 }  // namespace
 
@@ -1613,17 +1243,14 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
 
   // ---- scratch layout and size check ----
   const size_t H = static_cast<size_t>(num_heads);
-  const size_t off_items = 0;
+  const size_t off_queue = 0;
+  const size_t off_items = 256;
   const size_t off_qinfo = align256(off_items + sizeof(int4) * 2 * n_items);
   const size_t off_recs = align256(off_qinfo + sizeof(int4) * n_queries);
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
-  const int n_bins = n_ctas * kPersistWarps;
-  if (n_bins > kNoAllocMaxBins)
-    return set_error(KVC_ERR_INVALID_ARG, "too many SMs for kvc_decode_noalloc's schedule table.");
-  const size_t off_soff = align256(off_recs + sizeof(int4) * 3 * n_units);
-  const size_t off_merge = align256(off_soff + sizeof(int32_t) * (n_bins + 1));
+  const size_t off_merge = align256(off_recs + sizeof(int4) * 3 * n_units);
   const size_t plan_bytes = align256(off_merge + sizeof(int32_t) * n_queries);
   const size_t off_part_ml = plan_bytes;
   const size_t off_part_o = align256(off_part_ml + sizeof(float2) * slot * H);
@@ -1634,56 +1261,35 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
                      "scratch holds %zu bytes (use kvc_decode for larger batches).",
                      need, kNoAllocScratchBytes);
 
-  // ---- schedule: units onto warps, longest first onto the least-loaded warp ----
-  for (int b = 0; b < n_bins; ++b) {
-    h_heap_load[b] = 0;
-    h_heap_bin[b] = b;
-    h_bin_fill[b] = 0;
-  }
-  for (int r = 0; r < n_units; ++r) {
-    const int k = h_order[r / per_item];
-    const int64_t cost = (h_items[k].w - h_items[k].z) + 64;
-    h_unit_bin[r] = h_heap_bin[0];
-    h_bin_fill[h_heap_bin[0]]++;
-    h_heap_load[0] += cost;
-    heap_sift_down(0, n_bins);
-  }
-  h_sched_off[0] = 0;
-  for (int b = 0; b < n_bins; ++b) h_sched_off[b + 1] = h_sched_off[b] + h_bin_fill[b];
-  for (int b = 0; b < n_bins; ++b) h_bin_fill[b] = h_sched_off[b];
-  int4* recs = h_recs;
+  // ---- units, longest first (the kernel hands them out dynamically) ----
   for (int r = 0; r < n_units; ++r) {
     const int k = h_order[r / per_item];
     const int u = r % per_item;
     const int kvh = u / nhc, hc = u % nhc;
     const int4 it = h_items[k];
-    const int pos = h_bin_fill[h_unit_bin[r]]++;
-    recs[3 * pos + 0] = it;
-    recs[3 * pos + 1] = make_int4(0, h_qinfo[it.x].y, h_qinfo[it.x].z, h_qinfo[it.x].w);
-    recs[3 * pos + 1].x = it.x;  // block-table row of query i is row i
-    recs[3 * pos + 2] = make_int4(kvh, hc, kvh * group + hc * 8, std::min(8, group - hc * 8));
+    h_recs[3 * r + 0] = it;
+    h_recs[3 * r + 1] = h_qinfo[it.x];  // {bt row = query, ctx, slot0, n_splits}
+    h_recs[3 * r + 2] = make_int4(kvh, hc, kvh * group + hc * 8, std::min(8, group - hc * 8));
   }
   int n_merge = 0;
   for (int i = 0; i < n_queries; ++i)
     if (h_qinfo[i].w > 1) h_merge[n_merge++] = i;
-  // items are stored as {split, query record} pairs like kvc_plan_decode's
-  static int4 h_item_pairs[2 * kNoAllocMaxItems];
   for (int k = 0; k < n_items; ++k) {
     h_item_pairs[2 * k] = h_items[h_order[k]];
     h_item_pairs[2 * k + 1] = h_qinfo[h_items[h_order[k]].x];
   }
-  for (int i = 0; i < n_queries; ++i) h_qinfo[i].x = i;
 
   // ---- upload (pageable host source: the call returns once it is staged) ----
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* base = g_noalloc_dev_ptr[dev];
+  // the unit counter starts at zero (this call's merge kernel re-arms it too)
+  if ((e = cudaMemsetAsync(base + off_queue, 0, 256, s)))
+    return cuda_error(e, "kvc_decode_noalloc counter reset");
   if ((e = cudaMemcpyAsync(base + off_items, h_item_pairs, sizeof(int4) * 2 * n_items,
                            cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(base + off_qinfo, h_qinfo, sizeof(int4) * n_queries,
                            cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(base + off_recs, h_recs, sizeof(int4) * 3 * n_units,
-                           cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(base + off_soff, h_sched_off, sizeof(int32_t) * (n_bins + 1),
                            cudaMemcpyHostToDevice, s)) ||
       (n_merge > 0 && (e = cudaMemcpyAsync(base + off_merge, h_merge, sizeof(int32_t) * n_merge,
                                            cudaMemcpyHostToDevice, s))))
@@ -1701,8 +1307,9 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   a.part_o = reinterpret_cast<float*>(base + off_part_o);
   a.part_ml = reinterpret_cast<float2*>(base + off_part_ml);
   a.counters = nullptr;  // not used by the tensor-core path
-  a.sched_off = reinterpret_cast<const int32_t*>(base + off_soff);
   a.sched_recs = reinterpret_cast<const int4*>(base + off_recs);
+  a.n_units = n_units;
+  a.queue = reinterpret_cast<unsigned*>(base + off_queue);
   a.n_sched_ctas = n_units > 0 ? n_ctas : 0;
   a.early_prefetch = 0;
   a.merge_queries = reinterpret_cast<const int32_t*>(base + off_merge);

@@ -239,9 +239,11 @@ KVC_API int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
  * 16384 splits and 65536 work units, and the plan + partials must fit 16 MiB:
  * larger requests fail with KVC_ERR_INVALID_ARG.  The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress); make that first
- * call before any stream capture.  All calls share the array, so calls whose
- * kernels overlap on the GPU (different streams, or devices... one array per
- * device) race: serialise them on one stream per device. */
+ * call before any stream capture.  All calls on a device share its array, and
+ * each call overwrites it, so calls whose kernels overlap on that GPU (for
+ * example on two streams) race: serialise them on one stream.  The plan is
+ * staged through pageable host memory, so a call first waits for the work
+ * already queued on its stream. */
 KVC_API int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, int num_pages,
                                int page_size, int num_kv_heads, int head_dim, int dtype,
                                const int32_t* d_block_tables, int bt_stride,
