@@ -98,6 +98,9 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
 int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                        const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
                        int bt_stride, float scale, cudaStream_t s);
+// Split length (positions) for a batch: see kvc_host.cpp.
+int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
+                        int device);
 // Plan for q_len queries m = 0..q_len-1 of one sequence (block-table row 0)
 // whose context is min(kv_len, start_pos + m + 1) if causal, else kv_len
 // (attention.hip:75).

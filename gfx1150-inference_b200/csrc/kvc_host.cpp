@@ -355,20 +355,43 @@ extern "C" int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_ta
 // ============================================================================
 namespace kvc {
 
-// Positions per split: kSplitTokens rounded up to whole pages.  KVC_SPLIT_TOKENS
-// overrides it for tuning (changes the summation order, so results may differ
-// in the last bits between settings; every mode of one setting still agrees).
+// Positions per split, rounded up to whole pages.  A batch whose 512-position
+// splits already give every warp of the persistent grid at least one unit uses
+// them; a smaller batch (e.g. one sequence) uses 128-position splits so the
+// whole GPU streams.  The choice depends only on the context lengths and head
+// counts of the batch, so the same call always gets the same partition (the
+// resident and offloaded paths agree bit for bit).  KVC_SPLIT_TOKENS overrides
+// it for tuning.
 int split_tokens_for(int page_size) {
   static int base = [] {
     const char* e = getenv("KVC_SPLIT_TOKENS");
-    int v = e ? atoi(e) : kSplitTokens;
-    if (v < kSlab) v = kSlab;
+    int v = e ? atoi(e) : 0;
+    if (v < 0) v = 0;
+    if (v > 0 && v < kSlab) v = kSlab;
     return v;
   }();
-  int c = ((base + page_size - 1) / page_size) * page_size;
+  return base;  // 0: automatic
+}
+
+int round_split(int c, int page_size) {
+  c = ((c + page_size - 1) / page_size) * page_size;
   while (c / page_size > kMaxSplitPages) c -= page_size;
   if (c > kMaxSplitPages * kSlab) c = (kMaxSplitPages * kSlab / page_size) * page_size;
   return c < page_size ? page_size : c;
+}
+
+int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
+                        int device) {
+  const int forced = split_tokens_for(page_size);
+  if (forced > 0) return round_split(forced, page_size);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int64_t warps = static_cast<int64_t>(sms) * kPersistWarps;
+  const int big = round_split(kSplitTokens, page_size);
+  int64_t units = 0;
+  for (int i = 0; i < n_queries; ++i)
+    units += (ctx[i] > 0 ? (ctx[i] + big - 1) / big : 1) * static_cast<int64_t>(units_per_split);
+  return units >= warps ? big : round_split(kSplitTokensSmall, page_size);
 }
 
 // Build the split list on the host.  ctx_of(i) / row_of(i) describe query i.
@@ -378,14 +401,18 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   if (n_queries < 0) return set_error(KVC_ERR_INVALID_ARG, "n_queries must be non-negative.");
   if (num_heads <= 0 || num_heads % g.num_kv_heads != 0)
     return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
-  const int C = split_tokens_for(g.page_size);
+  std::vector<int> ctxs(std::max(0, n_queries));
+  for (int i = 0; i < n_queries; ++i) ctxs[i] = ctx_of(i);
+  const int C = choose_split_tokens(g.page_size, ctxs.data(), n_queries,
+                                    g.num_kv_heads * ((num_heads / g.num_kv_heads + 7) / 8),
+                                    device);
   p->items.clear();
   p->qinfo.clear();
   p->rows.clear();
   p->positions.clear();
   int slot = 0, max_ctx = 0;
   for (int i = 0; i < n_queries; ++i) {
-    const int ctx = ctx_of(i);
+    const int ctx = ctxs[i];
     const int row = row_of(i);
     if (ctx < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
     if (row < 0) return set_error(KVC_ERR_INVALID_ARG, "block-table row must be non-negative.");

@@ -45,6 +45,8 @@ __host__ __device__ __forceinline__ size_t unit_offset(int layout, int t, int u,
 // only on the context length, never on the storage mode, batch composition or
 // GPU count, so resident, offloaded and sharded runs add in the same order.
 constexpr int kSplitTokens = 512;
+// Split length for batches too small to give every warp a 512-position unit.
+constexpr int kSplitTokensSmall = 128;
 // Upper bound on pages per split the kernels accept (split tokens are capped at
 // kMaxSplitPages * 16).
 constexpr int kMaxSplitPages = 64;

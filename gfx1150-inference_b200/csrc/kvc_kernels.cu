@@ -405,9 +405,10 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
   int n_state = 0;  // 0: nothing, 1: ticket taken, 2: record fetched, 3: page ids fetched, 4: none left
   int n_pos = -1;
   unsigned n_ticket = 0;
-  uint32_t pq[KC][2];
+  constexpr bool kPrefetchQ = D <= 128;  // registers allow a second set of Q fragments
+  uint32_t pq[kPrefetchQ ? KC : 1][2];
   int pq_pos = -1;
-  auto load_q = [&](const int4& r0, const int4& r2, uint32_t (&q)[KC][2]) {
+  auto load_q = [&](const int4& r0, const int4& r2, auto& q) {
     const T* qrow = reinterpret_cast<const T*>(a.q) + (static_cast<size_t>(r0.x) * H + r2.z + gid) * D;
 #pragma unroll
     for (int kc = 0; kc < KC; ++kc) {
@@ -443,11 +444,13 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     // An empty context still gets one slab without data, so the consumer
     // finalizes the unit and writes its zero row (attention.hip:115).
     if (p_end <= p_j) p_end = p_j + 1;
-    if (dep_ready) {  // q may come from the preceding kernel
-      load_q(p_r0, p_r2, pq);
-      pq_pos = p_pos;
-    } else {
-      pq_pos = -1;
+    if constexpr (kPrefetchQ) {
+      if (dep_ready) {  // q may come from the preceding kernel
+        load_q(p_r0, p_r2, pq);
+        pq_pos = p_pos;
+      } else {
+        pq_pos = -1;
+      }
     }
   };
   if (p_pos < n_units) {
@@ -594,15 +597,18 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
       c_r0 = meta[s * 4 + 0];
       c_r1 = meta[s * 4 + 1];
       c_r2 = meta[s * 4 + 2];
-      if (pq_pos == cur) {
+      bool have_q = false;
+      if constexpr (kPrefetchQ) {
+        if (pq_pos == cur) {
 #pragma unroll
-        for (int kc = 0; kc < KC; ++kc) {
-          qa[kc][0] = pq[kc][0];
-          qa[kc][1] = pq[kc][1];
+          for (int kc = 0; kc < KC; ++kc) {
+            qa[kc][0] = pq[kc][0];
+            qa[kc][1] = pq[kc][1];
+          }
+          have_q = true;
         }
-      } else {
-        load_q(c_r0, c_r2, qa);
       }
+      if (!have_q) load_q(c_r0, c_r2, qa);
       m_run = kNegBig;
       l_run = 0.f;
 #pragma unroll
@@ -640,7 +646,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     }
     // K and V fragments of the slab (all of them when registers allow, so the
     // stage can be refilled before the math; otherwise K first, V after S).
-    uint32_t kf[K2][2][4];
+    constexpr int KF = kAllFragsFirst ? K2 : 1;
+    uint32_t kf[KF][2][4];
     uint32_t vf[kAllFragsFirst ? MT : 1][4];
     float sc[2][2][4];
 #pragma unroll
@@ -649,56 +656,59 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
       for (int par = 0; par < 2; ++par)
         sc[nt][par][0] = sc[nt][par][1] = sc[nt][par][2] = sc[nt][par][3] = 0.f;
     if (have) {
-#pragma unroll
-      for (int k2 = 0; k2 < K2; ++k2)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, kf[k2][nt][0],
-                  kf[k2][nt][1], kf[k2][nt][2], kf[k2][nt][3]);
       if constexpr (kAllFragsFirst) {
+#pragma unroll
+        for (int k2 = 0; k2 < K2; ++k2)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+            ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, kf[k2][nt][0],
+                    kf[k2][nt][1], kf[k2][nt][2], kf[k2][nt][3]);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
           ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, vf[mt][0],
                     vf[mt][1], vf[mt][2], vf[mt][3]);
       }
 #pragma unroll
-      for (int k2 = 0; k2 < K2; ++k2)
+      for (int k2 = 0; k2 < K2; ++k2) {
+        const int kk = kAllFragsFirst ? k2 : 0;
+        if constexpr (!kAllFragsFirst) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+            ldsm_x4(kbase + ((nt * U + k2 * 4 + (lane >> 3)) * 8 + (lane & 7)) * 16, kf[0][nt][0],
+                    kf[0][nt][1], kf[0][nt][2], kf[0][nt][3]);
+        }
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-          Mma<T>::run(sc[nt][0], qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, kf[k2][nt][0], kf[k2][nt][1]);
-          Mma<T>::run(sc[nt][1], qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, kf[k2][nt][2],
-                      kf[k2][nt][3]);
+          Mma<T>::run(sc[nt][0], qa[2 * k2][0], 0u, qa[2 * k2][1], 0u, kf[kk][nt][0], kf[kk][nt][1]);
+          Mma<T>::run(sc[nt][1], qa[2 * k2 + 1][0], 0u, qa[2 * k2 + 1][1], 0u, kf[kk][nt][2],
+                      kf[kk][nt][3]);
         }
-    }
-    uint32_t vlate[kAllFragsFirst ? 1 : MT][4];
-    if constexpr (!kAllFragsFirst) {
-      if (have) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-          ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16,
-                    vlate[mt][0], vlate[mt][1], vlate[mt][2], vlate[mt][3]);
       }
     }
-    // Every fragment has landed in registers (the XOR reads one register of
-    // each ldmatrix, so it waits for all of them): the stage can be refilled.
-    {
+    if constexpr (kAllFragsFirst) {
+      // Every fragment has landed in registers (the XOR reads one register of
+      // each ldmatrix, so it waits for all of them): the stage can be refilled
+      // before the math.
       uint32_t dep = 0;
       if (have) {
-        if constexpr (kAllFragsFirst) {
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) dep ^= vf[mt][0];
-        } else {
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) dep ^= vlate[mt][0];
-        }
+        for (int mt = 0; mt < MT; ++mt) dep ^= vf[mt][0];
       }
       asm volatile("" ::"r"(dep));
+      __syncwarp();
+      ++consumed;
+      if (lane == 0) fence_proxy_async();
+      p_issue();
     }
-    __syncwarp();
-    ++consumed;
-    if (lane == 0) fence_proxy_async();
-    p_issue();
-    if (!have) continue;
+    if (!have) {
+      if constexpr (!kAllFragsFirst) {
+        __syncwarp();
+        ++consumed;
+        if (lane == 0) fence_proxy_async();
+        p_issue();
+      }
+      continue;
+    }
 
     const int t0 = 2 * tig;
     const bool v0 = t0 < valid, v1 = t0 + 1 < valid, v2 = t0 + 8 < valid, v3 = t0 + 9 < valid;
@@ -731,8 +741,17 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
       if constexpr (kAllFragsFirst) {
         Mma<T>::run(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], pb0, pb1);
       } else {
-        Mma<T>::run(o[mt], vlate[mt][0], vlate[mt][1], vlate[mt][2], vlate[mt][3], pb0, pb1);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vbase + (((jm >> 1) * U + 2 * mt + (jm & 1)) * 8 + (lane & 7)) * 16, r0, r1, r2,
+                  r3);
+        Mma<T>::run(o[mt], r0, r1, r2, r3, pb0, pb1);
       }
+    }
+    if constexpr (!kAllFragsFirst) {  // the stage is released after the math
+      __syncwarp();
+      ++consumed;
+      if (lane == 0) fence_proxy_async();
+      p_issue();
     }
   }
   if (cur >= 0 && !dead) finalize();
@@ -1138,9 +1157,7 @@ cudaError_t launch_decode(const DecodeArgs& a, int dtype, int layout, cudaStream
 // buffers.  It calls no cudaMalloc / cudaFree or other allocating routine.
 // Requests that do not fit are rejected with KVC_ERR_INVALID_ARG.
 // =====================================================================================
-namespace kvc {
-int split_tokens_for(int page_size);
-}
+
 
 namespace {
 
@@ -1210,7 +1227,8 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   }
 
   // ---- split list (the same partition as kvc_plan_decode) ----
-  const int C = split_tokens_for(page_size);
+  const int C = choose_split_tokens(page_size, h_ctx_lens, n_queries,
+                                    num_kv_heads * ((num_heads / num_kv_heads + 7) / 8), dev);
   int n_items = 0, slot = 0, max_ctx = 0;
   for (int i = 0; i < n_queries; ++i) {
     const int ctx = h_ctx_lens[i];

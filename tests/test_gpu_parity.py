@@ -158,11 +158,16 @@ def test_cached_prefill_matches_host_attention_bit_exact():
     out2 = np.zeros_like(c["Q"])
     matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out2, 1, P, H, Hkv, D, P - 1, c["scale"])
     np.testing.assert_array_equal(out, out2)
-    # prefill row m of the cached call == a single decode query at position m
+    # Prefill row m of the cached call vs the same queries asked alone.  The two
+    # calls have different sizes, so the plan may cut their contexts into splits
+    # of different lengths (512 for the 1024-query prefill, 128 for 3 queries):
+    # the results agree to rounding, not bit for bit.
     outp2 = np.zeros_like(qp[:3])
     matmul_module.gqa_attention(qp[600:603], c["K"][:603], c["V"][:603], outp2, 3, 603, H, Hkv,
                                 D, 600, c["scale"])
-    np.testing.assert_array_equal(outp[600:603], outp2)
+    assert _maxerr(outp[600:603], outp2) <= 2e-3
+    ref = gqa_ref.ref_gqa_attention(qp[600:603], c["K"][:603], c["V"][:603], 600, c["scale"])
+    assert _maxerr(outp[600:603], ref) <= _fp16_tol(ref)
 
 
 def test_validation_matches_reference_exception_classes():
