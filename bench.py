@@ -51,6 +51,8 @@ CONFIGS = {
               lens=("fixed", 4095), seed=2),
     "4": dict(workload="llama3-70b-long-context-decode", layers=80, H=64, Hkv=8, D=128, batch=8,
               lens=("fixed", 32768), seed=4),
+    "5": dict(workload="llama3-70b-offload-kv-cpu", layers=80, H=64, Hkv=8, D=128, batch=1,
+              lens=("fixed", 131072), seed=5),
 }
 PAGE = 16
 
@@ -254,6 +256,14 @@ def run_b200(args, rank, world, local_rank):
     if args.layers:
         cfg["layers"] = args.layers  # profiling subset only (the bench line names it)
     L, H, Hkv, D, B = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["batch"]
+    shard = args.shard or ("heads" if args.config == "4" else "seq")
+    H_full = H
+    if shard == "heads" and world > 1:
+        # KV-head sharding: this rank owns KV heads [r*Hkv/n, (r+1)*Hkv/n) and their
+        # q-heads; the per-head outputs are all-gathered after every layer.
+        h0, h1 = paged.shard_heads(Hkv, world, rank)
+        Hkv = h1 - h0
+        H = H * Hkv // cfg["Hkv"]
     cached = cached_lengths(cfg)
     ctx = cached + 1                                  # context includes the appended token
     table, total_pages = paged.random_block_tables(ctx, args.page_size, cfg["seed"] + 17 * rank)
@@ -267,6 +277,13 @@ def run_b200(args, rank, world, local_rank):
     kn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
     vn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
     out = torch.empty_like(q)
+    gathered = None
+    if shard == "heads" and world > 1:
+        import sharding
+
+        # every rank ends each layer with all heads of every sequence
+        gathered = torch.empty((L, B, H_full, D), dtype=torch.float16, device=dev)
+        hsd = sharding.HeadShardedDecode(pool, H_full, cfg["Hkv"])
     pos = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
     rows = torch.arange(B, dtype=torch.int32, device=dev)
     scale = 1.0 / math.sqrt(D)
@@ -282,7 +299,12 @@ def run_b200(args, rank, world, local_rank):
         for l in range(L):
             if events is not None:
                 events[l][0].record(stream)
-            pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=stream)
+            if gathered is None:
+                pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=stream)
+            else:
+                # fused append + attention on this rank's heads, then the all-gather
+                hsd.append_decode(plan, l, q[l], kn[l], vn[l], gathered[l], bt, scale,
+                                  stream=stream)
             if events is not None:
                 events[l][1].record(stream)
 
@@ -320,7 +342,7 @@ def run_b200(args, rank, world, local_rank):
     if code:
         raise RuntimeError(f"device error {code} ({info}) during timing")
 
-    kv_read, appended, qo = step_bytes(cfg, ctx)
+    kv_read, appended, qo = step_bytes(dict(cfg, H=H, Hkv=Hkv), ctx)
     rank_bytes = kv_read + appended + qo
     # aggregate: max time over ranks, sum of bytes
     if world > 1:
@@ -344,9 +366,23 @@ def run_b200(args, rank, world, local_rank):
         ho = torch.empty_like(hq).pin_memory()
         e2e_steps = max(1, min(args.steps, args.e2e_steps))
 
+        if gathered is not None:
+            hg = torch.empty(tuple(gathered.shape), dtype=torch.float16).pin_memory()
+            qd, kd, vd = torch.empty_like(q[0]), torch.empty_like(kn[0]), torch.empty_like(vn[0])
+            od = torch.empty_like(gathered[0])
+
         def e2e_step():
             for l in range(L):
-                pool.decode_host(plan, l, hq[l], hk[l], hv[l], ho[l], bt, scale, stream=stream)
+                if gathered is None:
+                    pool.decode_host(plan, l, hq[l], hk[l], hv[l], ho[l], bt, scale, stream=stream)
+                    continue
+                # sharded: rank inputs in, fused decode, all-gather, all heads out, wait
+                qd.copy_(hq[l], non_blocking=True)
+                kd.copy_(hk[l], non_blocking=True)
+                vd.copy_(hv[l], non_blocking=True)
+                hsd.append_decode(plan, l, qd, kd, vd, od, bt, scale, stream=stream)
+                hg[l].copy_(od, non_blocking=True)
+                stream.synchronize()
 
         for _ in range(min(2, args.warmup)):
             e2e_step()
@@ -366,11 +402,14 @@ def run_b200(args, rank, world, local_rank):
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e2e_ms = float(t.item())
         h2d = L * B * (H * D + 2 * Hkv * D) * 2
-        d2h = L * B * H * D * 2
+        d2h = L * B * (H_full if gathered is not None else H) * D * 2
         e2e = {"value": round(job_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
                "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "call": "kvc_decode_host (pinned host q/k_new/v_new/out, per layer, waits)"}
+               "call": ("kvc_decode_host (pinned host q/k_new/v_new/out, per layer, waits)"
+                        if gathered is None else
+                        "HeadShardedDecode.append_decode (pinned H2D of this rank's q/k/v, "
+                        "fused decode, NCCL all-gather, D2H of all heads, per layer, waits)")}
 
     if rank != 0:
         return None
@@ -392,7 +431,7 @@ def run_b200(args, rank, world, local_rank):
         "steps_per_s": round(1e3 / ms_per_step, 2),
         "pct_of_peak": round(100.0 * value / (peak * world), 2),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if gathered is not None else "weak",
         "vs_baseline": None,
         "dtype": "f16 storage, f32 accumulate",
         "data": "synthetic: seeded N(0,1) K/V/q, random page permutation",
@@ -400,17 +439,21 @@ def run_b200(args, rank, world, local_rank):
             "workload": f"{cfg['workload']} (BASELINE config {args.config})"
                         + (f" [profiling subset: {L} layers]" if args.layers else ""),
             "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D,
-            "sequences_per_gpu": B, "global_batch": B * world,
+            "sequences_per_gpu": B, "global_batch": B if gathered is not None else B * world,
             "cached_len": (f"U[{cfg['lens'][1]},{cfg['lens'][2]}] seed {cfg['seed']}"
                            if cfg["lens"][0] == "uniform" else int(cfg["lens"][1])),
             "ctx_tokens_per_gpu": int(ctx.sum()), "page_size": args.page_size,
             "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * args.page_size * D * 2 / 1e9, 2),
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
-            "parallelism": f"sequence-sharded x{world} (independent batches, no collective)",
+            "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), NCCL all-gather "
+                            f"of {B * H * D * 2} B of head outputs per GPU per layer"
+                            if gathered is not None else
+                            f"sequence-sharded x{world} (independent batches, no collective)"),
         },
         "roofline": {
-            "bound": "hbm", "kernel": "decode_mma_kernel (append fused)",
+            "bound": "hbm",
+            "kernel": "decode_persistent_kernel (append fused) + merge_splits_kernel",
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
             "unit": "GB/s", "frac": round(achieved / peak, 4),
             "bytes_per_launch": int(dec_bytes), "avg_launch_us": round(dec_avg_ms * 1e3, 2),
@@ -418,7 +461,8 @@ def run_b200(args, rank, world, local_rank):
                               "CUDA events around the timed region / launches (launches overlap)"),
             "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
         },
-        "gpu_launches": L * args.steps,
+        # two launches per layer: the decode kernel and its split merge (PDL)
+        "gpu_launches": 2 * L * args.steps,
         "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
     }
     if e2e:
@@ -436,6 +480,93 @@ def run_b200(args, rank, world, local_rank):
     plan.close()
     pool.close()
     return res
+
+
+# ---------------------------------------------------------------------------------
+# offload arm: KV in host memory, streamed per layer
+# ---------------------------------------------------------------------------------
+def run_offload(args, rank, world, local_rank):
+    """--offload-kv-cpu decode steps through the drop-in KVCacheManager: every
+    layer's cached K/V is streamed from (registered) host memory to the GPU on a
+    copy stream while the previous layer attends.  Each attend call returns
+    after its output is on the host, so host wall time is device-complete time."""
+    import torch
+
+    from kv_cache import KVCacheManager
+
+    torch.cuda.set_device(local_rank)
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg["layers"] = args.layers
+    L, H, Hkv, D = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"]
+    cached = int(cfg["lens"][1])
+    S = cached + 1
+    t0 = time.perf_counter()
+    kv = KVCacheManager(L, S, Hkv, D, offload_to_cpu=True, max_kv_bytes=1 << 50)
+    rng = np.random.default_rng(cfg["seed"])
+    block = rng.standard_normal(1 << 23, dtype=np.float32).astype(np.float16)
+    for arr, shift in ((kv._k_host, 0), (kv._v_host, 12345)):
+        flat = arr.reshape(-1)
+        step = block.size
+        for o in range(0, flat.size, step):
+            n = min(step, flat.size - o)
+            flat[o:o + n] = np.roll(block, shift + o // step)[:n]
+    setup_s = time.perf_counter() - t0
+    q = rng.standard_normal((L, 1, H, D), dtype=np.float32).astype(np.float16)
+    kn = rng.standard_normal((L, 1, Hkv, D), dtype=np.float32).astype(np.float16)
+    vn = rng.standard_normal((L, 1, Hkv, D), dtype=np.float32).astype(np.float16)
+    out = np.empty((1, H, D), dtype=np.float16)
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        for l in range(L):
+            kv.attend(q[l], kn[l], vn[l], out, layer_idx=l, q_len=1, start_pos=cached,
+                      num_heads=H, scale=scale, causal=True)
+
+    t1 = time.perf_counter()
+    for _ in range(args.warmup):
+        step()
+    first = kv.offload_stats()
+    warm_s = time.perf_counter() - t1
+    torch.cuda.synchronize()
+    ts = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - ts
+    st = kv.offload_stats()
+    kv.close()
+    kv_bytes = L * S * Hkv * D * 2 * 2
+    h2d = st["h2d_bytes"] - first["h2d_bytes"]
+    h2d_ms = st["h2d_ms"] - first["h2d_ms"]
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC,
+        "value": round(kv_bytes * args.steps / elapsed / 1e9, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed / args.steps * 1e3, 2),
+        "steps_per_s": round(args.steps / elapsed, 4),
+        "higher_is_better": True,
+        "scaling": "replicas",
+        "vs_baseline": None,
+        "dtype": "f16 storage, f32 accumulate",
+        "data": "synthetic: seeded N(0,1) K/V/q (host KV filled from a tiled random block)",
+        "config": {"workload": f"{cfg['workload']} (BASELINE config {args.config})"
+                               + (f" [subset: {L} layers]" if args.layers else ""),
+                   "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D, "batch": 1,
+                   "cached_len": cached, "host_kv_gb": round(kv_bytes / 1e9, 2),
+                   "timing": "host wall clock; every attend call waits for its output"},
+        "host_link": {"h2d_gb_per_step": round(h2d / args.steps / 1e9, 3),
+                      "h2d_gbs_wall": round(h2d / elapsed / 1e9, 2),
+                      "h2d_gbs_copy_engine": round(h2d / (h2d_ms / 1e3) / 1e9, 2) if h2d_ms else None,
+                      "prefetch_hits": st["prefetch_hits"] - first["prefetch_hits"],
+                      "attend_calls": st["attend_calls"] - first["attend_calls"]},
+        "setup_s": round(setup_s, 1),
+        "warmup_s": round(warm_s, 1),
+    }
 
 
 # DRAM traffic per decode launch (dram__bytes_read.sum + dram__bytes_write.sum)
@@ -494,6 +625,9 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
+    ap.add_argument("--shard", choices=["seq", "heads"], default=None,
+                    help="multi-GPU split: independent sequences per GPU (weak scaling, default for "
+                         "config 3) or KV heads with a per-layer all-gather (strong, config 4)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: run this many layers instead of the config's")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -523,7 +657,10 @@ def main():
                 "nccl", timeout=datetime.timedelta(seconds=120),
                 device_id=torch.device("cuda", local_rank))
         try:
-            res = run_b200(args, rank, world, local_rank)
+            if args.config == "5":
+                res = run_offload(args, rank, world, local_rank)
+            else:
+                res = run_b200(args, rank, world, local_rank)
         finally:
             if world > 1:
                 import torch

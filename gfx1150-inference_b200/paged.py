@@ -232,10 +232,9 @@ def random_block_tables(ctx_lens: Sequence[int], page_size: int, seed: int):
 
 def shard_heads(num_kv_heads: int, world: int, rank: int):
     """KV heads [h0, h1) owned by `rank` when heads are split across `world` GPUs."""
-    if num_kv_heads % world != 0:
-        raise ValueError(f"{num_kv_heads} KV heads cannot be split evenly over {world} GPUs")
-    per = num_kv_heads // world
-    return rank * per, (rank + 1) * per
+    from sharding import shard_heads as _shard
+
+    return _shard(num_kv_heads, world, rank)
 
 
 def default_scale(head_dim: int) -> float:
