@@ -64,7 +64,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   }
 }
 
-// ---- bulk copies (TMA engine, no tensor map, no multicast) ---------------------
+// ---- bulk copies (TMA engine, no tensor map, this CTA only) ---------------------
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
