@@ -283,7 +283,8 @@ def run_b200(args, rank, world, local_rank):
 
         # every rank ends each layer with all heads of every sequence
         gathered = torch.empty((L, B, H_full, D), dtype=torch.float16, device=dev)
-        hsd = sharding.HeadShardedDecode(pool, H_full, cfg["Hkv"])
+        hsd = sharding.HeadShardedDecode(pool, H_full, cfg["Hkv"], transport=args.xchg,
+                                         num_queries=B)
     pos = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
     rows = torch.arange(B, dtype=torch.int32, device=dev)
     scale = 1.0 / math.sqrt(D)
@@ -302,8 +303,11 @@ def run_b200(args, rank, world, local_rank):
             if gathered is None:
                 pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=stream)
             else:
-                # fused append + attention on this rank's heads, then the all-gather
-                hsd.append_decode(plan, l, q[l], kn[l], vn[l], gathered[l], bt, scale,
+                # fused append + attention on this rank's heads; p2p: the merge kernel
+                # pushes the heads to every rank (result in an exchange slot), nccl:
+                # all-gather + copy into gathered[l]
+                hsd.append_decode(plan, l, q[l], kn[l], vn[l],
+                                  gathered[l] if args.xchg == "nccl" else None, bt, scale,
                                   stream=stream)
             if events is not None:
                 events[l][1].record(stream)
@@ -380,8 +384,10 @@ def run_b200(args, rank, world, local_rank):
                 qd.copy_(hq[l], non_blocking=True)
                 kd.copy_(hk[l], non_blocking=True)
                 vd.copy_(hv[l], non_blocking=True)
-                hsd.append_decode(plan, l, qd, kd, vd, od, bt, scale, stream=stream)
-                hg[l].copy_(od, non_blocking=True)
+                res = hsd.append_decode(plan, l, qd, kd, vd,
+                                        od if args.xchg == "nccl" else None, bt, scale,
+                                        stream=stream)
+                hg[l].copy_(res, non_blocking=True)
                 stream.synchronize()
 
         for _ in range(min(2, args.warmup)):
@@ -410,6 +416,9 @@ def run_b200(args, rank, world, local_rank):
                         if gathered is None else
                         "HeadShardedDecode.append_decode (pinned H2D of this rank's q/k/v, "
                         "fused decode, NCCL all-gather, D2H of all heads, per layer, waits)")}
+
+    if gathered is not None:
+        hsd.close()  # collective: the exchange buffers are freed after every rank is done
 
     if rank != 0:
         return None
@@ -446,8 +455,10 @@ def run_b200(args, rank, world, local_rank):
             "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * args.page_size * D * 2 / 1e9, 2),
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
-            "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), NCCL all-gather "
-                            f"of {B * H * D * 2} B of head outputs per GPU per layer"
+            "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), "
+                            + ("NCCL all-gather" if args.xchg == "nccl" else
+                               "merge kernel pushes outputs to every rank over NVLink (p2p)")
+                            + f", {B * H * D * 2} B of head outputs per GPU per layer"
                             if gathered is not None else
                             f"sequence-sharded x{world} (independent batches, no collective)"),
         },
@@ -461,8 +472,9 @@ def run_b200(args, rank, world, local_rank):
                               "CUDA events around the timed region / launches (launches overlap)"),
             "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
         },
-        # two launches per layer: the decode kernel and its split merge (PDL)
-        "gpu_launches": 2 * L * args.steps,
+        # per layer: the decode kernel and its split merge (PDL), plus the exchange
+        # wait kernel when the merge pushes outputs to the other ranks
+        "gpu_launches": (3 if gathered is not None and args.xchg == "p2p" else 2) * L * args.steps,
         "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
     }
     if e2e:
@@ -625,6 +637,8 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
+    ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
+                    help="head-sharded output exchange: fused peer stores or NCCL all-gather")
     ap.add_argument("--shard", choices=["seq", "heads"], default=None,
                     help="multi-GPU split: independent sequences per GPU (weak scaling, default for "
                          "config 3) or KV heads with a per-layer all-gather (strong, config 4)")

@@ -84,7 +84,36 @@ struct kvc_plan {
   }
 };
 
+// Head exchange between the ranks of one node (one process per GPU).  Device
+// buffer (cudaMalloc, shared with the peers through CUDA IPC):
+//   [0, 64)        flag words, one per source rank: the last epoch it published
+//   [128, 132)     merge-CTA completion counter (local use only)
+//   [256, ...)     n_slots output slots of slot_bytes each (256-byte aligned)
+struct kvc_xchg {
+  int device = 0, rank = 0, world = 1;
+  size_t slot_bytes = 0, slot_stride = 0;
+  int n_slots = 0;
+  uint8_t* base = nullptr;                   // this rank's buffer
+  uint8_t* peer_base[kvc::kMaxPeers] = {};   // every rank's buffer as mapped here
+  bool ipc_opened[kvc::kMaxPeers] = {};      // mapped by kvc_xchg_connect (to close)
+  bool connected = false;
+  unsigned int epoch = 0;                    // last epoch issued by this rank
+  unsigned long long wait_limit_ns = 2000000000ull;
+};
+
 namespace kvc {
+constexpr size_t kXchgFlagsOff = 0;
+constexpr size_t kXchgDoneOff = 128;
+constexpr size_t kXchgSlotsOff = 256;
+
+// Where a decode's outputs go when KV heads are split across ranks.
+struct XchgTarget {
+  kvc_xchg* x;
+  int slot;
+  int out_heads;    // q-heads of the whole model (row stride of a slot)
+  int out_head0;    // this rank's first q-head
+};
+
 int pool_alloc(kvc_pool* p, const PoolGeom& g, int device);
 void pool_release(kvc_pool* p);
 int do_append(kvc_pool* pool, int layer, const void* d_k_new, const void* d_v_new,
@@ -94,10 +123,12 @@ int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, 
               const int32_t* d_bt, int bt_stride, float scale, cudaStream_t s);
 int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                     void* d_out, const int32_t* d_bt, int bt_stride, float scale,
-                    const void* d_k_new, const void* d_v_new, cudaStream_t s);
+                    const void* d_k_new, const void* d_v_new, cudaStream_t s,
+                    const XchgTarget* xt = nullptr);
 int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                        const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
-                       int bt_stride, float scale, cudaStream_t s);
+                       int bt_stride, float scale, cudaStream_t s,
+                       const XchgTarget* xt = nullptr);
 // Split length (positions) for a batch: see kvc_host.cpp.
 int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
                         int device);

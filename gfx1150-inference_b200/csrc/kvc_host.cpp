@@ -545,7 +545,8 @@ int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, 
 
 int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                     void* d_out, const int32_t* d_bt, int bt_stride, float scale,
-                    const void* d_k_new, const void* d_v_new, cudaStream_t s) {
+                    const void* d_k_new, const void* d_v_new, cudaStream_t s,
+                    const XchgTarget* xt) {
   const PoolGeom& g = pool->g;
   if (!plan || !plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
   if (layer < 0 || layer >= g.num_layers)
@@ -554,7 +555,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
       plan->page_size != g.page_size)
     return set_error(KVC_ERR_INVALID_ARG, "plan was built for a pool of another geometry.");
   if (plan->n_queries == 0) return KVC_OK;
-  if (!d_q || !d_out || !d_bt)
+  if (!d_q || (!d_out && !xt) || !d_bt)
     return set_error(KVC_ERR_INVALID_ARG, "q, out and block tables must not be null.");
   if ((reinterpret_cast<uintptr_t>(d_q) | reinterpret_cast<uintptr_t>(d_out)) & 3u)
     return set_error(KVC_ERR_INVALID_ARG, "q and out must be 4-byte aligned.");
@@ -590,6 +591,26 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.page_size = g.page_size;
   a.num_pages = g.num_pages;
   a.scale_log2 = scale * kLog2e;
+  a.n_queries_total = plan->n_queries;
+  if (xt) {
+    kvc_xchg* x = xt->x;
+    if (!decode_uses_mma(g.dtype, g.head_dim, g.page_size) || g.layout != kLayoutCore)
+      return set_error(KVC_ERR_INVALID_ARG,
+                       "a head exchange needs fp16/bf16 KV with head_dim in "
+                       "{32,64,96,128,160,192,256} and a page size multiple of 16.");
+    if (plan->n_units == 0) return set_error(KVC_ERR_INVALID_ARG, "empty plan in a head exchange.");
+    a.xchg_peers = x->world;
+    a.out_heads = xt->out_heads;
+    a.out_head0 = xt->out_head0;
+    a.epoch = ++x->epoch;
+    for (int p = 0; p < x->world; ++p) {
+      a.peer_out[p] = x->peer_base[p] + kXchgSlotsOff + static_cast<size_t>(xt->slot) * x->slot_stride;
+      a.peer_flag[p] = reinterpret_cast<unsigned*>(x->peer_base[p] + kXchgFlagsOff) + x->rank;
+    }
+    a.done_ctr = reinterpret_cast<unsigned*>(x->base + kXchgDoneOff);
+    a.my_flags = reinterpret_cast<const unsigned*>(x->base + kXchgFlagsOff);
+    a.wait_limit_ns = x->wait_limit_ns;
+  }
   cudaError_t e = launch_decode(a, g.dtype, g.layout, s);
   if (e != cudaSuccess) return cuda_error(e, "decode kernel");
   return KVC_OK;
@@ -609,7 +630,7 @@ int plan_queries(kvc_plan* plan, const PoolGeom& g, int q_len, int num_heads, in
 // sequence read each other's new rows).
 int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                        const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
-                       int bt_stride, float scale, cudaStream_t s) {
+                       int bt_stride, float scale, cudaStream_t s, const XchgTarget* xt) {
   if (!d_k_new || !d_v_new) return set_error(KVC_ERR_INVALID_ARG, "K/V rows must not be null.");
   if ((reinterpret_cast<uintptr_t>(d_k_new) | reinterpret_cast<uintptr_t>(d_v_new)) & 15u)
     return set_error(KVC_ERR_INVALID_ARG, "K/V row buffers must be 16-byte aligned.");
@@ -617,13 +638,14 @@ int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const vo
     for (int32_t c : plan->positions)
       if (c < 0) return set_error(KVC_ERR_INVALID_ARG, "a query with an empty context has no new row.");
     return do_decode_fused(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, d_k_new, d_v_new,
-                           s);
+                           s, xt);
   }
   int rc = do_append(pool, layer, d_k_new, d_v_new, d_bt, bt_stride,
                      static_cast<const int32_t*>(plan->d_rows.ptr),
                      static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
   if (rc) return rc;
-  return do_decode(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, s);
+  return do_decode_fused(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, nullptr, nullptr,
+                         s, xt);
 }
 
 }  // namespace kvc

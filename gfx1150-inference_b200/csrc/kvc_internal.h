@@ -52,6 +52,8 @@ constexpr int kSplitTokensSmall = 128;
 constexpr int kMaxSplitPages = 64;
 // Warps per CTA of the persistent decode kernel (one CTA per SM).
 constexpr int kPersistWarps = 8;
+// Ranks a head exchange can span (one process per GPU of one node).
+constexpr int kMaxPeers = 8;
 
 struct PoolGeom {
   int num_layers = 0;
@@ -148,6 +150,22 @@ struct DecodeArgs {
   int page_size;
   int num_pages;
   float scale_log2;              // scale * log2(e)
+  // Head exchange (KV heads split across GPUs): when xchg_peers > 0 every query's
+  // output goes through the merge kernel, which stores each output row straight
+  // into the exchange slot of all xchg_peers ranks (peer memory over NVLink) at
+  // row stride out_heads * D and head offset out_head0, then the merge grid's
+  // last CTA publishes `epoch` in this rank's flag word on every rank
+  // (peer_flag[p] points at it); xchg_wait_kernel waits for all ranks' flags.
+  int n_queries_total = 0;       // queries of the plan (merge grid of an exchange)
+  int xchg_peers = 0;
+  int out_heads = 0;
+  int out_head0 = 0;
+  unsigned int epoch = 0;
+  void* peer_out[kMaxPeers] = {};
+  unsigned int* peer_flag[kMaxPeers] = {};
+  unsigned int* done_ctr = nullptr;        // merge CTAs finished (local, zero between launches)
+  const unsigned int* my_flags = nullptr;  // this rank's flag words, one per source rank
+  unsigned long long wait_limit_ns = 0;
 };
 
 struct FillArgs {

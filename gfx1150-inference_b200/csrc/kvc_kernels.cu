@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
     const float l_lo = __shfl_sync(0xffffffffu, l_run, (2 * tig) * 4);
     const float l_hi = __shfl_sync(0xffffffffu, l_run, (2 * tig + 1) * 4);
     const int h_lo = 2 * tig, h_hi = 2 * tig + 1;
-    if (n_splits == 1) {
+    if (n_splits == 1 && a.xchg_peers == 0) {  // exchanged outputs all go through the merge
       const float i_lo = l_lo > 0.f ? 1.0f / l_lo : 0.f;
       const float i_hi = l_hi > 0.f ? 1.0f / l_hi : 0.f;
       T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(query) * H + hq0) * D;
@@ -783,60 +783,109 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
   __syncthreads();
   // the next decode launch may start filling its ring while the merge runs
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  if (a.n_merge_queries == 0) return;
+  const bool xchg = a.xchg_peers > 0;
+  if (!xchg && a.n_merge_queries == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + warp;
-  if (h >= a.num_heads) return;
-  const int query = a.merge_queries[blockIdx.x];
-  const int4 qi = a.qinfo[query];
-  const int slot0 = qi.z, n = qi.w;
-  const int H = a.num_heads, D = a.head_dim;
-  const float2* ml = a.part_ml + static_cast<size_t>(slot0) * H + h;
-  const float* po = a.part_o + (static_cast<size_t>(slot0) * H + h) * D + lane;
-  float mx = kNegBig;
-  for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(&ml[static_cast<size_t>(k) * H]).x);
+  if (h < a.num_heads) {
+    // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
+    const int query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
+    const int4 qi = a.qinfo[query];
+    const int slot0 = qi.z, n = qi.w;
+    const int H = a.num_heads, D = a.head_dim;
+    const float2* ml = a.part_ml + static_cast<size_t>(slot0) * H + h;
+    const float* po = a.part_o + (static_cast<size_t>(slot0) * H + h) * D + lane;
+    float mx = kNegBig;
+    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(&ml[static_cast<size_t>(k) * H]).x);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.f;
-  float acc[EPL];
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    float acc[EPL];
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-  for (int k0 = 0; k0 < n; k0 += 32) {
-    const int kn = min(32, n - k0);
-    float w = 0.f;
-    if (lane < kn) {
-      const float2 v = __ldcg(&ml[static_cast<size_t>(k0 + lane) * H]);
-      w = fast_exp2(v.x - mx);
-      sum += v.y * w;
-    }
-    int kk = 0;
-    for (; kk + 4 <= kn; kk += 4) {  // four splits' loads in flight at once
-      float v[4][EPL];
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += 32) {
+      const int kn = min(32, n - k0);
+      float w = 0.f;
+      if (lane < kn) {
+        const float2 v = __ldcg(&ml[static_cast<size_t>(k0 + lane) * H]);
+        w = fast_exp2(v.x - mx);
+        sum += v.y * w;
+      }
+      int kk = 0;
+      for (; kk + 4 <= kn; kk += 4) {  // four splits' loads in flight at once
+        float v[4][EPL];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int e = 0; e < EPL; ++e)
+            v[u][e] = __ldcg(po + static_cast<size_t>(k0 + kk + u) * H * D + 32 * e);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float wk = __shfl_sync(0xffffffffu, w, kk + u);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) acc[e] += v[u][e] * wk;
+        }
+      }
+      for (; kk < kn; ++kk) {
+        const float wk = __shfl_sync(0xffffffffu, w, kk);
 #pragma unroll
         for (int e = 0; e < EPL; ++e)
-          v[u][e] = __ldcg(po + static_cast<size_t>(k0 + kk + u) * H * D + 32 * e);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float wk = __shfl_sync(0xffffffffu, w, kk + u);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] += v[u][e] * wk;
+          acc[e] += __ldcg(po + static_cast<size_t>(k0 + kk) * H * D + 32 * e) * wk;
       }
     }
-    for (; kk < kn; ++kk) {
-      const float wk = __shfl_sync(0xffffffffu, w, kk);
 #pragma unroll
-      for (int e = 0; e < EPL; ++e)
-        acc[e] += __ldcg(po + static_cast<size_t>(k0 + kk) * H * D + 32 * e) * wk;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+    if (!xchg) {
+      T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(query) * H + h) * D + lane;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) out[32 * e] = from_f32<T>(acc[e] * inv);
+      return;
+    }
+    // the row goes to every rank's exchange slot (this rank's included)
+    const size_t off = (static_cast<size_t>(query) * a.out_heads + a.out_head0 + h) * D + lane;
+    T val[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) val[e] = from_f32<T>(acc[e] * inv);
+    for (int p = 0; p < a.xchg_peers; ++p) {
+      T* out = reinterpret_cast<T*>(a.peer_out[p]) + off;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) out[32 * e] = val[e];
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float inv = sum > 0.f ? 1.0f / sum : 0.f;
-  T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(query) * H + h) * D + lane;
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) out[32 * e] = from_f32<T>(acc[e] * inv);
+  if (!xchg) return;
+  // Exchange completion: each CTA's peer stores are ordered before its count;
+  // the CTA that counts last publishes the epoch in this rank's flag on every rank.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned total = gridDim.x * gridDim.y;
+    const unsigned prev = atomicAdd(a.done_ctr, 1u);
+    if (prev == total - 1) {
+      *a.done_ctr = 0u;  // re-armed for the next launch (ordered by stream order)
+      __threadfence_system();
+      for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], a.epoch);
+    }
+  }
+}
+
+// Wait until every rank of a head exchange has published `epoch` (all heads of
+// this step are in this rank's slot).  One warp; lane p watches rank p's flag.
+// The kernel first waits for the merge grid before it (so it never spins on work
+// of its own GPU), and lets the next launch start early.
+__global__ void __launch_bounds__(32) xchg_wait_kernel(const DecodeArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int p = threadIdx.x;
+  if (p >= a.xchg_peers) return;
+  const unsigned long long t0 = globaltimer_ns();
+  while (static_cast<int>(ld_acquire_sys(a.my_flags + p) - a.epoch) < 0) {
+    if (globaltimer_ns() - t0 > a.wait_limit_ns) {
+      report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, 0x10000u + static_cast<uint32_t>(p));
+      return;
+    }
+    __nanosleep(200);
+  }
 }
 
 // =====================================================================================
@@ -1066,14 +1115,19 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   // merge (and counter re-arm) as a programmatic dependent launch: scheduled while
   // the decode grid drains
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(a.n_merge_queries > 0 ? a.n_merge_queries : 1),
-                     a.n_merge_queries > 0 ? (a.num_heads + 3) / 4 : 1, 1);
+  const int n_merge = a.xchg_peers > 0 ? a.n_queries_total : a.n_merge_queries;
+  cfg.gridDim = dim3(static_cast<unsigned>(n_merge > 0 ? n_merge : 1),
+                     n_merge > 0 ? (a.num_heads + 3) / 4 : 1, 1);
   cfg.blockDim = dim3(128, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a);
+  if ((e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a)) != cudaSuccess) return e;
+  if (a.xchg_peers == 0) return cudaSuccess;
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  return cudaLaunchKernelEx(&cfg, xchg_wait_kernel, a);
 }
 
 template <typename T, int D>

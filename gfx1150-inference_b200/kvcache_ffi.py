@@ -103,7 +103,19 @@ SIGNATURES = {
                                    ctypes.POINTER(ctypes.c_double),
                                    ctypes.POINTER(ctypes.c_int64),
                                    ctypes.POINTER(ctypes.c_int64)]),
+    "kvc_xchg_create": (_c_int, [_c_int, _c_int, _c_int, _c_size, _c_int, ctypes.POINTER(_vp)]),
+    "kvc_xchg_handle": (_c_int, [_vp, _vp]),
+    "kvc_xchg_connect": (_c_int, [_vp, _vp]),
+    "kvc_xchg_connect_ptrs": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "kvc_xchg_base": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "kvc_xchg_slot": (_c_int, [_vp, _c_int, ctypes.POINTER(_vp)]),
+    "kvc_xchg_set_wait_limit": (_c_int, [_vp, ctypes.c_double]),
+    "kvc_xchg_destroy": (_c_int, [_vp]),
+    "kvc_append_decode_xchg": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int,
+                                        _c_int, _vp, _c_int, _c_float, _vp]),
 }
+
+XCHG_HANDLE_BYTES = 64
 
 
 def _load() -> ctypes.CDLL:

@@ -172,6 +172,21 @@ class PagedKVCache:
             _dev(out, "out", self.dtype, n), _i32(block_tables), int(block_tables.shape[-1]),
             float(scale), _sp(stream)))
 
+    def append_decode_xchg(self, plan: DecodePlan, layer: int, q: torch.Tensor,
+                           k_new: Optional[torch.Tensor], v_new: Optional[torch.Tensor],
+                           xchg_handle, slot: int, total_heads: int, head_offset: int,
+                           block_tables: torch.Tensor, scale: float, stream=None):
+        """append_decode with the outputs pushed into every rank's exchange slot
+        (kvc_append_decode_xchg); see sharding.HeadExchange."""
+        n = plan.n_queries * plan.num_heads * self.head_dim
+        nk = plan.n_queries * self.num_kv_heads * self.head_dim
+        kp = None if k_new is None else _dev(k_new, "k_new", self.dtype, nk)
+        vp = None if v_new is None else _dev(v_new, "v_new", self.dtype, nk)
+        ffi.check(ffi.lib.kvc_append_decode_xchg(
+            self.handle, plan.handle, layer, _dev(q, "q", self.dtype, n), kp, vp, xchg_handle,
+            int(slot), int(total_heads), int(head_offset), _i32(block_tables),
+            int(block_tables.shape[-1]), float(scale), _sp(stream)))
+
     def decode_host(self, plan: DecodePlan, layer: int, h_q: torch.Tensor, h_k: torch.Tensor,
                     h_v: torch.Tensor, h_out: torch.Tensor, block_tables: torch.Tensor,
                     scale: float, stream=None):

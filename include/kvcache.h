@@ -295,6 +295,56 @@ KVC_API int kvc_offload_invalidate(kvc_offload_t* off);
 KVC_API int kvc_offload_stats(const kvc_offload_t* off, double* h2d_bytes, double* h2d_ms,
                       int64_t* prefetch_hits, int64_t* attend_calls);
 
+/* ==== 4. Head exchange across the GPUs of one node ========================
+ * No counterpart in the reference (it runs on one GPU).  When the KV heads of
+ * each layer are split over `world` GPUs (one process per GPU, rank r holding
+ * KV heads [r*Hkv/world, (r+1)*Hkv/world) and their q-heads), every rank needs
+ * all heads of the attention output.  kvc_append_decode_xchg runs the fused
+ * append + decode on this rank's heads; its merge kernel stores every output
+ * row straight into exchange slot `slot` of EVERY rank over NVLink (peer
+ * stores) and publishes a per-call epoch, and a wait kernel on this rank waits
+ * until all ranks have published it.  When the call's work has run on
+ * `stream`, slot `slot` of this rank holds (n_queries, total_heads, head_dim)
+ * outputs of all ranks.  All ranks must make the same sequence of calls (same
+ * slots, same plans' query counts).  A slot may be rewritten by a peer from the
+ * second following call on, so consume a slot on `stream` before the next
+ * call, or rotate at least two slots.  A rank that never arrives makes the wait
+ * give up after the wait limit (default 2 s): the device error word then holds
+ * KVC_DEVERR_WAIT_LIMIT with info 0x10000 + the missing rank. */
+
+typedef struct kvc_xchg kvc_xchg_t;
+
+#define KVC_XCHG_HANDLE_BYTES 64
+
+/* This rank's exchange buffer: n_slots slots of slot_bytes (a CUDA IPC
+ * allocation on `device`). */
+KVC_API int kvc_xchg_create(int device, int rank, int world, size_t slot_bytes, int n_slots,
+                            kvc_xchg_t** out);
+/* KVC_XCHG_HANDLE_BYTES bytes that let the other ranks map this buffer. */
+KVC_API int kvc_xchg_handle(const kvc_xchg_t* x, void* handle_out);
+/* Map every rank's buffer: `handles` holds world handles in rank order (this
+ * rank's own entry is ignored). */
+KVC_API int kvc_xchg_connect(kvc_xchg_t* x, const void* handles);
+/* Alternative to kvc_xchg_connect for hosts that map peer memory themselves:
+ * the device address of every rank's exchange buffer in this process, in rank
+ * order, peer_bases[rank] being this rank's own (kvc_xchg_base). */
+KVC_API int kvc_xchg_connect_ptrs(kvc_xchg_t* x, void* const* peer_bases);
+KVC_API int kvc_xchg_base(const kvc_xchg_t* x, void** d_base);
+/* Device address of slot `slot` of this rank's buffer. */
+KVC_API int kvc_xchg_slot(const kvc_xchg_t* x, int slot, void** d_ptr);
+/* Limit of the wait for the other ranks, in seconds (0, 60]. */
+KVC_API int kvc_xchg_set_wait_limit(kvc_xchg_t* x, double seconds);
+KVC_API int kvc_xchg_destroy(kvc_xchg_t* x);
+/* kvc_append_decode with the outputs exchanged: this rank's q-heads are heads
+ * [head_offset, head_offset + plan's num_heads) of total_heads.  d_k_new and
+ * d_v_new may both be null (decode without an append).  fp16/bf16 pools with
+ * the tensor-core head dims only. */
+KVC_API int kvc_append_decode_xchg(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
+                                   const void* d_q, const void* d_k_new, const void* d_v_new,
+                                   kvc_xchg_t* x, int slot, int total_heads, int head_offset,
+                                   const int32_t* d_block_tables, int bt_stride, float scale,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif
