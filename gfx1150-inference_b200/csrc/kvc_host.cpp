@@ -355,10 +355,18 @@ extern "C" int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_ta
 // ============================================================================
 namespace kvc {
 
-// Positions per split, rounded up to whole pages.  A batch whose 512-position
-// splits already give every warp of the persistent grid at least one unit uses
-// them; a smaller batch (e.g. one sequence) uses 128-position splits so the
-// whole GPU streams.  The choice depends only on the context lengths and head
+// Positions per split (a multiple of the page size, at most kMaxSplitPages
+// pages).  The persistent grid has W = SMs x 8 warps; each (split, KV head,
+// q-head chunk) unit runs on one warp, units longest first, handed out
+// dynamically.  For each candidate length s the host estimates the decode time
+// in position units:
+//   max( sum_u (len_u + c0) / W ,  max_u len_u + c0 )  +  (units > W ? s / 4 : 0)
+// (c0 = a unit's fixed cost: first-slab latency, q load, partial write; s / 4 =
+// the expected idle tail of the last wave) over the default 512 and every
+// length whose units fit one wave, and picks the cheapest, the longest on ties.  Long, even contexts with few units get one wave of equal units
+// (e.g. 8 x 32K positions on one KV head: 224-position splits, 1176 units on
+// 1184 warps); large ragged batches get 512-position splits and rely on the
+// dynamic schedule.  The choice depends only on the context lengths and head
 // counts of the batch, so the same call always gets the same partition (the
 // resident and offloaded paths agree bit for bit).  KVC_SPLIT_TOKENS overrides
 // it for tuning.
@@ -386,12 +394,33 @@ int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_
   if (forced > 0) return round_split(forced, page_size);
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  const int64_t warps = static_cast<int64_t>(sms) * kPersistWarps;
-  const int big = round_split(kSplitTokens, page_size);
-  int64_t units = 0;
-  for (int i = 0; i < n_queries; ++i)
-    units += (ctx[i] > 0 ? (ctx[i] + big - 1) / big : 1) * static_cast<int64_t>(units_per_split);
-  return units >= warps ? big : round_split(kSplitTokensSmall, page_size);
+  const double warps = static_cast<double>(sms) * kPersistWarps;
+  constexpr double kUnitCost = 64.0;   // c0, in positions
+  constexpr int kMinSplit = 64;
+  int64_t total = 0, max_ctx = 1;
+  for (int i = 0; i < n_queries; ++i) {
+    total += std::max(ctx[i], 1);
+    max_ctx = std::max<int64_t>(max_ctx, ctx[i]);
+  }
+  const int s_lo = round_split(kMinSplit, page_size);
+  const int s_hi = round_split(kMaxSplitPages * page_size, page_size);
+  int best = round_split(kSplitTokens, page_size);
+  double best_cost = -1.0;
+  for (int sp = s_hi; sp >= s_lo; sp -= page_size) {
+    int64_t units = 0;
+    for (int i = 0; i < n_queries; ++i) units += ctx[i] > 0 ? (ctx[i] + sp - 1) / sp : 1;
+    units *= units_per_split;
+    const double work = (static_cast<double>(total) * units_per_split + kUnitCost * units) / warps;
+    const double longest = static_cast<double>(std::min<int64_t>(sp, max_ctx)) + kUnitCost;
+    // multi-wave partitions other than the default one are not considered
+    if (units > warps && sp != round_split(kSplitTokens, page_size)) continue;
+    const double cost = std::max(work, longest) + (units > warps ? 0.25 * sp : 0.0);
+    if (best_cost < 0.0 || cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
 }
 
 // Build the split list on the host.  ctx_of(i) / row_of(i) describe query i.
@@ -410,7 +439,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->qinfo.clear();
   p->rows.clear();
   p->positions.clear();
-  int slot = 0, max_ctx = 0;
+  int slot = 0, max_ctx = 0, max_splits = 0;
   for (int i = 0; i < n_queries; ++i) {
     const int ctx = ctxs[i];
     const int row = row_of(i);
@@ -424,6 +453,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
       p->items.push_back(make_int4(i, k, k * C, std::min((k + 1) * C, ctx)));
     slot += ns;
     max_ctx = std::max(max_ctx, ctx);
+    max_splits = std::max(max_splits, ns);
   }
   // Longest splits first: CTAs are dispatched roughly in index order, so the
   // short tail splits fill the last wave.
@@ -473,6 +503,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->head_dim = g.head_dim;
   p->page_size = g.page_size;
   p->max_ctx = max_ctx;
+  p->max_splits = max_splits;
   p->device = device;
   {
     std::vector<int32_t> r(p->rows);
@@ -592,6 +623,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.num_pages = g.num_pages;
   a.scale_log2 = scale * kLog2e;
   a.n_queries_total = plan->n_queries;
+  a.merge_wph = merge_warps_per_head(plan->max_splits);
   if (xt) {
     kvc_xchg* x = xt->x;
     if (!decode_uses_mma(g.dtype, g.head_dim, g.page_size) || g.layout != kLayoutCore)

@@ -40,13 +40,12 @@ __host__ __device__ __forceinline__ size_t unit_offset(int layout, int t, int u,
 }
 
 
-// Split-K chunk: every query's context is cut into splits of this many
-// positions (rounded up to a whole number of pages).  The partition depends
-// only on the context length, never on the storage mode, batch composition or
-// GPU count, so resident, offloaded and sharded runs add in the same order.
+// Split-K chunk: every query's context is cut into splits of one length per
+// batch (a multiple of the page size), 512 positions unless a single wave of
+// shorter or longer splits is estimated faster (choose_split_tokens).  The
+// partition depends only on the batch's context lengths and head counts, never
+// on the storage mode, so resident and offloaded runs add in the same order.
 constexpr int kSplitTokens = 512;
-// Split length for batches too small to give every warp a 512-position unit.
-constexpr int kSplitTokensSmall = 128;
 // Upper bound on pages per split the kernels accept (split tokens are capped at
 // kMaxSplitPages * 16).
 constexpr int kMaxSplitPages = 64;
@@ -157,6 +156,7 @@ struct DecodeArgs {
   // last CTA publishes `epoch` in this rank's flag word on every rank
   // (peer_flag[p] points at it); xchg_wait_kernel waits for all ranks' flags.
   int n_queries_total = 0;       // queries of the plan (merge grid of an exchange)
+  int merge_wph = 1;             // merge warps per q-head: 1, 2, 4 or 8 (merge_warps_per_head)
   int xchg_peers = 0;
   int out_heads = 0;
   int out_head0 = 0;
@@ -176,6 +176,11 @@ struct FillArgs {
   float stddev;
   int dtype;
 };
+
+// Warps of the split merge that share one q-head, from the most splits of any query.
+inline int merge_warps_per_head(int max_splits) {
+  return max_splits <= 8 ? 1 : max_splits <= 16 ? 2 : max_splits <= 32 ? 4 : 8;
+}
 
 // Launchers: return cudaSuccess or the launch error.
 cudaError_t launch_append(const AppendArgs& a, int elem_size, cudaStream_t s);

@@ -764,15 +764,21 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
 }
 
 // =====================================================================================
-// Split merge of the persistent path: one warp per (query with several splits,
-// q-head), lanes over head dims.  Runs as a programmatic dependent launch after
-// decode_persistent_kernel and waits for it (griddepcontrol.wait) before
+// Split merge of the persistent path.  Runs as a programmatic dependent launch
+// after decode_persistent_kernel and waits for it (griddepcontrol.wait) before
 // reading the partial states:
 //   M = max_k M_k,  L = sum_k L_k 2^(M_k - M),  out = sum_k O_k 2^(M_k - M) / L
-// with the splits added in index order (the result does not depend on timing).
+// One CTA of 8 warps serves 8 / WPH q-heads of one query; the WPH warps of a
+// head split its splits into WPH contiguous ranges, each warp summing its range
+// in index order with 8 splits' loads in flight per batch, and the ranges are
+// added in range order — the result does not depend on timing.  Long contexts
+// with few queries (hundreds of splits per head) thus merge with WPH times the
+// memory-level parallelism of one warp per head.
 // =====================================================================================
 template <typename T, int EPL>
-__global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
+  __shared__ float red_acc[8][EPL * 32];
+  __shared__ float red_sum[8];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The decode grid has finished: re-arm its unit counter for the next launch,
   // visibly to the whole device before the next launch may start.
@@ -786,25 +792,31 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
   const bool xchg = a.xchg_peers > 0;
   if (!xchg && a.n_merge_queries == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y * 4 + warp;
-  if (h < a.num_heads) {
-    // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
-    const int query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
+  const int wph = a.merge_wph;                 // 1, 2, 4 or 8
+  const int sub = warp % wph;
+  const int h = blockIdx.y * (8 / wph) + warp / wph;
+  const bool active = h < a.num_heads;
+  // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
+  const int query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
+  const int H = a.num_heads, D = a.head_dim;
+  float sum = 0.f;
+  float acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+  if (active) {
     const int4 qi = a.qinfo[query];
     const int slot0 = qi.z, n = qi.w;
-    const int H = a.num_heads, D = a.head_dim;
     const float2* ml = a.part_ml + static_cast<size_t>(slot0) * H + h;
     const float* po = a.part_o + (static_cast<size_t>(slot0) * H + h) * D + lane;
     float mx = kNegBig;
     for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(&ml[static_cast<size_t>(k) * H]).x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-    float acc[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-    for (int k0 = 0; k0 < n; k0 += 32) {
-      const int kn = min(32, n - k0);
+    // this warp's range of splits
+    const int per = (n + wph - 1) / wph;
+    const int kb = min(n, sub * per), ke = min(n, kb + per);
+    for (int k0 = kb; k0 < ke; k0 += 32) {
+      const int kn = min(32, ke - k0);
       float w = 0.f;
       if (lane < kn) {
         const float2 v = __ldcg(&ml[static_cast<size_t>(k0 + lane) * H]);
@@ -812,15 +824,15 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
         sum += v.y * w;
       }
       int kk = 0;
-      for (; kk + 4 <= kn; kk += 4) {  // four splits' loads in flight at once
-        float v[4][EPL];
+      for (; kk + 8 <= kn; kk += 8) {  // eight splits' loads in flight at once
+        float v[8][EPL];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 8; ++u)
 #pragma unroll
           for (int e = 0; e < EPL; ++e)
             v[u][e] = __ldcg(po + static_cast<size_t>(k0 + kk + u) * H * D + 32 * e);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
           const float wk = __shfl_sync(0xffffffffu, w, kk + u);
 #pragma unroll
           for (int e = 0; e < EPL; ++e) acc[e] += v[u][e] * wk;
@@ -835,22 +847,37 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const DecodeArgs a) {
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  if (wph > 1) {  // add the ranges of a head in order
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) red_acc[warp][32 * e + lane] = acc[e];
+    if (lane == 0) red_sum[warp] = sum;
+    __syncthreads();
+    if (sub == 0 && active) {
+      for (int j = 1; j < wph; ++j) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] += red_acc[warp + j][32 * e + lane];
+        sum += red_sum[warp + j];
+      }
+    }
+  }
+  if (sub == 0 && active) {
     const float inv = sum > 0.f ? 1.0f / sum : 0.f;
     if (!xchg) {
       T* out = reinterpret_cast<T*>(a.out) + (static_cast<size_t>(query) * H + h) * D + lane;
 #pragma unroll
       for (int e = 0; e < EPL; ++e) out[32 * e] = from_f32<T>(acc[e] * inv);
-      return;
-    }
-    // the row goes to every rank's exchange slot (this rank's included)
-    const size_t off = (static_cast<size_t>(query) * a.out_heads + a.out_head0 + h) * D + lane;
-    T val[EPL];
+    } else {
+      // the row goes to every rank's exchange slot (this rank's included)
+      const size_t off = (static_cast<size_t>(query) * a.out_heads + a.out_head0 + h) * D + lane;
+      T val[EPL];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) val[e] = from_f32<T>(acc[e] * inv);
-    for (int p = 0; p < a.xchg_peers; ++p) {
-      T* out = reinterpret_cast<T*>(a.peer_out[p]) + off;
+      for (int e = 0; e < EPL; ++e) val[e] = from_f32<T>(acc[e] * inv);
+      for (int p = 0; p < a.xchg_peers; ++p) {
+        T* out = reinterpret_cast<T*>(a.peer_out[p]) + off;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) out[32 * e] = val[e];
+        for (int e = 0; e < EPL; ++e) out[32 * e] = val[e];
+      }
     }
   }
   if (!xchg) return;
@@ -1116,9 +1143,10 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   // the decode grid drains
   cudaLaunchConfig_t cfg = {};
   const int n_merge = a.xchg_peers > 0 ? a.n_queries_total : a.n_merge_queries;
+  const int heads_per_cta = 8 / a.merge_wph;
   cfg.gridDim = dim3(static_cast<unsigned>(n_merge > 0 ? n_merge : 1),
-                     n_merge > 0 ? (a.num_heads + 3) / 4 : 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
+                     n_merge > 0 ? (a.num_heads + heads_per_cta - 1) / heads_per_cta : 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cfg.attrs = attr;
@@ -1283,7 +1311,7 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   // ---- split list (the same partition as kvc_plan_decode) ----
   const int C = choose_split_tokens(page_size, h_ctx_lens, n_queries,
                                     num_kv_heads * ((num_heads / num_kv_heads + 7) / 8), dev);
-  int n_items = 0, slot = 0, max_ctx = 0;
+  int n_items = 0, slot = 0, max_ctx = 0, max_splits = 0;
   for (int i = 0; i < n_queries; ++i) {
     const int ctx = h_ctx_lens[i];
     if (ctx < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
@@ -1298,6 +1326,7 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
       h_items[n_items++] = make_int4(i, k, k * C, std::min((k + 1) * C, ctx));
     slot += ns;
     max_ctx = std::max(max_ctx, ctx);
+    max_splits = std::max(max_splits, ns);
   }
   for (int k = 0; k < n_items; ++k) h_order[k] = k;
   std::sort(h_order, h_order + n_items, [](int x, int y) {
@@ -1386,6 +1415,7 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   a.early_prefetch = 0;
   a.merge_queries = reinterpret_cast<const int32_t*>(base + off_merge);
   a.n_merge_queries = n_merge;
+  a.merge_wph = merge_warps_per_head(max_splits);
   a.k_new = nullptr;
   a.v_new = nullptr;
   a.n_items = n_items;

@@ -308,12 +308,19 @@ def test_paged_ragged_batch_decode_and_pool_bit_exact():
         k, v = pool.gather(0, bt, i, 0, ctx)
         np.testing.assert_array_equal(k.cpu().numpy(), c["ks"][i])
         np.testing.assert_array_equal(v.cpu().numpy(), c["vs"][i])
-    # one batched call == one call per sequence (the reference's sequential batch)
+    # one batched call == one call per sequence (the reference's sequential batch).
+    # The split length is chosen per batch, so a one-sequence plan may add its
+    # splits in another grouping: equal to the fp16 tolerance, not bit for bit.
     for i, ctx in enumerate(c["ctx"]):
         p1 = pool.plan([ctx], c["H"], rows=[i])
         o1 = torch.zeros_like(q[i:i + 1])
         pool.decode(p1, 0, q[i:i + 1].contiguous(), o1, bt, c["scale"])
-        assert torch.equal(o1[0], out[i])
+        ref = out[i].float().cpu().numpy()
+        assert _maxerr(o1[0].cpu().numpy(), ref) <= _fp16_tol(ref)
+        # the same one-sequence plan twice: bit for bit
+        o2 = torch.zeros_like(o1)
+        pool.decode(p1, 0, q[i:i + 1].contiguous(), o2, bt, c["scale"])
+        assert torch.equal(o1, o2)
 
 
 @pytest.mark.parametrize("page_size", [32, 64])
@@ -324,7 +331,10 @@ def test_page_size_does_not_change_results(page_size):
     o16, op = torch.zeros_like(q), torch.zeros_like(q)
     pool16.decode(pool16.plan(c["ctx"], c["H"]), 0, q, o16, bt16, c["scale"])
     poolp.decode(poolp.plan(c["ctx"], c["H"]), 0, q, op, btp, c["scale"])
-    assert torch.equal(o16, op)
+    # splits are whole pages, so the partition may differ with the page size
+    ref = o16.float().cpu().numpy()
+    assert _maxerr(op.cpu().numpy(), ref) <= _fp16_tol(ref)
+    assert _maxerr(op.cpu().numpy(), G["ragged_out"]) <= _fp16_tol(G["ragged_out"])
 
 
 def test_append_decode_fused_equals_separate_and_host_call():
