@@ -472,9 +472,9 @@ def run_b200(args, rank, world, local_rank):
                               "CUDA events around the timed region / launches (launches overlap)"),
             "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
         },
-        # per layer: the decode kernel and its split merge (PDL), plus the exchange
-        # wait kernel when the merge pushes outputs to the other ranks
-        "gpu_launches": (3 if gathered is not None and args.xchg == "p2p" else 2) * L * args.steps,
+        # per layer: the decode kernel and its split merge (PDL; with the p2p head
+        # exchange the merge also pushes the outputs and waits for the peers)
+        "gpu_launches": 2 * L * args.steps,
         "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
     }
     if e2e:

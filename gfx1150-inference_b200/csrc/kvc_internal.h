@@ -154,7 +154,7 @@ struct DecodeArgs {
   // into the exchange slot of all xchg_peers ranks (peer memory over NVLink) at
   // row stride out_heads * D and head offset out_head0, then the merge grid's
   // last CTA publishes `epoch` in this rank's flag word on every rank
-  // (peer_flag[p] points at it); xchg_wait_kernel waits for all ranks' flags.
+  // (peer_flag[p] points at it) and waits until all ranks' flags show the epoch.
   int n_queries_total = 0;       // queries of the plan (merge grid of an exchange)
   int merge_wph = 1;             // merge warps per q-head: 1, 2, 4 or 8 (merge_warps_per_head)
   int xchg_peers = 0;

@@ -882,7 +882,10 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
   }
   if (!xchg) return;
   // Exchange completion: each CTA's peer stores are ordered before its count;
-  // the CTA that counts last publishes the epoch in this rank's flag on every rank.
+  // the CTA that counts last publishes the epoch in this rank's flag on every
+  // rank, then waits (bounded) until every rank has published it here, so the
+  // grid ends only when this rank's slot holds all heads.  Only other GPUs'
+  // kernels are waited for: this grid's own CTAs have all counted.
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -892,26 +895,17 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
       *a.done_ctr = 0u;  // re-armed for the next launch (ordered by stream order)
       __threadfence_system();
       for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], a.epoch);
+      const unsigned long long t0 = globaltimer_ns();
+      for (int p = 0; p < a.xchg_peers; ++p) {
+        while (static_cast<int>(ld_acquire_sys(a.my_flags + p) - a.epoch) < 0) {
+          if (globaltimer_ns() - t0 > a.wait_limit_ns) {
+            report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, 0x10000u + static_cast<uint32_t>(p));
+            return;
+          }
+          __nanosleep(100);
+        }
+      }
     }
-  }
-}
-
-// Wait until every rank of a head exchange has published `epoch` (all heads of
-// this step are in this rank's slot).  One warp; lane p watches rank p's flag.
-// The kernel first waits for the merge grid before it (so it never spins on work
-// of its own GPU), and lets the next launch start early.
-__global__ void __launch_bounds__(32) xchg_wait_kernel(const DecodeArgs a) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int p = threadIdx.x;
-  if (p >= a.xchg_peers) return;
-  const unsigned long long t0 = globaltimer_ns();
-  while (static_cast<int>(ld_acquire_sys(a.my_flags + p) - a.epoch) < 0) {
-    if (globaltimer_ns() - t0 > a.wait_limit_ns) {
-      report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, 0x10000u + static_cast<uint32_t>(p));
-      return;
-    }
-    __nanosleep(200);
   }
 }
 
@@ -1151,11 +1145,7 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if ((e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a)) != cudaSuccess) return e;
-  if (a.xchg_peers == 0) return cudaSuccess;
-  cfg.gridDim = dim3(1, 1, 1);
-  cfg.blockDim = dim3(32, 1, 1);
-  return cudaLaunchKernelEx(&cfg, xchg_wait_kernel, a);
+  return cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a);
 }
 
 template <typename T, int D>

@@ -7,9 +7,9 @@
 // projection.  Instead of a separate all-gather after the decode, the merge
 // kernel stores each finished output row into the exchange slot of every rank
 // over NVLink (plain peer stores; the peers' buffers are mapped with CUDA IPC)
-// and publishes a per-step epoch in a flag word on every rank; a one-warp wait
-// kernel on each rank then waits, with a time limit, until all ranks have
-// published the epoch.  Nothing crosses NVLink but the outputs themselves.
+// and its last CTA publishes a per-step epoch in a flag word on every rank,
+// then waits, with a time limit, until all ranks have published the epoch.
+// Nothing crosses NVLink but the outputs and the flags.
 #include <cuda_runtime.h>
 
 #include <cstring>
