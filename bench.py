@@ -295,22 +295,23 @@ def run_b200(args, rank, world, local_rank):
     plan.set_kv_stable(True)
     torch.cuda.synchronize()
 
-    def step(events=None):
+    def step(events=None, s=None):
         # one fused launch per layer: append each sequence's new row + attend
+        s = stream if s is None else s
         for l in range(L):
             if events is not None:
-                events[l][0].record(stream)
+                events[l][0].record(s)
             if gathered is None:
-                pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=stream)
+                pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=s)
             else:
                 # fused append + attention on this rank's heads; p2p: the merge kernel
                 # pushes the heads to every rank (result in an exchange slot), nccl:
                 # all-gather + copy into gathered[l]
                 hsd.append_decode(plan, l, q[l], kn[l], vn[l],
                                   gathered[l] if args.xchg == "nccl" else None, bt, scale,
-                                  stream=stream)
+                                  stream=s)
             if events is not None:
-                events[l][1].record(stream)
+                events[l][1].record(s)
 
     for _ in range(args.warmup):
         step()
@@ -318,6 +319,18 @@ def run_b200(args, rank, world, local_rank):
     code, info = ffi.device_error(local_rank)
     if code:
         raise RuntimeError(f"device error {code} ({info}) during warm-up")
+    graph = None
+    if not args.no_graph and not args.launch_events:
+        # The step's 2 x L launches are recorded once into a CUDA graph and replayed:
+        # the same kernels, without the host's per-launch cost between them.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(s=torch.cuda.current_stream())
+        graph.replay()  # one untimed replay
+        torch.cuda.synchronize()
+        code, info = ffi.device_error(local_rank)
+        if code:
+            raise RuntimeError(f"device error {code} ({info}) in the captured step")
 
     # Per-launch events would serialise consecutive launches (they overlap by
     # programmatic dependent launch), so they are only recorded on request.
@@ -333,13 +346,20 @@ def run_b200(args, rank, world, local_rank):
     t_stop = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for s in range(args.steps):
-        step(evs[s] if evs else None)
+        if graph is not None:
+            graph.replay()
+        else:
+            step(evs[s] if evs else None)
     t_stop.record(stream)
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
     if world > 1:
         torch.distributed.barrier()
     elapsed_ms = t_start.elapsed_time(t_stop)
+    used_graph = graph is not None
+    if graph is not None:
+        graph.reset()  # released before any collective teardown (it may hold NCCL calls)
+        graph = None
     dec_ms = ([evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(args.steps) for l in range(L)]
               if evs else None)
     code, info = ffi.device_error(local_rank)
@@ -455,6 +475,8 @@ def run_b200(args, rank, world, local_rank):
             "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * args.page_size * D * 2 / 1e9, 2),
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
+            "launch": ("one CUDA graph replay per step (the step's 2 x layers kernel launches)"
+                       if used_graph else "direct launches from the host loop"),
             "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), "
                             + ("NCCL all-gather" if args.xchg == "nccl" else
                                "merge kernel pushes outputs to every rank over NVLink (p2p)")
@@ -637,6 +659,8 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every kernel from the host loop instead of replaying a CUDA graph")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
                     help="head-sharded output exchange: fused peer stores or NCCL all-gather")
     ap.add_argument("--shard", choices=["seq", "heads"], default=None,

@@ -88,6 +88,7 @@ struct kvc_plan {
 // buffer (cudaMalloc, shared with the peers through CUDA IPC):
 //   [0, 64)        flag words, one per source rank: the last epoch it published
 //   [128, 132)     merge-CTA completion counter (local use only)
+//   [192, 196)     last epoch this rank published (local use only)
 //   [256, ...)     n_slots output slots of slot_bytes each (256-byte aligned)
 struct kvc_xchg {
   int device = 0, rank = 0, world = 1;
@@ -97,13 +98,13 @@ struct kvc_xchg {
   uint8_t* peer_base[kvc::kMaxPeers] = {};   // every rank's buffer as mapped here
   bool ipc_opened[kvc::kMaxPeers] = {};      // mapped by kvc_xchg_connect (to close)
   bool connected = false;
-  unsigned int epoch = 0;                    // last epoch issued by this rank
   unsigned long long wait_limit_ns = 2000000000ull;
 };
 
 namespace kvc {
 constexpr size_t kXchgFlagsOff = 0;
 constexpr size_t kXchgDoneOff = 128;
+constexpr size_t kXchgEpochOff = 192;
 constexpr size_t kXchgSlotsOff = 256;
 
 // Where a decode's outputs go when KV heads are split across ranks.

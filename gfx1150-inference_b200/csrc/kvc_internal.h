@@ -160,7 +160,7 @@ struct DecodeArgs {
   int xchg_peers = 0;
   int out_heads = 0;
   int out_head0 = 0;
-  unsigned int epoch = 0;
+  unsigned int* epoch_ctr = nullptr;       // this rank's last epoch (local, device-side)
   void* peer_out[kMaxPeers] = {};
   unsigned int* peer_flag[kMaxPeers] = {};
   unsigned int* done_ctr = nullptr;        // merge CTAs finished (local, zero between launches)

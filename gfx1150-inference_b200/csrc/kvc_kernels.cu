@@ -25,6 +25,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "kvc_common.h"
@@ -893,11 +894,16 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
     const unsigned prev = atomicAdd(a.done_ctr, 1u);
     if (prev == total - 1) {
       *a.done_ctr = 0u;  // re-armed for the next launch (ordered by stream order)
+      // this exchange's epoch: one more than the last one on this rank (every rank
+      // makes the same sequence of exchanges, so the counters agree; kept on the
+      // device so that a captured graph replays with fresh epochs)
+      const unsigned epoch = *a.epoch_ctr + 1u;
+      *a.epoch_ctr = epoch;
       __threadfence_system();
-      for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], a.epoch);
+      for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], epoch);
       const unsigned long long t0 = globaltimer_ns();
       for (int p = 0; p < a.xchg_peers; ++p) {
-        while (static_cast<int>(ld_acquire_sys(a.my_flags + p) - a.epoch) < 0) {
+        while (static_cast<int>(ld_acquire_sys(a.my_flags + p) - epoch) < 0) {
           if (globaltimer_ns() - t0 > a.wait_limit_ns) {
             report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, 0x10000u + static_cast<uint32_t>(p));
             return;
@@ -1108,14 +1114,34 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
 // =====================================================================================
 namespace {
 
+// Dynamic shared memory opt-in, once per kernel, device and size (it is not a
+// stream operation, and skipping it keeps launches cheap and capture-safe).
+constexpr int kMaxDevices = 64;
+template <auto Kernel, typename F>
+cudaError_t set_smem_once(F kern, size_t smem) {
+  static std::atomic<size_t> done[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDevices && done[dev].load(std::memory_order_acquire) >= smem)
+    return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+  if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    size_t cur = done[dev].load(std::memory_order_relaxed);
+    while (cur < smem && !done[dev].compare_exchange_weak(cur, smem)) {
+    }
+  }
+  return e;
+}
+
 template <typename T, int D, int NW>
 cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   constexpr int NS = persist_stages<D>();
   const size_t smem =
       kPersistBarBytes + kPersistMetaBytes + static_cast<size_t>(NW) * NS * 2 * kSlab * D * 2;
   auto kern = decode_persistent_kernel<T, D, NW, NS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = set_smem_once<decode_persistent_kernel<T, D, NW, NS>>(kern, smem);
   if (e != cudaSuccess) return e;
   if (a.n_sched_ctas <= 0) return cudaSuccess;
   cudaLaunchAttribute attr[1];
@@ -1162,8 +1188,7 @@ cudaError_t run_simt(const DecodeArgs& a, int layout, cudaStream_t s) {
   if (merge > smem) smem = merge;
   smem += kBarBytes;
   auto kern = decode_simt_kernel<T, EPL, NS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = set_smem_once<decode_simt_kernel<T, EPL, NS>>(kern, smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = static_cast<unsigned>(a.n_items) * a.num_kv_heads * a.n_hchunk;
   kern<<<grid, 256, smem, s>>>(a, layout);
