@@ -357,6 +357,7 @@ def run_b200(args, rank, world, local_rank):
         torch.distributed.barrier()
     elapsed_ms = t_start.elapsed_time(t_stop)
     used_graph = graph is not None
+    hsd_p2p = gathered is not None and args.xchg == "p2p"
     if graph is not None:
         graph.reset()  # released before any collective teardown (it may hold NCCL calls)
         graph = None
@@ -494,9 +495,10 @@ def run_b200(args, rank, world, local_rank):
                               "CUDA events around the timed region / launches (launches overlap)"),
             "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
         },
-        # per layer: the decode kernel and its split merge (PDL; with the p2p head
-        # exchange the merge also pushes the outputs and waits for the peers)
-        "gpu_launches": 2 * L * args.steps,
+        # per layer: the decode kernel and its split merge (PDL); with the p2p head
+        # exchange the merge also pushes the outputs and a one-warp kernel
+        # publishes and waits for the peers' epochs
+        "gpu_launches": (3 if hsd_p2p else 2) * L * args.steps,
         "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
     }
     if e2e:

@@ -87,7 +87,6 @@ struct kvc_plan {
 // Head exchange between the ranks of one node (one process per GPU).  Device
 // buffer (cudaMalloc, shared with the peers through CUDA IPC):
 //   [0, 64)        flag words, one per source rank: the last epoch it published
-//   [128, 132)     merge-CTA completion counter (local use only)
 //   [192, 196)     last epoch this rank published (local use only)
 //   [256, ...)     n_slots output slots of slot_bytes each (256-byte aligned)
 struct kvc_xchg {
@@ -103,7 +102,6 @@ struct kvc_xchg {
 
 namespace kvc {
 constexpr size_t kXchgFlagsOff = 0;
-constexpr size_t kXchgDoneOff = 128;
 constexpr size_t kXchgEpochOff = 192;
 constexpr size_t kXchgSlotsOff = 256;
 

@@ -638,7 +638,6 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
       a.peer_out[p] = x->peer_base[p] + kXchgSlotsOff + static_cast<size_t>(xt->slot) * x->slot_stride;
       a.peer_flag[p] = reinterpret_cast<unsigned*>(x->peer_base[p] + kXchgFlagsOff) + x->rank;
     }
-    a.done_ctr = reinterpret_cast<unsigned*>(x->base + kXchgDoneOff);
     a.epoch_ctr = reinterpret_cast<unsigned*>(x->base + kXchgEpochOff);
     a.my_flags = reinterpret_cast<const unsigned*>(x->base + kXchgFlagsOff);
     a.wait_limit_ns = x->wait_limit_ns;

@@ -149,21 +149,20 @@ struct DecodeArgs {
   int page_size;
   int num_pages;
   float scale_log2;              // scale * log2(e)
+  int n_queries_total = 0;       // queries of the plan (merge grid of an exchange)
+  int merge_wph = 1;             // merge warps per q-head: 1, 2, 4 or 8 (merge_warps_per_head)
   // Head exchange (KV heads split across GPUs): when xchg_peers > 0 every query's
   // output goes through the merge kernel, which stores each output row straight
   // into the exchange slot of all xchg_peers ranks (peer memory over NVLink) at
-  // row stride out_heads * D and head offset out_head0, then the merge grid's
-  // last CTA publishes `epoch` in this rank's flag word on every rank
-  // (peer_flag[p] points at it) and waits until all ranks' flags show the epoch.
-  int n_queries_total = 0;       // queries of the plan (merge grid of an exchange)
-  int merge_wph = 1;             // merge warps per q-head: 1, 2, 4 or 8 (merge_warps_per_head)
+  // row stride out_heads * D and head offset out_head0; xchg_signal_kernel then
+  // publishes the next epoch (epoch_ctr + 1) in this rank's flag word on every
+  // rank (peer_flag[p] points at it) and waits until all ranks' flags show it.
   int xchg_peers = 0;
   int out_heads = 0;
   int out_head0 = 0;
   unsigned int* epoch_ctr = nullptr;       // this rank's last epoch (local, device-side)
   void* peer_out[kMaxPeers] = {};
   unsigned int* peer_flag[kMaxPeers] = {};
-  unsigned int* done_ctr = nullptr;        // merge CTAs finished (local, zero between launches)
   const unsigned int* my_flags = nullptr;  // this rank's flag words, one per source rank
   unsigned long long wait_limit_ns = 0;
 };

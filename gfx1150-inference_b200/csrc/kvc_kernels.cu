@@ -881,37 +881,38 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
       }
     }
   }
-  if (!xchg) return;
-  // Exchange completion: each CTA's peer stores are ordered before its count;
-  // the CTA that counts last publishes the epoch in this rank's flag on every
-  // rank, then waits (bounded) until every rank has published it here, so the
-  // grid ends only when this rank's slot holds all heads.  Only other GPUs'
-  // kernels are waited for: this grid's own CTAs have all counted.
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned total = gridDim.x * gridDim.y;
-    const unsigned prev = atomicAdd(a.done_ctr, 1u);
-    if (prev == total - 1) {
-      *a.done_ctr = 0u;  // re-armed for the next launch (ordered by stream order)
-      // this exchange's epoch: one more than the last one on this rank (every rank
-      // makes the same sequence of exchanges, so the counters agree; kept on the
-      // device so that a captured graph replays with fresh epochs)
-      const unsigned epoch = *a.epoch_ctr + 1u;
-      *a.epoch_ctr = epoch;
-      __threadfence_system();
-      for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], epoch);
-      const unsigned long long t0 = globaltimer_ns();
-      for (int p = 0; p < a.xchg_peers; ++p) {
-        while (static_cast<int>(ld_acquire_sys(a.my_flags + p) - epoch) < 0) {
-          if (globaltimer_ns() - t0 > a.wait_limit_ns) {
-            report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, 0x10000u + static_cast<uint32_t>(p));
-            return;
-          }
-          __nanosleep(100);
-        }
-      }
+}
+
+// Exchange completion, one warp after the merge grid (programmatic dependent
+// launch).  griddepcontrol.wait returns when the merge grid has finished and its
+// stores (this rank's heads, already written into every rank's slot) are
+// performed; one system-scope fence then orders them before the epoch this rank
+// publishes in its flag word on every rank, and lane p waits (bounded) until
+// rank p has published the same epoch here.  Only other GPUs' kernels are
+// waited for.  The epoch is one more than this rank's previous one, kept on the
+// device so a captured graph replays with fresh epochs; every rank makes the
+// same sequence of exchanges, so the counters agree.
+__global__ void __launch_bounds__(32) xchg_signal_kernel(const DecodeArgs a) {
+  // the next decode launch may be scheduled while this waits
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x;
+  unsigned epoch = 0;
+  if (lane == 0) {
+    epoch = *a.epoch_ctr + 1u;
+    *a.epoch_ctr = epoch;
+    __threadfence_system();
+    for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], epoch);
+  }
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
+  if (lane >= a.xchg_peers) return;
+  const unsigned long long t0 = globaltimer_ns();
+  while (static_cast<int>(ld_acquire_sys(a.my_flags + lane) - epoch) < 0) {
+    if (globaltimer_ns() - t0 > a.wait_limit_ns) {
+      report_error(2u /*KVC_DEVERR_WAIT_LIMIT*/, 0x10000u + static_cast<uint32_t>(lane));
+      return;
     }
+    __nanosleep(64);
   }
 }
 
@@ -1171,7 +1172,11 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a);
+  if ((e = cudaLaunchKernelEx(&cfg, merge_splits_kernel<T, D / 32>, a)) != cudaSuccess) return e;
+  if (a.xchg_peers == 0) return cudaSuccess;
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  return cudaLaunchKernelEx(&cfg, xchg_signal_kernel, a);
 }
 
 template <typename T, int D>

@@ -6,9 +6,9 @@
 // needs all heads of the attention output before the next layer's output
 // projection.  Instead of a separate all-gather after the decode, the merge
 // kernel stores each finished output row into the exchange slot of every rank
-// over NVLink (plain peer stores; the peers' buffers are mapped with CUDA IPC)
-// and its last CTA publishes a per-step epoch in a flag word on every rank,
-// then waits, with a time limit, until all ranks have published the epoch.
+// over NVLink (plain peer stores; the peers' buffers are mapped with CUDA IPC);
+// a one-warp kernel behind it then publishes a per-step epoch in a flag word on
+// every rank and waits, with a time limit, until all ranks have published it.
 // Nothing crosses NVLink but the outputs and the flags.
 #include <cuda_runtime.h>
 

@@ -14,7 +14,7 @@ multi-device form.  On an 8-GPU B200 node the decode step shards two ways:
   per-head outputs are exchanged once per layer (strong scaling: total work
   fixed, per-GPU KV shrinks with the number of GPUs).  Two transports:
   ``"p2p"`` (default on GPUs) — the decode's merge kernel stores every output
-  row into all ranks' exchange slots over NVLink and its last CTA waits for the
+  row into all ranks' exchange slots over NVLink and a one-warp kernel waits for the
   ranks' epochs (``HeadExchange``, the C ABI's kvc_xchg_*); ``"nccl"`` — a
   separate ``all_gather_into_tensor`` after the decode, plus a strided copy
   back into head order (``gather_head_outputs``, also runs over gloo on CPU).

@@ -302,8 +302,8 @@ KVC_API int kvc_offload_stats(const kvc_offload_t* off, double* h2d_bytes, doubl
  * all heads of the attention output.  kvc_append_decode_xchg runs the fused
  * append + decode on this rank's heads; its merge kernel stores every output
  * row straight into exchange slot `slot` of EVERY rank over NVLink (peer
- * stores), publishes a per-call epoch on every rank and waits until all ranks
- * have published it (the merge grid ends only then).  When the call's work has run on
+ * stores), and a one-warp kernel behind it publishes a per-call epoch on every
+ * rank and waits until all ranks have published it.  When the call's work has run on
  * `stream`, slot `slot` of this rank holds (n_queries, total_heads, head_dim)
  * outputs of all ranks.  All ranks must make the same sequence of calls (same
  * slots, same plans' query counts).  A slot may be rewritten by a peer from the

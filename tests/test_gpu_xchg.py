@@ -126,7 +126,7 @@ def test_xchg_fused_append_matches_append_decode(cuda_device):
 
 
 def test_xchg_wait_gives_up_when_a_rank_never_publishes(cuda_device):
-    """Rank 1's flag is never written (nothing plays rank 1): the merge kernel's wait must
+    """Rank 1's flag is never written (nothing plays rank 1): the exchange wait must
     give up after its limit, report it, and leave the context usable."""
     H, Hkv, D, ctx, pool, bt, q = _case(seed=8, ctx=(300, 40))
     plan = pool.plan(ctx, H)
