@@ -493,7 +493,9 @@ def run_b200(args, rank, world, local_rank):
             "bytes_per_launch": int(dec_bytes), "avg_launch_us": round(dec_avg_ms * 1e3, 2),
             "duration_from": ("per-launch CUDA events" if dec_ms else
                               "CUDA events around the timed region / launches (launches overlap)"),
-            "traffic": TRAFFIC_PER_LAUNCH.get(args.config),
+            "traffic": (TRAFFIC_PER_LAUNCH.get(args.config)
+                        if not args.layers and world == 1 and args.page_size == PAGE else None),
+            "traffic_from": "ncu dram__bytes_read.sum + dram__bytes_write.sum, decode kernel",
         },
         # per layer: the decode kernel and its split merge (PDL); with the p2p head
         # exchange the merge also pushes the outputs and a one-warp kernel
@@ -607,7 +609,11 @@ def run_offload(args, rank, world, local_rank):
 
 # DRAM traffic per decode launch (dram__bytes_read.sum + dram__bytes_write.sum)
 # from the committed ncu captures; None until captured for a workload.
-TRAFFIC_PER_LAUNCH = {}
+# DRAM bytes (read + write) of one decode_persistent_kernel launch, from an ncu
+# capture of the same per-launch shape (profiles/decode_persistent_kernel_*.md).
+TRAFFIC_PER_LAUNCH = {
+    "3": 566_632_960 + 7_981_824,
+}
 
 
 # ---------------------------------------------------------------------------------
