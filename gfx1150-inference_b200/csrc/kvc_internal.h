@@ -150,7 +150,7 @@ struct DecodeArgs {
   int num_pages;
   float scale_log2;              // scale * log2(e)
   int n_queries_total = 0;       // queries of the plan (merge grid of an exchange)
-  int merge_wph = 1;             // merge warps per q-head: 1, 2, 4 or 8 (merge_warps_per_head)
+  int merge_wph = 1;             // merge warps per q-head: 1, 2, 4, 8 or 16 (merge_warps_per_head)
   // Head exchange (KV heads split across GPUs): when xchg_peers > 0 every query's
   // output goes through the merge kernel, which stores each output row straight
   // into the exchange slot of all xchg_peers ranks (peer memory over NVLink) at
@@ -176,9 +176,11 @@ struct FillArgs {
   int dtype;
 };
 
-// Warps of the split merge that share one q-head, from the most splits of any query.
+// Warps of one split-merge CTA, and how many of them share one q-head (from the
+// most splits of any query: about eight splits per warp).
+constexpr int kMergeWarps = 16;
 inline int merge_warps_per_head(int max_splits) {
-  return max_splits <= 8 ? 1 : max_splits <= 16 ? 2 : max_splits <= 32 ? 4 : 8;
+  return max_splits <= 8 ? 1 : max_splits <= 16 ? 2 : max_splits <= 32 ? 4 : max_splits <= 64 ? 8 : 16;
 }
 
 // Launchers: return cudaSuccess or the launch error.

@@ -769,17 +769,18 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
 // after decode_persistent_kernel and waits for it (griddepcontrol.wait) before
 // reading the partial states:
 //   M = max_k M_k,  L = sum_k L_k 2^(M_k - M),  out = sum_k O_k 2^(M_k - M) / L
-// One CTA of 8 warps serves 8 / WPH q-heads of one query; the WPH warps of a
-// head split its splits into WPH contiguous ranges, each warp summing its range
-// in index order with 8 splits' loads in flight per batch, and the ranges are
-// added in range order — the result does not depend on timing.  Long contexts
-// with few queries (hundreds of splits per head) thus merge with WPH times the
-// memory-level parallelism of one warp per head.
+// One CTA of 16 warps serves 16 / WPH q-heads of one query.  The WPH warps of a
+// head take contiguous ranges of its splits; each warp merges its range in one
+// pass (running maximum per 32 splits, eight splits' loads in flight), and the
+// ranges are then combined in range order through shared memory.  The order of
+// every addition is fixed, so the result does not depend on timing, and a long
+// context with few queries (hundreds of splits per head) merges in a few memory
+// round trips.
 // =====================================================================================
 template <typename T, int EPL>
-__global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
-  __shared__ float red_acc[8][EPL * 32];
-  __shared__ float red_sum[8];
+__global__ void __launch_bounds__(512) merge_splits_kernel(const DecodeArgs a) {
+  __shared__ float red_acc[kMergeWarps][EPL * 32];
+  __shared__ float red_m[kMergeWarps], red_l[kMergeWarps];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The decode grid has finished: re-arm its unit counter for the next launch,
   // visibly to the whole device before the next launch may start.
@@ -793,14 +794,14 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
   const bool xchg = a.xchg_peers > 0;
   if (!xchg && a.n_merge_queries == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wph = a.merge_wph;                 // 1, 2, 4 or 8
+  const int wph = a.merge_wph;                 // 1, 2, 4, 8 or 16
   const int sub = warp % wph;
-  const int h = blockIdx.y * (8 / wph) + warp / wph;
+  const int h = blockIdx.y * (kMergeWarps / wph) + warp / wph;
   const bool active = h < a.num_heads;
   // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
   const int query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
   const int H = a.num_heads, D = a.head_dim;
-  float sum = 0.f;
+  float m_run = kNegBig, sum = 0.f;
   float acc[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
@@ -809,56 +810,68 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
     const int slot0 = qi.z, n = qi.w;
     const float2* ml = a.part_ml + static_cast<size_t>(slot0) * H + h;
     const float* po = a.part_o + (static_cast<size_t>(slot0) * H + h) * D + lane;
-    float mx = kNegBig;
-    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(&ml[static_cast<size_t>(k) * H]).x);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     // this warp's range of splits
     const int per = (n + wph - 1) / wph;
     const int kb = min(n, sub * per), ke = min(n, kb + per);
     for (int k0 = kb; k0 < ke; k0 += 32) {
       const int kn = min(32, ke - k0);
-      float w = 0.f;
-      if (lane < kn) {
-        const float2 v = __ldcg(&ml[static_cast<size_t>(k0 + lane) * H]);
-        w = fast_exp2(v.x - mx);
-        sum += v.y * w;
+      float2 st = make_float2(kNegBig, 0.f);
+      if (lane < kn) st = __ldcg(&ml[static_cast<size_t>(k0 + lane) * H]);
+      float cm = st.x;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+      if (cm > m_run) {  // warp-uniform: rescale what this warp has so far
+        const float r = fast_exp2(m_run - cm);
+        sum *= r;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] *= r;
+        m_run = cm;
       }
-      int kk = 0;
-      for (; kk + 8 <= kn; kk += 8) {  // eight splits' loads in flight at once
+      const float w = lane < kn ? fast_exp2(st.x - m_run) : 0.f;
+      sum += st.y * w;
+      // eight splits' loads in flight at once; the batch past the range's end
+      // loads nothing and adds zeros
+      for (int kk = 0; kk < kn; kk += 8) {
         float v[8][EPL];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < 8; ++u) {
+          const bool ok = kk + u < kn;
 #pragma unroll
           for (int e = 0; e < EPL; ++e)
-            v[u][e] = __ldcg(po + static_cast<size_t>(k0 + kk + u) * H * D + 32 * e);
+            v[u][e] = ok ? __ldcg(po + static_cast<size_t>(k0 + kk + u) * H * D + 32 * e) : 0.f;
+        }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float wk = __shfl_sync(0xffffffffu, w, kk + u);
+          float wk = __shfl_sync(0xffffffffu, w, (kk + u) & 31);
+          wk = kk + u < kn ? wk : 0.f;
 #pragma unroll
           for (int e = 0; e < EPL; ++e) acc[e] += v[u][e] * wk;
         }
-      }
-      for (; kk < kn; ++kk) {
-        const float wk = __shfl_sync(0xffffffffu, w, kk);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e)
-          acc[e] += __ldcg(po + static_cast<size_t>(k0 + kk) * H * D + 32 * e) * wk;
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   }
-  if (wph > 1) {  // add the ranges of a head in order
+  if (wph > 1) {  // combine the ranges of a head in order
 #pragma unroll
     for (int e = 0; e < EPL; ++e) red_acc[warp][32 * e + lane] = acc[e];
-    if (lane == 0) red_sum[warp] = sum;
+    if (lane == 0) {
+      red_m[warp] = m_run;
+      red_l[warp] = sum;
+    }
     __syncthreads();
     if (sub == 0 && active) {
-      for (int j = 1; j < wph; ++j) {
+      float mx = m_run;
+      for (int j = 1; j < wph; ++j) mx = fmaxf(mx, red_m[warp + j]);
+      const float r0 = fast_exp2(m_run - mx);
+      sum *= r0;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] += red_acc[warp + j][32 * e + lane];
-        sum += red_sum[warp + j];
+      for (int e = 0; e < EPL; ++e) acc[e] *= r0;
+      for (int j = 1; j < wph; ++j) {
+        const float r = fast_exp2(red_m[warp + j] - mx);
+        sum += red_l[warp + j] * r;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] += red_acc[warp + j][32 * e + lane] * r;
       }
     }
   }
@@ -886,7 +899,7 @@ __global__ void __launch_bounds__(256) merge_splits_kernel(const DecodeArgs a) {
 // Exchange completion, one warp after the merge grid (programmatic dependent
 // launch).  griddepcontrol.wait returns when the merge grid has finished and its
 // stores (this rank's heads, already written into every rank's slot) are
-// performed; one system-scope fence then orders them before the epoch this rank
+// performed; one system-scope acq_rel fence then orders them before the epoch this rank
 // publishes in its flag word on every rank, and lane p waits (bounded) until
 // rank p has published the same epoch here.  Only other GPUs' kernels are
 // waited for.  The epoch is one more than this rank's previous one, kept on the
@@ -901,8 +914,9 @@ __global__ void __launch_bounds__(32) xchg_signal_kernel(const DecodeArgs a) {
   if (lane == 0) {
     epoch = *a.epoch_ctr + 1u;
     *a.epoch_ctr = epoch;
-    __threadfence_system();
-    for (int p = 0; p < a.xchg_peers; ++p) st_release_sys(a.peer_flag[p], epoch);
+    // release pattern: one acq_rel fence at system scope, then relaxed flag stores
+    fence_acq_rel_sys();
+    for (int p = 0; p < a.xchg_peers; ++p) st_relaxed_sys(a.peer_flag[p], epoch);
   }
   epoch = __shfl_sync(0xffffffffu, epoch, 0);
   if (lane >= a.xchg_peers) return;
@@ -1164,10 +1178,10 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   // the decode grid drains
   cudaLaunchConfig_t cfg = {};
   const int n_merge = a.xchg_peers > 0 ? a.n_queries_total : a.n_merge_queries;
-  const int heads_per_cta = 8 / a.merge_wph;
+  const int heads_per_cta = kMergeWarps / a.merge_wph;
   cfg.gridDim = dim3(static_cast<unsigned>(n_merge > 0 ? n_merge : 1),
                      n_merge > 0 ? (a.num_heads + heads_per_cta - 1) / heads_per_cta : 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
+  cfg.blockDim = dim3(32 * kMergeWarps, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cfg.attrs = attr;
