@@ -113,6 +113,16 @@ struct XchgTarget {
   int out_head0;    // this rank's first q-head
 };
 
+// Device address of page-locked host memory (written directly by the kernels),
+// or nullptr for pageable memory.
+void* mapped_host_ptr(void* h);
+// End of a host-buffer call on stream s: copy `bytes` of d_out to h_out unless
+// the kernels wrote h_out directly (d_out == nullptr), read the device error
+// word into page-locked memory on the same stream, wait for the stream, and
+// report a device error under `what`.
+int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t bytes,
+                     const char* what);
+
 int pool_alloc(kvc_pool* p, const PoolGeom& g, int device);
 void pool_release(kvc_pool* p);
 int do_append(kvc_pool* pool, int layer, const void* d_k_new, const void* d_v_new,
@@ -123,11 +133,13 @@ int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, 
 int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                     void* d_out, const int32_t* d_bt, int bt_stride, float scale,
                     const void* d_k_new, const void* d_v_new, cudaStream_t s,
-                    const XchgTarget* xt = nullptr);
+                    const XchgTarget* xt = nullptr, int early = -1);
+// early: -1 = the plan's KVC_PLAN_KV_STABLE flag; 1 = the launch before this one
+// (stream order) writes neither KV pages nor block tables, so KV may stream early.
 int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                        const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
                        int bt_stride, float scale, cudaStream_t s,
-                       const XchgTarget* xt = nullptr);
+                       const XchgTarget* xt = nullptr, int early = -1);
 // Split length (positions) for a batch: see kvc_host.cpp.
 int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
                         int device);

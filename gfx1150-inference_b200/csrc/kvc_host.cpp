@@ -58,6 +58,61 @@ int check_device_error(const char* what) {
   return set_error(KVC_ERR_DEVICE, "%s: %s (value %d)", what, name, static_cast<int>(info));
 }
 
+void* mapped_host_ptr(void* h) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, h) != cudaSuccess) {
+    cudaGetLastError();  // pageable memory on older runtimes reports an error
+    return nullptr;
+  }
+  return attr.type == cudaMemoryTypeHost ? attr.devicePointer : nullptr;
+}
+
+namespace {
+// Page-locked landing place of each device's error word, and the word's address.
+struct ErrMirror {
+  uint32_t* host = nullptr;
+  void* dev = nullptr;
+};
+std::mutex g_mirror_mu;
+ErrMirror g_mirror[64];
+
+cudaError_t error_mirror(ErrMirror** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_mirror_mu);
+  ErrMirror& m = g_mirror[dev];
+  if (!m.host) {
+    void* h = nullptr;
+    if ((e = cudaMallocHost(&h, 64)) != cudaSuccess) return e;
+    if ((e = device_error_address(&m.dev)) != cudaSuccess) {
+      cudaFreeHost(h);
+      return e;
+    }
+    m.host = static_cast<uint32_t*>(h);
+  }
+  *out = &m;
+  return cudaSuccess;
+}
+}  // namespace
+
+int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t bytes,
+                     const char* what) {
+  cudaError_t e;
+  if (d_out && bytes && (e = cudaMemcpyAsync(h_out, d_out, bytes, cudaMemcpyDeviceToHost, s)))
+    return cuda_error(e, "cudaMemcpyAsync(D2H)");
+  ErrMirror* m = nullptr;
+  if ((e = error_mirror(&m)) != cudaSuccess) return cuda_error(e, "device error mirror");
+  // Concurrent calls on one device copy the same word into the same place: a call
+  // sees at least every error raised before its own kernels finished.
+  if ((e = cudaMemcpyAsync(m->host, m->dev, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s)))
+    return cuda_error(e, "cudaMemcpyAsync(error word)");
+  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  if ((reinterpret_cast<volatile uint32_t*>(m->host)[0]) == KVC_DEVERR_NONE) return KVC_OK;
+  return check_device_error(what);  // rare: read, clear and report
+}
+
 int elem_size_of(int dtype) {
   switch (dtype) {
     case KVC_DTYPE_F16: return 2;
@@ -577,7 +632,7 @@ int do_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q, 
 int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                     void* d_out, const int32_t* d_bt, int bt_stride, float scale,
                     const void* d_k_new, const void* d_v_new, cudaStream_t s,
-                    const XchgTarget* xt) {
+                    const XchgTarget* xt, int early) {
   const PoolGeom& g = pool->g;
   if (!plan || !plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
   if (layer < 0 || layer >= g.num_layers)
@@ -608,7 +663,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.n_units = plan->n_units;
   a.queue = static_cast<unsigned*>(plan->d_queue.ptr);
   a.n_sched_ctas = plan->n_sched_ctas;
-  a.early_prefetch = (plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0;
+  a.early_prefetch = early >= 0 ? early : ((plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0);
   a.merge_queries = static_cast<const int32_t*>(plan->d_merge.ptr);
   a.n_merge_queries = static_cast<int>(plan->merge_queries.size());
   a.k_new = static_cast<const uint8_t*>(d_k_new);
@@ -661,7 +716,8 @@ int plan_queries(kvc_plan* plan, const PoolGeom& g, int q_len, int num_heads, in
 // sequence read each other's new rows).
 int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const void* d_q,
                        const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
-                       int bt_stride, float scale, cudaStream_t s, const XchgTarget* xt) {
+                       int bt_stride, float scale, cudaStream_t s, const XchgTarget* xt,
+                       int early) {
   if (!d_k_new || !d_v_new) return set_error(KVC_ERR_INVALID_ARG, "K/V rows must not be null.");
   if ((reinterpret_cast<uintptr_t>(d_k_new) | reinterpret_cast<uintptr_t>(d_v_new)) & 15u)
     return set_error(KVC_ERR_INVALID_ARG, "K/V row buffers must be 16-byte aligned.");
@@ -669,7 +725,7 @@ int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const vo
     for (int32_t c : plan->positions)
       if (c < 0) return set_error(KVC_ERR_INVALID_ARG, "a query with an empty context has no new row.");
     return do_decode_fused(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, d_k_new, d_v_new,
-                           s, xt);
+                           s, xt, early);
   }
   int rc = do_append(pool, layer, d_k_new, d_v_new, d_bt, bt_stride,
                      static_cast<const int32_t*>(plan->d_rows.ptr),
@@ -769,17 +825,38 @@ extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int lay
   uint8_t* d_out = d + qb_al;
   uint8_t* d_k = d + 2 * qb_al;
   uint8_t* d_v = d_k + kb_al;
-  if ((e = cudaMemcpyAsync(d_q, h_q, qb, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(d_k, h_k_new, kb, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(d_v, h_v_new, kb, cudaMemcpyHostToDevice, s)))
+  // Page-locked inputs are read by a staging kernel that lets the decode stream
+  // KV meanwhile (the staging kernel writes no pages or block tables, so the
+  // decode may start early); other inputs are copied by the copy engine.
+  const void* mq = mapped_host_ptr(const_cast<void*>(h_q));
+  const void* mk = mapped_host_ptr(const_cast<void*>(h_k_new));
+  const void* mv = mapped_host_ptr(const_cast<void*>(h_v_new));
+  const bool staged = mq && mk && mv &&
+      ((reinterpret_cast<uintptr_t>(mq) | reinterpret_cast<uintptr_t>(mk) |
+        reinterpret_cast<uintptr_t>(mv)) & 15u) == 0;
+  if (staged) {
+    StageArgs st;
+    st.src[0] = static_cast<const uint8_t*>(mq);
+    st.src[1] = static_cast<const uint8_t*>(mk);
+    st.src[2] = static_cast<const uint8_t*>(mv);
+    st.dst[0] = d_q;
+    st.dst[1] = d_k;
+    st.dst[2] = d_v;
+    st.bytes[0] = qb;
+    st.bytes[1] = kb;
+    st.bytes[2] = kb;
+    if ((e = launch_stage_inputs(st, s))) return cuda_error(e, "input staging kernel");
+  } else if ((e = cudaMemcpyAsync(d_q, h_q, qb, cudaMemcpyHostToDevice, s)) ||
+             (e = cudaMemcpyAsync(d_k, h_k_new, kb, cudaMemcpyHostToDevice, s)) ||
+             (e = cudaMemcpyAsync(d_v, h_v_new, kb, cudaMemcpyHostToDevice, s))) {
     return cuda_error(e, "cudaMemcpyAsync(H2D)");
-  int rc = append_then_decode(pool, plan, layer, d_q, d_k, d_v, d_out, d_block_tables, bt_stride,
-                              scale, s);
+  }
+  // page-locked output: the kernels write it directly, no device copy and D2H
+  void* direct = mapped_host_ptr(h_out);
+  int rc = append_then_decode(pool, plan, layer, d_q, d_k, d_v, direct ? direct : d_out,
+                              d_block_tables, bt_stride, scale, s, nullptr, staged ? 1 : -1);
   if (rc) return rc;
-  if ((e = cudaMemcpyAsync(h_out, d_out, qb, cudaMemcpyDeviceToHost, s)))
-    return cuda_error(e, "cudaMemcpyAsync(D2H)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
-  return check_device_error("kvc_decode_host");
+  return finish_host_call(s, h_out, direct ? nullptr : d_out, qb, "kvc_decode_host");
 }
 
 // ============================================================================
@@ -965,13 +1042,12 @@ extern "C" int kvc_gqa_attention_cached(const void* h_Q, const void* h_K_new,
       (e = cudaMemcpyAsync(d_v, h_V_new, kb, cudaMemcpyHostToDevice, s)) ||
       (e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
     return cuda_error(e, "cudaMemcpyAsync(H2D)");
+  void* direct = mapped_host_ptr(h_Out);
   rc = cached_attend(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_q, d_k,
-                     d_v, d_out, layer_idx, q_len, start_pos, num_heads, scale, causal != 0, s);
+                     d_v, direct ? static_cast<uint8_t*>(direct) : d_out, layer_idx, q_len,
+                     start_pos, num_heads, scale, causal != 0, s);
   if (rc) return rc;
-  if ((e = cudaMemcpyAsync(h_Out, d_out, qb, cudaMemcpyDeviceToHost, s)))
-    return cuda_error(e, "cudaMemcpyAsync(D2H)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
-  return check_device_error("gqa_attention_cached");
+  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "gqa_attention_cached");
 }
 
 extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_new,
@@ -1016,8 +1092,7 @@ extern "C" int kvc_cache_gather(int layer_idx, int start, int count, void* h_K_o
   if ((e = cudaMemcpyAsync(h_K_out, d, rb, cudaMemcpyDeviceToHost, s)) ||
       (e = cudaMemcpyAsync(h_V_out, d + rb_al, rb, cudaMemcpyDeviceToHost, s)))
     return cuda_error(e, "cudaMemcpyAsync(D2H)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
-  return check_device_error("kv_cache_gather");
+  return finish_host_call(s, nullptr, nullptr, 0, "kv_cache_gather");
 }
 
 // Full-KV host attention (launch_gqa_attention_fp16, attention.hip:228-284): the
@@ -1074,11 +1149,10 @@ extern "C" int kvc_gqa_attention_ex(const void* h_Q, const void* h_K, const void
     return rc;
   rc = plan_queries(&C.plan, g, q_len, num_heads, start_pos, kv_len, causal != 0, device, s);
   if (rc) return rc;
-  if ((rc = do_decode(&C.pool, &C.plan, 0, d_q, d_out, bt, C.bt_len, scale, s))) return rc;
-  if ((e = cudaMemcpyAsync(h_Out, d_out, qb, cudaMemcpyDeviceToHost, s)))
-    return cuda_error(e, "cudaMemcpyAsync(D2H)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
-  return check_device_error("gqa_attention");
+  void* direct = mapped_host_ptr(h_Out);
+  if ((rc = do_decode(&C.pool, &C.plan, 0, d_q, direct ? direct : d_out, bt, C.bt_len, scale, s)))
+    return rc;
+  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "gqa_attention");
 }
 
 extern "C" int kvc_gqa_attention(const void* h_Q, const void* h_K, const void* h_V, void* h_Out,

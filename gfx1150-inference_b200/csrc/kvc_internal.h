@@ -183,15 +183,27 @@ inline int merge_warps_per_head(int max_splits) {
   return max_splits <= 8 ? 1 : max_splits <= 16 ? 2 : max_splits <= 32 ? 4 : max_splits <= 64 ? 8 : 16;
 }
 
+// Copy of up to three host-mapped (page-locked) input buffers into device
+// staging, 16 bytes per thread, by a kernel that lets the next launch (the
+// decode, a programmatic dependent) start streaming KV while the copy runs.
+// Every pointer is 16-byte aligned.
+struct StageArgs {
+  const uint8_t* src[3];
+  uint8_t* dst[3];
+  size_t bytes[3];
+};
+
 // Launchers: return cudaSuccess or the launch error.
 cudaError_t launch_append(const AppendArgs& a, int elem_size, cudaStream_t s);
 cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
+cudaError_t launch_stage_inputs(const StageArgs& a, cudaStream_t s);
 cudaError_t launch_fill_normal(const FillArgs& a, cudaStream_t s);
 // kind: 0 = tensor-core kernel, 1 = CUDA-core kernel (selected by the host).
 cudaError_t launch_decode(const DecodeArgs& a, int dtype, int layout, cudaStream_t s);
 bool decode_uses_mma(int dtype, int head_dim, int page_size);
 
-// Device error word (per device): read and optionally clear.
+// Device error word (per device): read and optionally clear; its device address.
 cudaError_t read_device_error(uint32_t* code, uint32_t* info, bool clear);
+cudaError_t device_error_address(void** p);
 
 }  // namespace kvc

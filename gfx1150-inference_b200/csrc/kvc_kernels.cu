@@ -44,6 +44,8 @@ __device__ __forceinline__ void report_error(uint32_t code, uint32_t info) {
   if (atomicCAS(&g_kvc_deverr[0], 0u, code) == 0u) g_kvc_deverr[1] = info;
 }
 
+cudaError_t device_error_address(void** p) { return cudaGetSymbolAddress(p, g_kvc_deverr); }
+
 cudaError_t read_device_error(uint32_t* code, uint32_t* info, bool clear) {
   uint32_t w[2] = {0, 0};
   cudaError_t e = cudaMemcpyFromSymbol(w, g_kvc_deverr, sizeof(w));
@@ -135,6 +137,34 @@ cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s) {
   const size_t total = static_cast<size_t>(a.count) * a.num_kv_heads * a.row_units;
   if (total == 0) return cudaSuccess;
   gather_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// =====================================================================================
+// Input staging for the host-buffer entry points: q and the new K/V rows are read
+// straight from page-locked host memory (over PCIe) into device staging.  The
+// kernel triggers its dependents first, so the decode launched behind it streams
+// KV from HBM while the inputs cross the host link; the decode reads them only
+// after griddepcontrol.wait.
+// =====================================================================================
+__global__ void __launch_bounds__(256) stage_inputs_kernel(const StageArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    const size_t n16 = a.bytes[b] / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(a.src[b]);
+    uint4* dst = reinterpret_cast<uint4*>(a.dst[b]);
+    for (size_t i = t0; i < n16; i += stride) dst[i] = src[i];
+    for (size_t i = n16 * 16 + t0; i < a.bytes[b]; i += stride) a.dst[b][i] = a.src[b][i];
+  }
+}
+
+cudaError_t launch_stage_inputs(const StageArgs& a, cudaStream_t s) {
+  const size_t n16 = (a.bytes[0] + a.bytes[1] + a.bytes[2]) / 16 + 1;
+  const unsigned grid = static_cast<unsigned>(std::min<size_t>(1184, (n16 + 255) / 256));
+  stage_inputs_kernel<<<grid, 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -333,9 +333,9 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
   if ((rc = plan_queries(&o->plan, o->slot.g, q_len, num_heads, start_pos, total, causal != 0,
                          o->device, s)))
     return rc;
-  if ((rc = do_decode(&o->slot, &o->plan, 0, d_q, d_out, bt, o->bt_len, scale, s))) return rc;
-  if ((e = cudaMemcpyAsync(h_Out, d_out, qb, cudaMemcpyDeviceToHost, s)))
-    return cuda_error(e, "cudaMemcpyAsync(out)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
-  return check_device_error("offload attend");
+  void* direct = mapped_host_ptr(h_Out);
+  if ((rc = do_decode(&o->slot, &o->plan, 0, d_q, direct ? direct : d_out, bt, o->bt_len, scale,
+                      s)))
+    return rc;
+  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "offload attend");
 }

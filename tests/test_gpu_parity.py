@@ -360,8 +360,11 @@ def test_append_decode_fused_equals_separate_and_host_call():
     assert torch.equal(o_fused, o_sep)
     hq, hk, hv = q.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
     ho = torch.zeros_like(hq).pin_memory()
-    pool.decode_host(plan, 1, hq, hk, hv, ho, bt, 0.088)
+    pool.decode_host(plan, 1, hq, hk, hv, ho, bt, 0.088)  # staged inputs, direct output
     assert torch.equal(ho, o_fused.cpu())
+    ho2 = torch.zeros_like(ho, pin_memory=False)
+    pool.decode_host(plan, 1, q.cpu(), kn.cpu(), vn.cpu(), ho2, bt, 0.088)  # pageable: copies
+    assert torch.equal(ho2, o_fused.cpu())
     # against the oracle, from the gathered pool contents
     for i, c in enumerate(ctx):
         k, v = pool.gather(1, bt, i, 0, c)
