@@ -63,6 +63,7 @@ struct kvc_plan {
   int n_sched_ctas = 0, n_units = 0;
   kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters, d_queue,
       d_sched_units, d_merge;
+  kvc::DevBuf d_rope;          // rotated q and new K rows (kvc_append_decode_rope)
   kvc::HostBuf h_stage;
   cudaEvent_t upload_done = nullptr;
 
@@ -77,6 +78,7 @@ struct kvc_plan {
     d_queue.release();
     d_sched_units.release();
     d_merge.release();
+    d_rope.release();
     h_stage.release();
     if (upload_done) cudaEventDestroy(upload_done);
     upload_done = nullptr;

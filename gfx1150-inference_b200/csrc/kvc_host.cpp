@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <queue>
 #include <string>
@@ -800,6 +801,135 @@ extern "C" int kvc_append_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int l
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return append_then_decode(pool, plan, layer, d_q, d_k_new, d_v_new, d_out, d_block_tables,
                             bt_stride, scale, s);
+}
+
+// ============================================================================
+// rotary position embedding (rope.hip:21-55, bindings.cpp:392-412)
+// ============================================================================
+namespace kvc {
+
+void rope_inv_freq(float freq_base, int head_dim, float* out) {
+  for (int i = 0; i < head_dim / 2; ++i)
+    out[i] = 1.0f / std::pow(freq_base, static_cast<float>(2 * i) / static_cast<float>(head_dim));
+}
+
+int check_rope_args(int num_heads, int head_dim, float freq_base) {
+  if (head_dim <= 0 || head_dim % 2 != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "head_dim must be a positive even integer for RoPE.");
+  if (head_dim / 2 > kMaxRopePairs)
+    return set_error(KVC_ERR_INVALID_ARG, "head_dim must be at most %d for RoPE.", 2 * kMaxRopePairs);
+  if (num_heads < 0) return set_error(KVC_ERR_INVALID_ARG, "num_heads must be non-negative.");
+  if (!(freq_base > 0.0f)) return set_error(KVC_ERR_INVALID_ARG, "freq_base must be positive.");
+  return KVC_OK;
+}
+
+}  // namespace kvc
+
+extern "C" int kvc_rope(const void* d_x, void* d_out, int n_tokens, int num_heads, int head_dim,
+                        const int32_t* d_positions, int pos_offset, float freq_base, int neox,
+                        int dtype, void* stream) {
+  int rc = check_rope_args(num_heads, head_dim, freq_base);
+  if (rc) return rc;
+  if (n_tokens < 0) return set_error(KVC_ERR_INVALID_ARG, "n_tokens must be non-negative.");
+  if (elem_size_of(dtype) == 0) return set_error(KVC_ERR_INVALID_ARG, "unknown dtype %d.", dtype);
+  if (n_tokens == 0 || num_heads == 0) return KVC_OK;
+  if (!d_x || !d_out) return set_error(KVC_ERR_INVALID_ARG, "x and out must not be null.");
+  RopeArgs a = {};
+  a.src[0] = static_cast<const uint8_t*>(d_x);
+  a.dst[0] = static_cast<uint8_t*>(d_out);
+  a.heads[0] = num_heads;
+  a.heads[1] = 0;
+  a.n_tokens = n_tokens;
+  a.head_dim = head_dim;
+  a.dtype = dtype;
+  a.neox = neox ? 1 : 0;
+  a.pos0 = pos_offset;
+  a.positions = d_positions;
+  rope_inv_freq(freq_base, head_dim, a.inv_freq);
+  cudaError_t e = launch_rope(a, static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess) return cuda_error(e, "rope kernel");
+  return KVC_OK;
+}
+
+namespace {
+struct RopeHostWs {
+  std::mutex mu;  // one process-wide workspace, like rope.hip's RoPEWorkspace
+  DevBuf buf;
+};
+RopeHostWs& rope_ws() {
+  static RopeHostWs ws;
+  return ws;
+}
+}  // namespace
+
+extern "C" int kvc_rope_host(const void* h_x, void* h_out, int seq_len, int num_heads, int head_dim,
+                             int pos_offset, float freq_base, int neox) {
+  int rc = check_rope_args(num_heads, head_dim, freq_base);
+  if (rc) return rc;
+  if (seq_len < 0) return set_error(KVC_ERR_INVALID_ARG, "seq_len must be non-negative.");
+  const size_t bytes = static_cast<size_t>(seq_len) * num_heads * head_dim * 2;
+  if (bytes == 0) return KVC_OK;
+  if (!h_x || !h_out) return set_error(KVC_ERR_INVALID_ARG, "x_in and x_out must not be null.");
+  RopeHostWs& ws = rope_ws();
+  std::lock_guard<std::mutex> lock(ws.mu);
+  const size_t al = (bytes + 255) & ~static_cast<size_t>(255);
+  cudaError_t e = ws.buf.ensure(2 * al);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(rope)");
+  uint8_t* d_in = static_cast<uint8_t*>(ws.buf.ptr);
+  uint8_t* d_out = d_in + al;
+  cudaStream_t s = nullptr;
+  if ((e = cudaMemcpyAsync(d_in, h_x, bytes, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpyAsync(H2D)");
+  if ((rc = kvc_rope(d_in, d_out, seq_len, num_heads, head_dim, nullptr, pos_offset, freq_base,
+                     neox, KVC_DTYPE_F16, s)))
+    return rc;
+  return finish_host_call(s, h_out, d_out, bytes, "rope");
+}
+
+extern "C" int kvc_append_decode_rope(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
+                                      const void* d_q, const void* d_k_new, const void* d_v_new,
+                                      void* d_out, const int32_t* d_block_tables, int bt_stride,
+                                      float scale, float freq_base, int neox, void* stream) {
+  if (!pool || !plan) return set_error(KVC_ERR_INVALID_ARG, "pool and plan must not be null.");
+  if (!plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
+  if (!d_q || !d_k_new || !d_v_new)
+    return set_error(KVC_ERR_INVALID_ARG, "q and the K/V rows must not be null.");
+  const PoolGeom& g = pool->g;
+  int rc = check_rope_args(plan->num_heads, g.head_dim, freq_base);
+  if (rc) return rc;
+  if (plan->n_queries == 0) return KVC_OK;
+  cudaSetDevice(pool->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  kvc_plan* p = const_cast<kvc_plan*>(plan);
+  const size_t n = static_cast<size_t>(plan->n_queries);
+  const size_t qb = n * plan->num_heads * g.head_dim * g.elem_size;
+  const size_t kb = n * g.num_kv_heads * g.head_dim * g.elem_size;
+  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
+  const size_t kb_al = (kb + 255) & ~static_cast<size_t>(255);
+  cudaError_t e = p->d_rope.ensure(qb_al + kb_al);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(rope staging)");
+  uint8_t* q_rot = static_cast<uint8_t*>(p->d_rope.ptr);
+  uint8_t* k_rot = q_rot + qb_al;
+  // q and the new K rows rotated at each query's own position (the plan's
+  // positions: ctx - 1 of a decode step), then the fused append + attention.  The
+  // rotation writes only this staging, so the decode behind it may stream KV
+  // while it runs.
+  RopeArgs a = {};
+  a.src[0] = static_cast<const uint8_t*>(d_q);
+  a.dst[0] = q_rot;
+  a.heads[0] = plan->num_heads;
+  a.src[1] = static_cast<const uint8_t*>(d_k_new);
+  a.dst[1] = k_rot;
+  a.heads[1] = g.num_kv_heads;
+  a.n_tokens = plan->n_queries;
+  a.head_dim = g.head_dim;
+  a.dtype = g.dtype;
+  a.neox = neox ? 1 : 0;
+  a.positions = static_cast<const int32_t*>(plan->d_pos.ptr);
+  rope_inv_freq(freq_base, g.head_dim, a.inv_freq);
+  if ((e = launch_rope(a, s, true)) != cudaSuccess) return cuda_error(e, "rope kernel");
+  return append_then_decode(pool, plan, layer, q_rot, k_rot, d_v_new, d_out, d_block_tables,
+                            bt_stride, scale, s, nullptr, 1);
 }
 
 extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,

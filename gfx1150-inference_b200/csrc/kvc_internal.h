@@ -193,10 +193,33 @@ struct StageArgs {
   size_t bytes[3];
 };
 
+// Rotary position embedding of up to two tensors (q and the new K rows) of
+// n_tokens tokens, (n_tokens, heads, D) each: the pair (i0, i1) of head h of
+// token t is rotated by angle positions[t] * inv_freq[i] (positions == nullptr:
+// pos0 + t), i0 = 2i, i1 = 2i + 1 (interleaved) or i0 = i, i1 = i + D/2 (NeoX),
+// in fp32, rounded to the storage type (the rope kernel of rope.hip:21-55).
+constexpr int kMaxRopePairs = 128;   // head_dim <= 256
+struct RopeArgs {
+  const uint8_t* src[2];
+  uint8_t* dst[2];
+  int heads[2];                      // 0: tensor absent
+  int n_tokens;
+  int head_dim;
+  int dtype;
+  int neox;
+  int pos0;
+  const int32_t* positions;
+  float inv_freq[kMaxRopePairs];
+};
+// Host table inv_freq[i] = 1 / freq_base^(2i / head_dim) in fp32 (rope.hip:79-83).
+void rope_inv_freq(float freq_base, int head_dim, float* out);
+
 // Launchers: return cudaSuccess or the launch error.
 cudaError_t launch_append(const AppendArgs& a, int elem_size, cudaStream_t s);
 cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
 cudaError_t launch_stage_inputs(const StageArgs& a, cudaStream_t s);
+// pdl: the rotation lets the next launch (a decode) start before it ends.
+cudaError_t launch_rope(const RopeArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_fill_normal(const FillArgs& a, cudaStream_t s);
 // kind: 0 = tensor-core kernel, 1 = CUDA-core kernel (selected by the host).
 cudaError_t launch_decode(const DecodeArgs& a, int dtype, int layout, cudaStream_t s);

@@ -169,6 +169,62 @@ cudaError_t launch_stage_inputs(const StageArgs& a, cudaStream_t s) {
 }
 
 // =====================================================================================
+// Rotary position embedding (rope.hip:21-55 semantics): one thread per rotation
+// pair.  As the staging step of the rotate + append + attend path it triggers its
+// dependents first, so the decode behind it streams KV while q and the new K rows
+// are rotated; the decode reads them only after griddepcontrol.wait.
+// =====================================================================================
+template <typename T>
+__global__ void __launch_bounds__(256) rope_kernel(const RopeArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int half = a.head_dim / 2;
+  const size_t n0 = static_cast<size_t>(a.n_tokens) * a.heads[0] * half;
+  const size_t n1 = static_cast<size_t>(a.n_tokens) * a.heads[1] * half;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n0 + n1;
+       idx += stride) {
+    const int b = idx < n0 ? 0 : 1;
+    const size_t r = b == 0 ? idx : idx - n0;
+    const int i = static_cast<int>(r % half);
+    const size_t th = r / half;                       // token * heads + head
+    const int t = static_cast<int>(th / a.heads[b]);
+    const int pos = a.positions ? a.positions[t] : a.pos0 + t;
+    const float angle = static_cast<float>(pos) * a.inv_freq[i];
+    float sn, cs;
+    sincosf(angle, &sn, &cs);
+    const int i0 = a.neox ? i : 2 * i;
+    const int i1 = a.neox ? i + half : 2 * i + 1;
+    const T* x = reinterpret_cast<const T*>(a.src[b]) + th * a.head_dim;
+    T* y = reinterpret_cast<T*>(a.dst[b]) + th * a.head_dim;
+    const float v0 = to_f32<T>(x[i0]), v1 = to_f32<T>(x[i1]);
+    y[i0] = from_f32<T>(v0 * cs - v1 * sn);
+    y[i1] = from_f32<T>(v0 * sn + v1 * cs);
+  }
+}
+
+cudaError_t launch_rope(const RopeArgs& a, cudaStream_t s, bool pdl) {
+  const size_t pairs =
+      static_cast<size_t>(a.n_tokens) * (a.heads[0] + a.heads[1]) * (a.head_dim / 2);
+  if (pairs == 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>(148 * 8, (pairs + 255) / 256)), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  switch (a.dtype) {
+    case 0: return cudaLaunchKernelEx(&cfg, rope_kernel<__half>, a);
+    case 1: return cudaLaunchKernelEx(&cfg, rope_kernel<__nv_bfloat16>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, rope_kernel<float>, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// =====================================================================================
 // Seeded normal fill (synthetic benchmark contents).  Counter-based: element i
 // of the pool always receives the same value for a given seed.
 // =====================================================================================

@@ -103,6 +103,11 @@ SIGNATURES = {
                                    ctypes.POINTER(ctypes.c_double),
                                    ctypes.POINTER(ctypes.c_int64),
                                    ctypes.POINTER(ctypes.c_int64)]),
+    "kvc_rope_host": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int]),
+    "kvc_rope": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_float, _c_int, _c_int,
+                          _vp]),
+    "kvc_append_decode_rope": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int,
+                                        _c_float, _c_float, _c_int, _vp]),
     "kvc_xchg_create": (_c_int, [_c_int, _c_int, _c_int, _c_size, _c_int, ctypes.POINTER(_vp)]),
     "kvc_xchg_handle": (_c_int, [_vp, _vp]),
     "kvc_xchg_connect": (_c_int, [_vp, _vp]),

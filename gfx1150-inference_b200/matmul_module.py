@@ -131,6 +131,18 @@ def gqa_attention(Q, K, V, Out, q_len: int, kv_len: int, num_heads: int, num_kv_
         int(bool(causal)), _ffi.dtype_code_of(dt)))
 
 
+def rope(x_in, x_out, seq_len: int, num_heads: int, head_dim: int, pos_offset: int = 0,
+         freq_base: float = 10000.0, neox_style: bool = False) -> None:
+    """Rotary Positional Embeddings (bindings.cpp:392-412, defaults :763-774) on
+    host fp16 arrays (seq_len, num_heads, head_dim); x_out may not alias x_in."""
+    total = int(seq_len) * int(num_heads) * int(head_dim)
+    x_in = _check_array(x_in, "x_in", total, np.dtype(np.float16))
+    x_out = _check_array(x_out, "x_out", total, np.dtype(np.float16), require_writeable=True)
+    _ffi.check(_ffi.lib.kvc_rope_host(_ffi.np_ptr(x_in), _ffi.np_ptr(x_out), int(seq_len),
+                                      int(num_heads), int(head_dim), int(pos_offset),
+                                      float(freq_base), int(bool(neox_style))))
+
+
 def kv_cache_gather(layer_idx: int, start: int, count: int):
     """Copy positions [start, start+count) of a layer out of the pool as
     (count, num_kv_heads, head_dim) K and V arrays (bit-exact pool checks)."""

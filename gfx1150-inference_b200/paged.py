@@ -172,6 +172,20 @@ class PagedKVCache:
             _dev(out, "out", self.dtype, n), _i32(block_tables), int(block_tables.shape[-1]),
             float(scale), _sp(stream)))
 
+    def append_decode_rope(self, plan: DecodePlan, layer: int, q: torch.Tensor,
+                           k_new: torch.Tensor, v_new: torch.Tensor, out: torch.Tensor,
+                           block_tables: torch.Tensor, scale: float, freq_base: float = 10000.0,
+                           neox: bool = False, stream=None):
+        """append_decode with q and k_new rotated (RoPE) at each query's position
+        first (kvc_append_decode_rope); q and k_new are not modified."""
+        n = plan.n_queries * plan.num_heads * self.head_dim
+        nk = plan.n_queries * self.num_kv_heads * self.head_dim
+        ffi.check(ffi.lib.kvc_append_decode_rope(
+            self.handle, plan.handle, layer, _dev(q, "q", self.dtype, n),
+            _dev(k_new, "k_new", self.dtype, nk), _dev(v_new, "v_new", self.dtype, nk),
+            _dev(out, "out", self.dtype, n), _i32(block_tables), int(block_tables.shape[-1]),
+            float(scale), float(freq_base), int(bool(neox)), _sp(stream)))
+
     def append_decode_xchg(self, plan: DecodePlan, layer: int, q: torch.Tensor,
                            k_new: Optional[torch.Tensor], v_new: Optional[torch.Tensor],
                            xchg_handle, slot: int, total_heads: int, head_offset: int,
@@ -222,6 +236,24 @@ class PagedKVCache:
 
 
 # -- layout helpers -------------------------------------------------------------------
+def rope(x: torch.Tensor, out: torch.Tensor, positions: Optional[torch.Tensor] = None,
+         pos_offset: int = 0, freq_base: float = 10000.0, neox: bool = False, stream=None):
+    """Rotary position embedding of x (tokens, heads, D) into out on the GPU
+    (kvc_rope); token t at positions[t] (int32 CUDA tensor) or pos_offset + t."""
+    if x.dim() != 3:
+        raise ValueError("x must be (tokens, heads, head_dim)")
+    n, heads, d = x.shape
+    dt = _TORCH_CODE.get(x.dtype)
+    if dt is None:
+        raise ValueError(f"unsupported dtype {x.dtype}")
+    xp = _dev(x, "x", x.dtype, n * heads * d)
+    op = _dev(out, "out", x.dtype, n * heads * d)
+    pp = None if positions is None else _i32(positions)
+    ffi.check(ffi.lib.kvc_rope(xp, op, n, heads, d, pp, int(pos_offset), float(freq_base),
+                               int(bool(neox)), dt, _sp(stream)))
+    return out
+
+
 def pages_for(ctx_lens: Sequence[int], page_size: int) -> np.ndarray:
     return np.array([(int(c) + page_size - 1) // page_size for c in ctx_lens], dtype=np.int64)
 

@@ -255,6 +255,32 @@ KVC_API int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, int
 KVC_API int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_tables, int bt_stride,
                int row, int start, int count, void* d_k_out, void* d_v_out, void* stream);
 
+/* ---- rotary position embedding ------------------------------------------------ */
+
+/* The reference's `rope` (bindings.cpp:392-412, rope.hip:21-55 and :154-200) on
+ * host fp16 arrays (seq_len, num_heads, head_dim), synchronous: the pair (i0, i1)
+ * of every head of token t rotated by (pos_offset + t) / freq_base^(2i/head_dim),
+ * i0 = 2i, i1 = 2i + 1, or i0 = i, i1 = i + head_dim/2 when neox != 0; fp32
+ * math, fp16 result.  head_dim must be a positive even number <= 256. */
+KVC_API int kvc_rope_host(const void* h_x, void* h_out, int seq_len, int num_heads, int head_dim,
+                          int pos_offset, float freq_base, int neox);
+/* The same on device buffers (fp16, bf16 or fp32 by `dtype`) on `stream`;
+ * token t's position is d_positions[t] (int32, device) or, when d_positions is
+ * null, pos_offset + t.  No counterpart in the reference for the per-token
+ * positions (a batch of sequences each at its own position). */
+KVC_API int kvc_rope(const void* d_x, void* d_out, int n_tokens, int num_heads, int head_dim,
+                     const int32_t* d_positions, int pos_offset, float freq_base, int neox,
+                     int dtype, void* stream);
+/* kvc_append_decode with q and the new K rows rotated first, each query at its
+ * plan position (ctx - 1): the rope + append + attend of one decode step
+ * (layer.py:291-298 followed by kv_cache.py:240-256) as one launch chain.  The
+ * rotation runs as a programmatic dependent ahead of the decode, which streams
+ * KV meanwhile.  d_q / d_k_new are read, not modified. */
+KVC_API int kvc_append_decode_rope(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
+                                   const void* d_q, const void* d_k_new, const void* d_v_new,
+                                   void* d_out, const int32_t* d_block_tables, int bt_stride,
+                                   float scale, float freq_base, int neox, void* stream);
+
 /* ==== 3. Host-streamed offload (--offload-kv-cpu / --kv-mmap-dir) ========== */
 
 typedef struct kvc_offload kvc_offload_t;

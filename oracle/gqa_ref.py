@@ -21,10 +21,16 @@ Restatements of the reference's own CPU code for this path
   (attention.hip:115).
 * ``append_rows`` — the host-mode append of KVCacheManager.attend
   (src/kv_cache.py:222-225): plain slice assignment into (L, S, Hkv, D) arrays.
+* ``ref_rope`` — tests/test_layer.py:44-73, the numpy oracle of the reference's
+  rope kernel (src/kernels/rope.hip:21-55): fp32 inv_freq = 1 / base^(2i/D),
+  angle = position * inv_freq, pairs (2i, 2i+1) or (i, i+D/2) for NeoX, result
+  cast to fp16.  ``positions`` extends it to one position per token (a batch of
+  sequences at different positions), which the reference has no call for.
 
-Pinning: tests/test_oracle_golden.py checks ``ref_gqa_attention`` and
-``online_softmax_attention`` against golden vectors produced by importing the
-reference's own ``ref_gqa_attention`` (tests/golden/make_golden.py).
+Pinning: tests/test_oracle_golden.py checks ``ref_gqa_attention``,
+``online_softmax_attention`` and ``ref_rope`` against golden vectors produced by
+importing the reference's own ``ref_gqa_attention`` and ``ref_rope``
+(tests/golden/make_golden.py).
 """
 
 from __future__ import annotations
@@ -108,3 +114,54 @@ def batched_decode(q, ks, vs, ctx_lens, scale: float, out_dtype=np.float32) -> n
         out[i] = ref_gqa_attention(q[i:i + 1], ks[i][:c], vs[i][:c], start_pos=c - 1,
                                    scale=scale, causal=True, out_dtype=np.float32)[0]
     return out.astype(out_dtype)
+
+
+def ref_rope(x, pos_offset: int = 0, freq_base: float = 10000.0, neox_style: bool = False,
+             positions=None, out_dtype=np.float16, inv_freq=None) -> np.ndarray:
+    """tests/test_layer.py:44-73 restated; x (tokens, heads, D).  Token t sits at
+    positions[t] when given, else pos_offset + t.  ``inv_freq`` replaces the
+    numpy power table (e.g. with the libm ``powf`` table rope.hip:79-83 builds on
+    the host: the two differ by an ulp in some entries, which a large position
+    turns into a visible angle difference)."""
+    n, heads, head_dim = x.shape
+    half = head_dim // 2
+    xf = x.astype(np.float32)
+    i = np.arange(half, dtype=np.float32)
+    if inv_freq is None:
+        inv_freq = np.float32(1.0) / (np.float32(freq_base) ** (np.float32(2.0) * i / np.float32(head_dim)))
+    inv_freq = np.asarray(inv_freq, dtype=np.float32)
+    if positions is None:
+        pos = np.arange(pos_offset, pos_offset + n, dtype=np.float32)
+    else:
+        pos = np.asarray(positions, dtype=np.float32)
+    ang = pos[:, None] * inv_freq[None, :]
+    cs = np.cos(ang)[:, None, :]
+    sn = np.sin(ang)[:, None, :]
+    if neox_style:
+        v0, v1 = xf[:, :, :half], xf[:, :, half:]
+    else:
+        v0, v1 = xf[:, :, 0::2], xf[:, :, 1::2]
+    r0 = v0 * cs - v1 * sn
+    r1 = v0 * sn + v1 * cs
+    out = np.empty_like(xf)
+    if neox_style:
+        out[:, :, :half], out[:, :, half:] = r0, r1
+    else:
+        out[:, :, 0::2], out[:, :, 1::2] = r0, r1
+    return out.astype(out_dtype)
+
+
+def libm_inv_freq(freq_base: float, head_dim: int) -> np.ndarray:
+    """inv_freq[i] = 1 / powf(freq_base, 2i / head_dim) with the C library's powf,
+    the host table of rope.hip:79-83."""
+    import ctypes
+    import ctypes.util
+
+    libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+    libm.powf.restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    out = np.empty(head_dim // 2, dtype=np.float32)
+    for i in range(head_dim // 2):
+        e = np.float32(np.float32(2 * i) / np.float32(head_dim))
+        out[i] = np.float32(1.0) / np.float32(libm.powf(float(freq_base), float(e)))
+    return out

@@ -112,3 +112,21 @@ def ragged_case():
 
 def load_golden():
     return dict(np.load(GOLDEN_FILE, allow_pickle=False))
+
+
+def rope_cases():
+    """tests/test_layer.py:134-152: seed 20, 16 heads x 64, N(0,1) fp16, interleaved
+    and NeoX, (seq 8, offset 0) and (seq 1, offset 17); plus long-context decode
+    positions (one token at 4095, 32768, 131072) and head_dim 128 (seed 21)."""
+    out = []
+    rng = np.random.default_rng(20)
+    for neox in (False, True):
+        for seq_len, pos in [(8, 0), (1, 17)]:
+            x = _draw(rng, (seq_len, 16, 64), 1.0, np.float16)
+            out.append(dict(x=x, pos_offset=pos, freq_base=10000.0, neox=neox))
+    rng = np.random.default_rng(21)
+    for neox in (False, True):
+        for pos, base in [(4095, 10000.0), (32768, 500000.0), (131072, 500000.0)]:
+            x = _draw(rng, (1, 8, 128), 1.0, np.float16)
+            out.append(dict(x=x, pos_offset=pos, freq_base=base, neox=neox))
+    return out

@@ -4,7 +4,8 @@ Usage:  PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference
 
 <checkout> is a gfx1150-inference source tree.  This script imports its
 ``tests/test_layer.py`` and calls its ``ref_gqa_attention`` (test_layer.py:
-76-105) on the inputs of tests/golden/cases.py.  Importing that module pulls
+76-105) and ``ref_rope`` (test_layer.py:44-73) on the inputs of
+tests/golden/cases.py.  Importing that module pulls
 in ``layer`` / ``kv_cache``, which import the native ``matmul_module``; a stub
 namespace stands in for it (the same trick as the reference's own CPU suite,
 tests/test_cpu_only.py:391-400), since no attention kernel is called.
@@ -51,14 +52,14 @@ def load_reference_oracle(ref_root: str):
     ref = test_layer.ref_gqa_attention
     ref_f32 = types.FunctionType(ref.__code__, dict(ref.__globals__, np=_NpNoHalf()),
                                  "ref_gqa_attention_f32", ref.__defaults__)
-    return ref, ref_f32
+    return ref, ref_f32, test_layer.ref_rope
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="gfx1150-inference source checkout")
     args = ap.parse_args()
-    ref, ref_f32 = load_reference_oracle(os.path.abspath(args.reference))
+    ref, ref_f32, ref_rope = load_reference_oracle(os.path.abspath(args.reference))
     g = {}
 
     for i, c in enumerate(cases.layer_cases()):
@@ -96,6 +97,11 @@ def main():
     g["ragged_out"] = np.concatenate([
         ref(c["q"][i:i + 1], c["ks"][i], c["vs"][i], start_pos=n - 1, scale=c["scale"])
         for i, n in enumerate(c["ctx"])])
+
+    for i, c in enumerate(cases.rope_cases()):
+        g[f"rope{i}_digest"] = np.array(cases.digest(c["x"]))
+        g[f"rope{i}_out"] = ref_rope(c["x"], pos_offset=c["pos_offset"], freq_base=c["freq_base"],
+                                     neox_style=c["neox"])
 
     np.savez_compressed(cases.GOLDEN_FILE, **g)
     print(f"wrote {cases.GOLDEN_FILE}: {len(g)} arrays, "

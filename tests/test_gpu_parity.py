@@ -426,3 +426,96 @@ def test_bad_block_table_is_reported_and_context_survives():
     torch.cuda.synchronize()
     assert ffi.device_error(0, clear=True) == (0, 0)
     assert torch.isfinite(out).all()
+
+
+# ---- rotary position embedding (rope.hip:21-55; ref_rope, test_layer.py:44-73) --------
+def _rope_bound(x, pos):
+    """2e-3 (the reference's own rope test, test_layer.py:145-150) plus what an ulp
+    of difference in one inv_freq entry (numpy's float32 power vs the libm powf
+    table rope.hip:79-83 builds) makes of the angle at position pos."""
+    return 2e-3 + 2.0 * float(np.max(np.abs(x.astype(np.float32)))) * pos * 2.0 ** -23
+
+
+def test_rope_host_matches_reference_golden():
+    """matmul_module.rope vs the reference's ref_rope outputs (positions up to
+    131072), and vs the oracle on the same libm inv_freq table within the
+    reference test's 2e-3 at every position."""
+    import matmul_module
+
+    for i, c in enumerate(cases.rope_cases()):
+        x = c["x"]
+        out = np.zeros_like(x)
+        matmul_module.rope(x, out, x.shape[0], x.shape[1], x.shape[2], c["pos_offset"],
+                           c["freq_base"], c["neox"])
+        last = c["pos_offset"] + x.shape[0] - 1
+        err = _maxerr(out, G[f"rope{i}_out"])
+        assert err < _rope_bound(x, last), (i, err)
+        same_table = gqa_ref.ref_rope(x, pos_offset=c["pos_offset"], neox_style=c["neox"],
+                                      inv_freq=gqa_ref.libm_inv_freq(c["freq_base"], x.shape[2]))
+        err = _maxerr(out, same_table)
+        assert err < 2e-3, (i, err)
+    with pytest.raises(ValueError):
+        matmul_module.rope(np.zeros((1, 2, 7), np.float16), np.zeros((1, 2, 7), np.float16),
+                           1, 2, 7)
+    with pytest.raises(ValueError):
+        matmul_module.rope(np.zeros((1, 2, 8), np.float32), np.zeros((1, 2, 8), np.float16),
+                           1, 2, 8)
+
+
+def test_rope_device_per_token_positions_and_dtypes():
+    rng = np.random.default_rng(5)
+    pos = np.array([0, 1, 4095, 32768, 131072, 7], dtype=np.int32)
+    for neox in (False, True):
+        x = rng.standard_normal((len(pos), 8, 128), dtype=np.float32).astype(np.float16)
+        table = gqa_ref.libm_inv_freq(500000.0, 128)
+        ref = gqa_ref.ref_rope(x, neox_style=neox, positions=pos, inv_freq=table)
+        xt = torch.from_numpy(x).cuda()
+        out = torch.empty_like(xt)
+        paged.rope(xt, out, positions=torch.from_numpy(pos).cuda(), freq_base=500000.0, neox=neox)
+        assert _maxerr(out.cpu().numpy(), ref) < 2e-3
+        ref32 = gqa_ref.ref_rope(x.astype(np.float32), neox_style=neox, positions=pos,
+                                 out_dtype=np.float32, inv_freq=table)
+        x32 = xt.float()
+        o32 = torch.empty_like(x32)
+        paged.rope(x32, o32, positions=torch.from_numpy(pos).cuda(), freq_base=500000.0, neox=neox)
+        assert _maxerr(o32.cpu().numpy(), ref32) < 1e-4
+
+
+def test_append_decode_rope_equals_rope_then_append_decode():
+    """The fused rotate + append + attend chain == kvc_rope of q and k at the plan
+    positions followed by kvc_append_decode, bit for bit; the pool holds the
+    rotated K row; and the output matches the oracle on the rotated inputs."""
+    rng = np.random.default_rng(14)
+    H, Hkv, D, ps = 32, 8, 128, 16
+    ctx = [700, 1, 2049, 33]
+    for neox in (False, True):
+        table, total = paged.random_block_tables(ctx, ps, 6)
+        pools = [paged.PagedKVCache(1, total, ps, Hkv, D) for _ in range(2)]
+        for p in pools:
+            p.fill_normal(seed=3)
+        bt = torch.from_numpy(table).cuda()
+        n = len(ctx)
+        q = torch.from_numpy(rng.standard_normal((n, H, D), dtype=np.float32)).half().cuda()
+        kn = torch.from_numpy(rng.standard_normal((n, Hkv, D), dtype=np.float32)).half().cuda()
+        vn = torch.from_numpy(rng.standard_normal((n, Hkv, D), dtype=np.float32)).half().cuda()
+        plans = [p.plan(ctx, H) for p in pools]
+        o1 = torch.zeros_like(q)
+        pools[0].append_decode_rope(plans[0], 0, q, kn, vn, o1, bt, 0.088, 500000.0, neox)
+        pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32, device="cuda")
+        qr, kr = torch.empty_like(q), torch.empty_like(kn)
+        paged.rope(q, qr, positions=pos, freq_base=500000.0, neox=neox)
+        paged.rope(kn, kr, positions=pos, freq_base=500000.0, neox=neox)
+        o2 = torch.zeros_like(q)
+        pools[1].append_decode(plans[1], 0, qr, kr, vn, o2, bt, 0.088)
+        torch.cuda.synchronize()
+        assert torch.equal(o1, o2)
+        for i, c in enumerate(ctx):
+            k, v = pools[0].gather(0, bt, i, 0, c)
+            assert torch.equal(k[c - 1], kr[i]) and torch.equal(v[c - 1], vn[i])
+            ref = gqa_ref.ref_gqa_attention(qr[i:i + 1].cpu().numpy(), k.cpu().numpy(),
+                                            v.cpu().numpy(), c - 1, 0.088)
+            assert _maxerr(o1[i:i + 1].cpu().numpy(), ref) <= _fp16_tol(ref)
+        # rotated q/k against the oracle rotation
+        ref_k = gqa_ref.ref_rope(kn.cpu().numpy(), neox_style=neox, positions=pos.cpu().numpy(),
+                                 inv_freq=gqa_ref.libm_inv_freq(500000.0, D))
+        assert _maxerr(kr.cpu().numpy(), ref_k) < 2e-3

@@ -1,6 +1,6 @@
 """Pin the CPU oracle (oracle/) to the reference's own outputs (CPU only).
 
-The golden file holds outputs of the reference's ``ref_gqa_attention``
+The golden file holds outputs of the reference's ``ref_gqa_attention`` and ``ref_rope``
 (tests/test_layer.py:76-105 of gfx1150-inference), produced by
 tests/golden/make_golden.py.  Every oracle used by the GPU tests must agree
 with it before it is trusted as a checker.
@@ -136,3 +136,18 @@ def test_append_rows_is_slice_assignment():
     gqa_ref.append_rows(k, v, 1, 4, rows, -rows)
     assert np.array_equal(k[1, 4:7], rows) and np.array_equal(v[1, 4:7], -rows)
     assert not k[0].any() and not k[1, :4].any() and not k[1, 7:].any()
+
+
+def test_rope_restatement_matches_reference():
+    """gqa_ref.ref_rope against the reference's ref_rope outputs (test_layer.py:44-73):
+    bit for bit on every case, including positions up to 131072."""
+    for i, c in enumerate(cases.rope_cases()):
+        assert cases.digest(c["x"]) == str(G[f"rope{i}_digest"])
+        got = gqa_ref.ref_rope(c["x"], pos_offset=c["pos_offset"], freq_base=c["freq_base"],
+                               neox_style=c["neox"])
+        np.testing.assert_array_equal(got, G[f"rope{i}_out"], err_msg=f"case {i}")
+        # per-token positions: the same rotation when they equal pos_offset + t
+        pos = np.arange(c["pos_offset"], c["pos_offset"] + c["x"].shape[0])
+        again = gqa_ref.ref_rope(c["x"], freq_base=c["freq_base"], neox_style=c["neox"],
+                                 positions=pos)
+        np.testing.assert_array_equal(again, got)
