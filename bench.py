@@ -55,6 +55,7 @@ CONFIGS = {
               lens=("fixed", 131072), seed=5),
 }
 PAGE = 16
+ROPE_BASE = 500000.0  # Llama-3 rope_freq_base (only with --rope)
 
 
 def cached_lengths(cfg):
@@ -301,7 +302,11 @@ def run_b200(args, rank, world, local_rank):
         for l in range(L):
             if events is not None:
                 events[l][0].record(s)
-            if gathered is None:
+            if gathered is None and args.rope:
+                # rotate q and the new K row (RoPE at each sequence's position) first
+                pool.append_decode_rope(plan, l, q[l], kn[l], vn[l], out[l], bt, scale,
+                                        ROPE_BASE, False, stream=s)
+            elif gathered is None:
                 pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=s)
             else:
                 # fused append + attention on this rank's heads; p2p: the merge kernel
@@ -476,6 +481,7 @@ def run_b200(args, rank, world, local_rank):
             "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * args.page_size * D * 2 / 1e9, 2),
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
+            "rope": bool(args.rope),
             "launch": ("one CUDA graph replay per step (the step's 2 x layers kernel launches)"
                        if used_graph else "direct launches from the host loop"),
             "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), "
@@ -500,7 +506,7 @@ def run_b200(args, rank, world, local_rank):
         # per layer: the decode kernel and its split merge (PDL); with the p2p head
         # exchange the merge also pushes the outputs and a one-warp kernel
         # publishes and waits for the peers' epochs
-        "gpu_launches": (3 if hsd_p2p else 2) * L * args.steps,
+        "gpu_launches": (3 if hsd_p2p or (args.rope and gathered is None) else 2) * L * args.steps,
         "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
     }
     if e2e:
@@ -667,6 +673,8 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="3")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
+    ap.add_argument("--rope", action="store_true",
+                    help="rotate q and the new K rows (RoPE) inside the step (rope + append + attend)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every kernel from the host loop instead of replaying a CUDA graph")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
