@@ -265,6 +265,14 @@ def run_b200(args, rank, world, local_rank):
         h0, h1 = paged.shard_heads(Hkv, world, rank)
         Hkv = h1 - h0
         H = H * Hkv // cfg["Hkv"]
+    one_rank_of = args.one_rank_of if world == 1 else 0
+    if one_rank_of > 1:
+        # profiling mode: rank 0's shard of a one_rank_of-way KV-head split on this one
+        # GPU, its head exchange connected to itself (same kernels and launches as a
+        # real rank, no peers to wait for)
+        h0, h1 = paged.shard_heads(Hkv, one_rank_of, 0)
+        Hkv = h1 - h0
+        H = H * Hkv // cfg["Hkv"]
     cached = cached_lengths(cfg)
     ctx = cached + 1                                  # context includes the appended token
     table, total_pages = paged.random_block_tables(ctx, args.page_size, cfg["seed"] + 17 * rank)
@@ -286,6 +294,14 @@ def run_b200(args, rank, world, local_rank):
         gathered = torch.empty((L, B, H_full, D), dtype=torch.float16, device=dev)
         hsd = sharding.HeadShardedDecode(pool, H_full, cfg["Hkv"], transport=args.xchg,
                                          num_queries=B)
+    self_xchg = None
+    if one_rank_of > 1:
+        self_xchg = ctypes.c_void_p()
+        ffi.check(ffi.lib.kvc_xchg_create(local_rank, 0, 1, B * H_full * D * 2, 2,
+                                          ctypes.byref(self_xchg)))
+        base = ctypes.c_void_p()
+        ffi.check(ffi.lib.kvc_xchg_base(self_xchg, ctypes.byref(base)))
+        ffi.check(ffi.lib.kvc_xchg_connect_ptrs(self_xchg, (ctypes.c_void_p * 1)(base.value)))
     pos = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
     rows = torch.arange(B, dtype=torch.int32, device=dev)
     scale = 1.0 / math.sqrt(D)
@@ -302,7 +318,10 @@ def run_b200(args, rank, world, local_rank):
         for l in range(L):
             if events is not None:
                 events[l][0].record(s)
-            if gathered is None and args.rope:
+            if self_xchg is not None:
+                pool.append_decode_xchg(plan, l, q[l], kn[l], vn[l], self_xchg, l & 1, H_full, 0,
+                                        bt, scale, stream=s)
+            elif gathered is None and args.rope:
                 # rotate q and the new K row (RoPE at each sequence's position) first
                 pool.append_decode_rope(plan, l, q[l], kn[l], vn[l], out[l], bt, scale,
                                         ROPE_BASE, False, stream=s)
@@ -362,7 +381,7 @@ def run_b200(args, rank, world, local_rank):
         torch.distributed.barrier()
     elapsed_ms = t_start.elapsed_time(t_stop)
     used_graph = graph is not None
-    hsd_p2p = gathered is not None and args.xchg == "p2p"
+    hsd_p2p = (gathered is not None and args.xchg == "p2p") or self_xchg is not None
     if graph is not None:
         graph.reset()  # released before any collective teardown (it may hold NCCL calls)
         graph = None
@@ -445,6 +464,9 @@ def run_b200(args, rank, world, local_rank):
 
     if gathered is not None:
         hsd.close()  # collective: the exchange buffers are freed after every rank is done
+    if self_xchg is not None:
+        torch.cuda.synchronize()
+        ffi.lib.kvc_xchg_destroy(self_xchg)
 
     if rank != 0:
         return None
@@ -472,7 +494,9 @@ def run_b200(args, rank, world, local_rank):
         "data": "synthetic: seeded N(0,1) K/V/q, random page permutation",
         "config": {
             "workload": f"{cfg['workload']} (BASELINE config {args.config})"
-                        + (f" [profiling subset: {L} layers]" if args.layers else ""),
+                        + (f" [profiling subset: {L} layers]" if args.layers else "")
+                        + (f" [profiling: one rank's shard of a {one_rank_of}-way KV-head split, "
+                           "exchange connected to itself]" if one_rank_of > 1 else ""),
             "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D,
             "sequences_per_gpu": B, "global_batch": B if gathered is not None else B * world,
             "cached_len": (f"U[{cfg['lens'][1]},{cfg['lens'][2]}] seed {cfg['seed']}"
@@ -675,6 +699,9 @@ def main():
     ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
     ap.add_argument("--rope", action="store_true",
                     help="rotate q and the new K rows (RoPE) inside the step (rope + append + attend)")
+    ap.add_argument("--one-rank-of", type=int, default=0,
+                    help="profiling on one GPU: run rank 0's shard of an N-way KV-head split "
+                         "with its head exchange connected to itself")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every kernel from the host loop instead of replaying a CUDA graph")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",
