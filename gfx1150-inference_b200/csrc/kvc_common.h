@@ -52,7 +52,7 @@ struct kvc_plan {
   int device = -1;
   int n_queries = 0, n_items = 0, n_slots = 0;
   int num_heads = 0, num_kv_heads = 0, group = 0, n_hchunk = 0;
-  int head_dim = 0, page_size = 0, max_ctx = 0, max_splits = 0;
+  int head_dim = 0, page_size = 0, max_ctx = 0, max_splits = 0, split_tokens = 0;
   bool rows_distinct = true;   // every query has its own block-table row
   int flags = 0;               // KVC_PLAN_*
   kvc::PoolGeom pool_geom;

@@ -426,6 +426,17 @@ namespace kvc {
 // counts of the batch, so the same call always gets the same partition (the
 // resident and offloaded paths agree bit for bit).  KVC_SPLIT_TOKENS overrides
 // it for tuning.
+int l2_ahead_slabs(int split_tokens) {
+  static int forced = [] {
+    const char* e = getenv("KVC_L2_AHEAD");
+    if (!e) return -1;
+    const int x = atoi(e);
+    return x < 0 ? 0 : (x > 32 ? 32 : x);
+  }();
+  if (forced >= 0) return forced;
+  return split_tokens >= kL2AheadMinSplit ? kL2AheadSlabs : 0;
+}
+
 int split_tokens_for(int page_size) {
   static int base = [] {
     const char* e = getenv("KVC_SPLIT_TOKENS");
@@ -560,6 +571,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->page_size = g.page_size;
   p->max_ctx = max_ctx;
   p->max_splits = max_splits;
+  p->split_tokens = C;
   p->device = device;
   {
     std::vector<int32_t> r(p->rows);
@@ -665,6 +677,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.queue = static_cast<unsigned*>(plan->d_queue.ptr);
   a.n_sched_ctas = plan->n_sched_ctas;
   a.early_prefetch = early >= 0 ? early : ((plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0);
+  a.l2_ahead = l2_ahead_slabs(plan->split_tokens);
   a.merge_queries = static_cast<const int32_t*>(plan->d_merge.ptr);
   a.n_merge_queries = static_cast<int>(plan->merge_queries.size());
   a.k_new = static_cast<const uint8_t*>(d_k_new);

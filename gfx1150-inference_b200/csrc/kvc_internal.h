@@ -51,6 +51,14 @@ constexpr int kSplitTokens = 512;
 constexpr int kMaxSplitPages = 64;
 // Warps per CTA of the persistent decode kernel (one CTA per SM).
 constexpr int kPersistWarps = 8;
+// Slabs per warp brought into L2 while a decode launch waits for the preceding
+// kernel (early KV streaming only), for plans whose splits are at least
+// kL2AheadMinSplit positions long; KVC_L2_AHEAD overrides (0 ... 32).  Measured
+// on B200: +1.9 % for one rank of an 8-way KV-head split of config 4 (224-position
+// splits), +0.5 % config 4, neutral config 3; 7 % slower for config 2's
+// 112-position splits, hence the threshold; deeper prefetch was slower everywhere.
+constexpr int kL2AheadSlabs = 2;
+constexpr int kL2AheadMinSplit = 192;
 // Ranks a head exchange can span (one process per GPU of one node).
 constexpr int kMaxPeers = 8;
 
@@ -137,6 +145,7 @@ struct DecodeArgs {
   // (plan flag KVC_PLAN_KV_STABLE): the decode kernel may start streaming them
   // before that kernel's results are visible.
   int early_prefetch;
+  int l2_ahead = 0;              // slabs per warp prefetched into L2 before the wait
   // queries with more than one split (merged by merge_splits_kernel)
   const int32_t* merge_queries;
   int n_merge_queries;

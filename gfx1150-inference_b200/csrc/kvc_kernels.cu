@@ -606,6 +606,23 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
 #pragma unroll 1
   for (int k = 0; k < NS; ++k) p_issue();
   if (!dep_ready) {
+    // Still waiting for the preceding kernel (its merge, or the head exchange):
+    // use the wait to bring the next l2_ahead slabs of this unit into L2, so
+    // HBM streams during the wait and the ring later refills from L2.
+    const int j = p_j + lane;
+    const int idx = j / spp - p_pg0;
+    const int v0 = __shfl_sync(0xffffffffu, p_page0, idx & 31);
+    const int v1 = __shfl_sync(0xffffffffu, p_page1, idx & 31);
+    if (lane < a.l2_ahead && p_pos < n_units && j < p_end && p_r0.w > p_r0.z) {
+      const int phys = idx < 32 ? v0 : v1;
+      if (phys >= 0) {
+        const size_t off = static_cast<size_t>(phys) * page_stride +
+                           static_cast<size_t>(p_r2.x) * ps * D * 2 +
+                           static_cast<size_t>(j % spp) * SLAB_BYTES;
+        bulk_prefetch_l2(a.k_layer + off, SLAB_BYTES);
+        bulk_prefetch_l2(a.v_layer + off, SLAB_BYTES);
+      }
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     dep_ready = true;
   }
