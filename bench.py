@@ -569,6 +569,13 @@ def run_offload(args, rank, world, local_rank):
     L, H, Hkv, D = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"]
     cached = int(cfg["lens"][1])
     S = cached + 1
+    # every rank holds its own host copy of the KV history (replicas): refuse
+    # before allocating when the node's RAM cannot hold all of them
+    need = world * L * S * Hkv * D * 2 * 2
+    ram = os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_PHYS_PAGES")
+    if need > 0.8 * ram:
+        raise SystemExit(f"offload replicas need {need / 1e9:.1f} GB of host RAM for {world} ranks; "
+                         f"this node has {ram / 1e9:.1f} GB (run fewer ranks or --layers)")
     t0 = time.perf_counter()
     kv = KVCacheManager(L, S, Hkv, D, offload_to_cpu=True, max_kv_bytes=1 << 50)
     rng = np.random.default_rng(cfg["seed"])
