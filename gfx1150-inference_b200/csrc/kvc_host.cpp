@@ -455,12 +455,8 @@ int round_split(int c, int page_size) {
   return c < page_size ? page_size : c;
 }
 
-int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
-                        int device) {
-  const int forced = split_tokens_for(page_size);
-  if (forced > 0) return round_split(forced, page_size);
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+int split_tokens_model(int page_size, const int* ctx, int n_queries, int units_per_split,
+                       int sms) {
   const double warps = static_cast<double>(sms) * kPersistWarps;
   constexpr double kUnitCost = 64.0;   // c0, in positions
   constexpr int kMinSplit = 64;
@@ -488,6 +484,18 @@ int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_
     }
   }
   return best;
+}
+
+int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
+                        int device) {
+  const int forced = split_tokens_for(page_size);
+  if (forced > 0) return round_split(forced, page_size);
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  return split_tokens_model(page_size, ctx, n_queries, units_per_split, sms);
 }
 
 // Build the split list on the host.  ctx_of(i) / row_of(i) describe query i.
@@ -750,6 +758,22 @@ int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const vo
 }
 
 }  // namespace kvc
+
+extern "C" int kvc_plan_split_tokens(const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                                     int num_kv_heads, int page_size, int sm_count, int* out) {
+  if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");
+  if (n_queries < 0 || (n_queries > 0 && !h_ctx_lens))
+    return set_error(KVC_ERR_INVALID_ARG, "ctx_lens must hold n_queries lengths.");
+  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_heads must be a positive multiple of num_kv_heads.");
+  if (page_size <= 0 || page_size % kSlab != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "page_size must be a positive multiple of 16.");
+  if (sm_count <= 0) return set_error(KVC_ERR_INVALID_ARG, "sm_count must be positive.");
+  const int group = num_heads / num_kv_heads;
+  *out = split_tokens_model(page_size, h_ctx_lens, n_queries, num_kv_heads * ((group + 7) / 8),
+                            sm_count);
+  return KVC_OK;
+}
 
 extern "C" int kvc_plan_create(kvc_plan_t** out) {
   if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");

@@ -191,6 +191,13 @@ KVC_API int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const int3
                     const int32_t* h_ctx_lens, int n_queries, int num_heads,
                     void* stream);
 
+/* The split length (positions) kvc_plan_decode chooses for a batch on a GPU
+ * with sm_count SMs: 512, or the one-wave length its cost model estimates
+ * faster (KVC_SPLIT_TOKENS, when set, overrides the plan but not this query).
+ * Host only; no counterpart in the reference. */
+KVC_API int kvc_plan_split_tokens(const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                                  int num_kv_heads, int page_size, int sm_count, int* out);
+
 /* Plan flags.  KVC_PLAN_KV_STABLE: the block tables and KV pages the plan reads
  * are not written by the kernel launched immediately before each decode on the
  * stream (e.g. they change only through host copies or earlier steps), so the

@@ -84,3 +84,38 @@ def test_status_code_mapping():
     with pytest.raises(RuntimeError):
         ffi.check(ffi.KVC_ERR_CUDA)
     ffi.check(ffi.KVC_OK)
+
+
+def test_split_length_model_on_the_baseline_shapes():
+    """The plan's split length (host-only model, kvc_plan_split_tokens) for the
+    BASELINE shapes on a 148-SM B200: 512 for the ragged batch and the unsharded
+    70B shape, one wave of equal units for long even contexts and their KV-head
+    shards, and the 4K single sequence."""
+    import ctypes
+
+    import numpy as np
+
+    import bench
+    import kvcache_ffi as ffi
+
+    def split(ctx, H, Hkv, ps=16, sms=148):
+        c = np.ascontiguousarray(np.asarray(ctx, dtype=np.int32))
+        out = ctypes.c_int(0)
+        ffi.check(ffi.lib.kvc_plan_split_tokens(ffi.np_ptr(c), len(c), H, Hkv, ps, sms,
+                                                ctypes.byref(out)))
+        return out.value
+
+    c3 = bench.cached_lengths(bench.CONFIGS["3"]) + 1
+    assert split(c3, 32, 8) == 512
+    assert split([32769] * 8, 64, 8) == 512
+    assert split([32769] * 8, 32, 4) == 896     # 2-way KV-head shard: 1,184 units
+    assert split([32769] * 8, 16, 2) == 448     # 4-way
+    assert split([32769] * 8, 8, 1) == 224      # 8-way: 1,176 units
+    assert split([4096], 32, 32) == 112         # config 2: 1,184 units
+    assert split([4096], 32, 32, ps=32) % 32 == 0
+    for bad in ((c3, 30, 8), (c3, 32, 0)):
+        out = ctypes.c_int(0)
+        c = np.ascontiguousarray(np.asarray(bad[0], dtype=np.int32))
+        rc = ffi.lib.kvc_plan_split_tokens(ffi.np_ptr(c), len(c), bad[1], bad[2], 16, 148,
+                                           ctypes.byref(out))
+        assert rc == ffi.KVC_ERR_INVALID_ARG
