@@ -3,9 +3,14 @@
 //   decode_persistent_kernel  split-K flash-decoding GQA attention, 16-bit storage: one
 //                             CTA per SM, warps streaming KV slabs through bulk-copy rings,
 //                             tensor-core math, the row append fused in
-//   merge_splits_kernel       merge of the split partials (programmatic dependent launch)
+//   merge_splits_kernel       merge of the split partials (programmatic dependent launch);
+//                             with KV heads split over GPUs it stores the rows into every
+//                             rank's exchange slot
+//   xchg_signal_kernel        publishes the head exchange's epoch and waits for the peers
 //   decode_simt_kernel        split-K GQA attention on CUDA cores (fp32 storage, other
 //                             head dims), splits merged by the last CTA of a query
+//   stage_inputs_kernel       page-locked host inputs -> device staging (host-buffer calls)
+//   rope_kernel               rotary position embedding (rope.hip semantics)
 //   gather_kernel             pool -> token-major rows (bit-exact pool checks)
 //   fill_normal_kernel        seeded N(0, s^2) synthetic pool contents
 //
@@ -401,16 +406,17 @@ __device__ void finish_split(const DecodeArgs& a, float* sm, int query, int kvh,
 // Persistent tensor-core decode kernel (16-bit storage, head_dim multiple of 32).
 //
 // One CTA of NW warps per SM; every warp is an independent streaming engine.
-// The host assigns whole split units (one split of one query for one KV head
-// and <= 8 of its q-heads) to warps, longest first onto the least-loaded warp,
-// so all warps stream about the same number of positions.  A warp walks its
-// list in order: its producer side keeps NS slabs (16 positions of K and V,
-// one bulk copy each) in flight in the warp's shared-memory ring, running into
-// the next unit before the current one is finished, and prefetches the next
-// unit's page ids one unit ahead; its consumer side does the math of a slab
+// The host lists whole split units (one split of one query for one KV head and
+// <= 8 of its q-heads) longest first; warp w of the grid starts with unit w and
+// then takes the next unlisted unit from a global counter, so every warp keeps
+// streaming until the list is done.  A warp's producer side keeps NS slabs (16
+// positions of K and V, one bulk copy each) in flight in the warp's
+// shared-memory ring, running into the next unit before the current one is
+// finished, and fetches the next unit's record and page ids one step per
+// issued slab; its consumer side does the math of a slab
 // as soon as it lands (S = Q K^T, online softmax, O^T += V^T P^T, mma.sync
 // m16n8k16) and, at the end of a unit, writes the output or the split's
-// partial state (the last split of a query to finish merges all of them).
+// partial state (merged by merge_splits_kernel, launched behind it).
 // There is no CTA-wide synchronisation after start-up.
 // =====================================================================================
 constexpr int kPersistBarBytes = 1024;   // NW * NS mbarriers
