@@ -59,12 +59,20 @@ struct kvc_offload {
 
   cudaStream_t copy = nullptr, compute = nullptr;
 
+  // HBM mirror of layers [0, n_mirror) (kvc_offload_set_mirror): their pages stay
+  // on the device; an attend uploads only the rows the mirror lacks.
+  kvc_pool mirror;
+  int n_mirror = 0;
+  std::vector<int> mirror_rows;  // rows [0, mirror_rows[l]) of layer l are current
+  DevBuf mstage_k, mstage_v;     // H2D staging of mirror uploads
+
   // copy-engine timing: ring of (start, stop, bytes) harvested when complete
   cudaEvent_t t_start[kTimingRing] = {}, t_stop[kTimingRing] = {};
   double t_bytes[kTimingRing] = {};
   int t_head = 0, t_tail = 0;
 
-  double h2d_bytes = 0.0, h2d_ms = 0.0;
+  double h2d_bytes = 0.0, h2d_ms = 0.0;  // streamed layers (copy-stream events)
+  double mirror_bytes = 0.0;             // rows uploaded into the HBM mirror
   int64_t hits = 0, calls = 0;
 };
 
@@ -134,6 +142,11 @@ void destroy_locked(kvc_offload* o) {
     o->t_start[i] = o->t_stop[i] = nullptr;
   }
   pool_release(&o->slot);
+  pool_release(&o->mirror);
+  o->n_mirror = 0;
+  o->mirror_rows.clear();
+  o->mstage_k.release();
+  o->mstage_v.release();
   o->bt.release();
   o->io.release();
   o->plan.release();
@@ -145,6 +158,80 @@ void destroy_locked(kvc_offload* o) {
   if (o->copy) cudaStreamDestroy(o->copy);
   if (o->compute) cudaStreamDestroy(o->compute);
   o->copy = o->compute = nullptr;
+}
+
+}  // namespace
+
+namespace {
+
+// The next layer after `layer` that is streamed (not mirrored), cyclically, and
+// how many of its rows are final now: within a step the prefix [0, start_pos);
+// a layer of the next step [0, total).  Prefetch it into bounce `bi` unless a
+// bounce already holds it.
+int prefetch_next(kvc_offload* o, int layer, int start_pos, int total, int bi) {
+  if (o->n_mirror >= o->num_layers) return KVC_OK;  // nothing is streamed
+  // mirrored layers are [0, n_mirror): the next streamed one in this step, or the
+  // first one of the next step
+  const bool this_step = layer + 1 < o->num_layers;
+  const int next = this_step ? std::max(layer + 1, o->n_mirror) : o->n_mirror;
+  if (next == layer) return KVC_OK;
+  for (const auto& B : o->b)
+    if (B.layer == next) return KVC_OK;
+  return start_fill(o, bi, next, this_step ? start_pos : total);
+}
+
+// Attend on a mirrored layer: bring the mirror up to rows [0, total) (in
+// decode, just the appended row), then the resident path's kernels on the
+// mirror's pages.  Same page geometry and split partition as the streamed path,
+// so outputs are bit-identical.
+int attend_mirrored(kvc_offload* o, const void* h_Q, void* h_Out, int layer, int q_len,
+                    int start_pos, int num_heads, float scale, int causal, int total) {
+  cudaStream_t s = o->compute;
+  cudaError_t e;
+  int rc;
+  const int32_t* bt = static_cast<const int32_t*>(o->bt.ptr);
+  constexpr int kChunkRows = 4096;
+  int r0 = std::min(o->mirror_rows[layer], start_pos);  // the appended rows are new
+  if (r0 < total) {
+    const int chunk = std::min(kChunkRows, total - r0);
+    const size_t cb = static_cast<size_t>(chunk) * o->row_bytes;
+    if ((e = o->mstage_k.ensure(cb)) || (e = o->mstage_v.ensure(cb)))
+      return cuda_error(e, "cudaMalloc(mirror staging)");
+  }
+  // Row chunks through the staging buffers on the compute stream (stream order
+  // keeps a chunk's scatter ahead of the next chunk's copy into the staging).
+  for (; r0 < total; r0 += kChunkRows) {
+    const int n = std::min(kChunkRows, total - r0);
+    const size_t off = static_cast<size_t>(layer) * o->layer_bytes +
+                       static_cast<size_t>(r0) * o->row_bytes;
+    const size_t nb = static_cast<size_t>(n) * o->row_bytes;
+    if ((e = cudaMemcpyAsync(o->mstage_k.ptr, o->h_k + off, nb, cudaMemcpyHostToDevice, s)) ||
+        (e = cudaMemcpyAsync(o->mstage_v.ptr, o->h_v + off, nb, cudaMemcpyHostToDevice, s)))
+      return cuda_error(e, "cudaMemcpyAsync(mirror rows)");
+    o->mirror_bytes += 2.0 * static_cast<double>(nb);
+    if ((rc = do_append(&o->mirror, layer, o->mstage_k.ptr, o->mstage_v.ptr, bt, o->bt_len,
+                        nullptr, nullptr, r0, n, s)))
+      return rc;
+  }
+  o->mirror_rows[layer] = total;
+  // the streamed layers keep coming in on the copy stream meanwhile
+  if ((rc = prefetch_next(o, layer, start_pos, total, 1 - o->last_used))) return rc;
+
+  const size_t qb = static_cast<size_t>(q_len) * num_heads * o->head_dim * o->es;
+  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
+  if ((e = o->io.ensure(2 * qb_al))) return cuda_error(e, "cudaMalloc(io)");
+  uint8_t* d_q = static_cast<uint8_t*>(o->io.ptr);
+  uint8_t* d_out = d_q + qb_al;
+  if ((e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpyAsync(Q)");
+  if ((rc = plan_queries(&o->plan, o->mirror.g, q_len, num_heads, start_pos, total, causal != 0,
+                         o->device, s)))
+    return rc;
+  void* direct = mapped_host_ptr(h_Out);
+  if ((rc = do_decode(&o->mirror, &o->plan, layer, d_q, direct ? direct : d_out, bt, o->bt_len,
+                      scale, s)))
+    return rc;
+  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "offload attend");
 }
 
 }  // namespace
@@ -240,6 +327,42 @@ extern "C" int kvc_offload_invalidate(kvc_offload_t* off) {
     B.layer = -1;
     B.rows = 0;
   }
+  std::fill(off->mirror_rows.begin(), off->mirror_rows.end(), 0);
+  return KVC_OK;
+}
+
+extern "C" int kvc_offload_set_mirror(kvc_offload_t* off, size_t budget_bytes, int* n_layers) {
+  if (!off) return set_error(KVC_ERR_INVALID_ARG, "offload handle must not be null.");
+  kvc_offload* o = off;
+  std::lock_guard<std::mutex> lock(o->mu);
+  cudaError_t e = cudaSetDevice(o->device);
+  if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+  if ((e = cudaStreamSynchronize(o->compute))) return cuda_error(e, "cudaStreamSynchronize");
+  pool_release(&o->mirror);
+  o->n_mirror = 0;
+  o->mirror_rows.clear();
+  const PoolGeom& sg = o->slot.g;
+  const size_t per_layer = 2 * sg.layer_bytes;  // K and V pages of one layer
+  const int n = static_cast<int>(std::min<size_t>(o->num_layers, budget_bytes / per_layer));
+  if (n > 0) {
+    PoolGeom g;
+    int rc = make_geom(n, sg.num_pages, sg.page_size, sg.num_kv_heads, sg.head_dim, sg.dtype, &g);
+    if (rc) return rc;
+    if ((rc = pool_alloc(&o->mirror, g, o->device))) return rc;
+    o->n_mirror = n;
+    o->mirror_rows.assign(n, 0);
+  }
+  if (n_layers) *n_layers = o->n_mirror;
+  return KVC_OK;
+}
+
+extern "C" int kvc_offload_mirror_stats(const kvc_offload_t* off, int* n_layers,
+                                        double* uploaded_bytes) {
+  if (!off) return set_error(KVC_ERR_INVALID_ARG, "offload handle must not be null.");
+  kvc_offload* o = const_cast<kvc_offload*>(off);
+  std::lock_guard<std::mutex> lock(o->mu);
+  if (n_layers) *n_layers = o->n_mirror;
+  if (uploaded_bytes) *uploaded_bytes = o->mirror_bytes;
   return KVC_OK;
 }
 
@@ -289,6 +412,9 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
   for (auto& B : o->b)
     if (B.layer == layer_idx && B.rows > start_pos) B.rows = start_pos;
 
+  if (layer_idx < o->n_mirror) return attend_mirrored(o, h_Q, h_Out, layer_idx, q_len, start_pos,
+                                                       num_heads, scale, causal, total);
+
   // 2. make rows [0, total) of the layer resident in a bounce buffer.
   int bi = -1;
   for (int i = 0; i < 2; ++i)
@@ -306,15 +432,8 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
   if ((e = cudaEventRecord(B.ready, o->copy))) return cuda_error(e, "cudaEventRecord(ready)");
   o->last_used = bi;
 
-  // 3. prefetch the next layer into the other bounce buffer: within a step the
-  //    next layer's prefix [0, start_pos) is final; after the last layer, layer 0
-  //    of the next step needs [0, total).
-  const int next = (layer_idx + 1) % o->num_layers;
-  const int next_rows = next > layer_idx ? start_pos : total;
-  if (next != layer_idx) {
-    const int nbi = 1 - bi;
-    if ((rc = start_fill(o, nbi, next, next_rows))) return rc;
-  }
+  // 3. prefetch the next streamed layer into the other bounce buffer.
+  if ((rc = prefetch_next(o, layer_idx, start_pos, total, 1 - bi))) return rc;
 
   // 4. compute stream: scatter the rows into the paged slot, attend, copy out.
   const size_t qb = static_cast<size_t>(q_len) * num_heads * o->head_dim * o->es;

@@ -26,8 +26,11 @@ copy stream while the previous layer attends, and the next layer is
 prefetched.  Outputs are bit-identical to the gpu mode's.  Nothing touches the
 GPU before the first ``attend`` in those modes, as in the reference.
 
-Extension: ``dtype`` (keyword-only) selects float16 (the reference's only
-type) or float32 storage.
+Extensions (keyword-only): ``dtype`` selects float16 (the reference's only
+type) or float32 storage; ``offload_mirror_bytes`` lets the cpu/mmap modes keep
+an HBM copy of as many layers as that many bytes of device memory hold (the
+host arrays stay the source of truth; a mirrored layer uploads only its new
+rows per attend; outputs unchanged).
 """
 
 from __future__ import annotations
@@ -88,6 +91,7 @@ class KVCacheManager:
         max_kv_bytes: int = DEFAULT_MAX_KV_BYTES,
         *,
         dtype=np.float16,
+        offload_mirror_bytes: int = 0,
     ):
         self.num_layers = int(num_layers)
         self.max_seq_len = int(max_seq_len)
@@ -104,6 +108,9 @@ class KVCacheManager:
         self._v_mm: Optional[mmap.mmap] = None
         self._created_mmap_files: List[str] = []
         self._offload = None  # kvc_offload_t* (created on first attend)
+        self.offload_mirror_bytes = int(offload_mirror_bytes)
+        if self.offload_mirror_bytes < 0:
+            raise ValueError("offload_mirror_bytes must be non-negative")
 
         if self.dtype not in (np.dtype(np.float16), np.dtype(np.float32)):
             raise ValueError(f"unsupported KV storage dtype {self.dtype}")
@@ -232,21 +239,29 @@ class KVCacheManager:
                 ffi.dtype_code_of(self.dtype), ffi.OFFLOAD_REGISTER, _current_device(),
                 ctypes.byref(h)))
             self._offload = h
+            if self.offload_mirror_bytes > 0:
+                n = ctypes.c_int(0)
+                ffi.check(ffi.lib.kvc_offload_set_mirror(h, self.offload_mirror_bytes,
+                                                         ctypes.byref(n)))
         return self._offload
 
     def offload_stats(self) -> dict:
         """Host-link statistics of the cpu/mmap modes (bytes, copy-engine ms,
         prefetch hits, attend calls)."""
         if self._offload is None:
-            return {"h2d_bytes": 0.0, "h2d_ms": 0.0, "prefetch_hits": 0, "attend_calls": 0}
+            return {"h2d_bytes": 0.0, "h2d_ms": 0.0, "prefetch_hits": 0, "attend_calls": 0,
+                    "mirror_layers": 0, "mirror_bytes": 0.0}
         import kvcache_ffi as ffi
 
         b, ms = ctypes.c_double(), ctypes.c_double()
         hits, calls = ctypes.c_int64(), ctypes.c_int64()
         ffi.check(ffi.lib.kvc_offload_stats(self._offload, ctypes.byref(b), ctypes.byref(ms),
                                             ctypes.byref(hits), ctypes.byref(calls)))
+        nl, mb = ctypes.c_int(), ctypes.c_double()
+        ffi.check(ffi.lib.kvc_offload_mirror_stats(self._offload, ctypes.byref(nl),
+                                                   ctypes.byref(mb)))
         return {"h2d_bytes": b.value, "h2d_ms": ms.value, "prefetch_hits": hits.value,
-                "attend_calls": calls.value}
+                "attend_calls": calls.value, "mirror_layers": nl.value, "mirror_bytes": mb.value}
 
     def attend(
         self,

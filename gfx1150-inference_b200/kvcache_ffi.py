@@ -110,6 +110,9 @@ SIGNATURES = {
                           _vp]),
     "kvc_append_decode_rope": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int,
                                         _c_float, _c_float, _c_int, _vp]),
+    "kvc_offload_set_mirror": (_c_int, [_vp, _c_size, ctypes.POINTER(_c_int)]),
+    "kvc_offload_mirror_stats": (_c_int, [_vp, ctypes.POINTER(_c_int),
+                                          ctypes.POINTER(ctypes.c_double)]),
     "kvc_xchg_create": (_c_int, [_c_int, _c_int, _c_int, _c_size, _c_int, ctypes.POINTER(_vp)]),
     "kvc_xchg_handle": (_c_int, [_vp, _vp]),
     "kvc_xchg_connect": (_c_int, [_vp, _vp]),

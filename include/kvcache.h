@@ -323,10 +323,23 @@ KVC_API int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const void* 
 /* Discard prefetched layers (call after the host pools were written elsewhere). */
 KVC_API int kvc_offload_invalidate(kvc_offload_t* off);
 
-/* Cumulative host-to-device bytes and copy-engine time (ms) of the offload path,
- * and how many attend calls found their layer already prefetched. */
+/* Cumulative host-to-device bytes and copy-engine time (ms) of the streamed
+ * layers, and how many attend calls found their layer already prefetched. */
 KVC_API int kvc_offload_stats(const kvc_offload_t* off, double* h2d_bytes, double* h2d_ms,
                       int64_t* prefetch_hits, int64_t* attend_calls);
+
+/* No counterpart in the reference.  Keep an HBM mirror of as many layers as
+ * `budget_bytes` of device memory holds (layers 0 .. n-1, *n_layers = n; 0
+ * releases it).  The host pools stay the source of truth: an attend on a
+ * mirrored layer appends on the host as before, uploads only the rows the
+ * mirror lacks (the appended ones in decode; the whole layer on its first use
+ * or after kvc_offload_invalidate) and attends on the mirror, bit-identical to
+ * the streamed and resident paths; the other layers are streamed as before.
+ * For a B200, whose HBM holds what a smaller GPU had to offload. */
+KVC_API int kvc_offload_set_mirror(kvc_offload_t* off, size_t budget_bytes, int* n_layers);
+/* Mirrored layers and the bytes uploaded into the mirror so far. */
+KVC_API int kvc_offload_mirror_stats(const kvc_offload_t* off, int* n_layers,
+                                     double* uploaded_bytes);
 
 /* ==== 4. Head exchange across the GPUs of one node ========================
  * No counterpart in the reference (it runs on one GPU).  When the KV heads of

@@ -262,6 +262,36 @@ def test_offload_cpu_and_mmap_bit_identical_to_resident():
         assert _maxerr(row, ref) < 2e-3
 
 
+def test_offload_hbm_mirror_bit_identical_and_uploads_only_new_rows():
+    """offload_mirror_bytes: some layers mirrored in HBM (the rest streamed), every
+    output bit-identical to the resident pool; after the prefill a decode step
+    uploads just the appended rows of the mirrored layers; invalidate re-uploads."""
+    c = _seq_case()
+    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"]) as kv:
+        gpu = _by_position(_run_sequence(kv, c))
+    layer_bytes = 2 * 64 * c["Hkv"] * c["D"] * 2     # K + V pages of one layer (64 positions)
+    for budget, expect_layers in ((layer_bytes * 2, 2), (layer_bytes * 10, 3)):
+        with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], offload_to_cpu=True,
+                            offload_mirror_bytes=budget) as kv:
+            got = _by_position(_run_sequence(kv, c))
+            st = kv.offload_stats()
+            assert st["mirror_layers"] == expect_layers
+            row = c["Hkv"] * c["D"] * 2
+            # prefill chunks: 8 rows per mirrored layer; then 3 decode steps of 1 row each
+            assert st["mirror_bytes"] == 2 * row * expect_layers * (8 + 3)
+            if expect_layers == c["L"]:
+                assert st["h2d_bytes"] == 0  # nothing streamed
+            # a further step after invalidate re-uploads whole layers, same results
+            ffi.check(ffi.lib.kvc_offload_invalidate(kv._offload))
+            out = np.zeros((1, c["H"], c["D"]), np.float16)
+            kv.attend(c["Q"][0, 10:11], c["K"][0, 10:11], c["V"][0, 10:11], out, layer_idx=0,
+                      q_len=1, start_pos=10, num_heads=c["H"], scale=c["scale"], causal=True)
+            np.testing.assert_array_equal(out[0], gpu[(0, 10)])
+            assert kv.offload_stats()["mirror_bytes"] == st["mirror_bytes"] + 2 * row * 11
+        for key in gpu:
+            np.testing.assert_array_equal(got[key], gpu[key], err_msg=f"{budget} {key}")
+
+
 def test_chunked_prefill_bit_identical():
     """test_phase5_scale.py:199-206 (full vs chunked prefill) at the attention level."""
     c = _seq_case()
