@@ -577,7 +577,8 @@ def run_offload(args, rank, world, local_rank):
         raise SystemExit(f"offload replicas need {need / 1e9:.1f} GB of host RAM for {world} ranks; "
                          f"this node has {ram / 1e9:.1f} GB (run fewer ranks or --layers)")
     t0 = time.perf_counter()
-    kv = KVCacheManager(L, S, Hkv, D, offload_to_cpu=True, max_kv_bytes=1 << 50)
+    kv = KVCacheManager(L, S, Hkv, D, offload_to_cpu=True, max_kv_bytes=1 << 50,
+                        offload_mirror_bytes=int(args.mirror_gb * 1e9))
     rng = np.random.default_rng(cfg["seed"])
     block = rng.standard_normal(1 << 23, dtype=np.float32).astype(np.float16)
     for arr, shift in ((kv._k_host, 0), (kv._v_host, 12345)):
@@ -634,6 +635,9 @@ def run_offload(args, rank, world, local_rank):
                    "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D, "batch": 1,
                    "cached_len": cached, "host_kv_gb": round(kv_bytes / 1e9, 2),
                    "timing": "host wall clock; every attend call waits for its output"},
+        "hbm_mirror": {"budget_gb": args.mirror_gb, "layers": st["mirror_layers"],
+                       "uploaded_gb_per_step": round((st["mirror_bytes"] - first["mirror_bytes"])
+                                                     / args.steps / 1e9, 6)},
         "host_link": {"h2d_gb_per_step": round(h2d / args.steps / 1e9, 3),
                       "h2d_gbs_wall": round(h2d / elapsed / 1e9, 2),
                       "h2d_gbs_copy_engine": round(h2d / (h2d_ms / 1e3) / 1e9, 2) if h2d_ms else None,
@@ -706,6 +710,8 @@ def main():
     ap.add_argument("--page-size", type=int, default=PAGE, help="positions per KV page (multiple of 16)")
     ap.add_argument("--rope", action="store_true",
                     help="rotate q and the new K rows (RoPE) inside the step (rope + append + attend)")
+    ap.add_argument("--mirror-gb", type=float, default=0.0,
+                    help="config 5: keep an HBM mirror of as many layers as this many GB hold")
     ap.add_argument("--one-rank-of", type=int, default=0,
                     help="profiling on one GPU: run rank 0's shard of an N-way KV-head split "
                          "with its head exchange connected to itself")
