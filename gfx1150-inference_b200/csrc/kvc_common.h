@@ -61,23 +61,25 @@ struct kvc_plan {
   std::vector<int4> sched_recs;   // 3 per scheduled unit
   std::vector<int32_t> merge_queries;
   int n_sched_ctas = 0, n_units = 0;
-  kvc::DevBuf d_items, d_qinfo, d_rows, d_pos, d_part_o, d_part_ml, d_counters, d_queue,
-      d_sched_units, d_merge;
+  kvc::DevBuf d_blob;          // items, qinfo, rows, positions, unit records, merge list, counter
+  kvc::DevBuf d_part_o, d_part_ml, d_counters;
+  // parts of d_blob (set by the upload)
+  const int4* dev_items = nullptr;
+  const int4* dev_qinfo = nullptr;
+  const int32_t* dev_rows = nullptr;
+  const int32_t* dev_pos = nullptr;
+  const int4* dev_sched = nullptr;
+  const int32_t* dev_merge = nullptr;
+  unsigned int* dev_queue = nullptr;
   kvc::DevBuf d_rope;          // rotated q and new K rows (kvc_append_decode_rope)
   kvc::HostBuf h_stage;
   cudaEvent_t upload_done = nullptr;
 
   void release() {
-    d_items.release();
-    d_qinfo.release();
-    d_rows.release();
-    d_pos.release();
+    d_blob.release();
     d_part_o.release();
     d_part_ml.release();
     d_counters.release();
-    d_queue.release();
-    d_sched_units.release();
-    d_merge.release();
     d_rope.release();
     h_stage.release();
     if (upload_done) cudaEventDestroy(upload_done);

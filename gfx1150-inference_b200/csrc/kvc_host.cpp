@@ -588,56 +588,59 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   }
 
   cudaError_t e;
-  // device buffers (grow-only)
-  const size_t items_b = sizeof(int4) * std::max<size_t>(1, p->item_pairs.size());
-  const size_t qinfo_b = sizeof(int4) * std::max(1, n_queries);
-  const size_t rows_b = sizeof(int32_t) * std::max(1, n_queries);
+  // Scratch (grow-only): split partials and the per-(query, head) counters.
   const size_t po_b = sizeof(float) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads * g.head_dim);
   const size_t pml_b = sizeof(float2) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads);
   const size_t cnt_b = sizeof(unsigned) * std::max<size_t>(1, static_cast<size_t>(n_queries) * g.num_kv_heads * p->n_hchunk);
-  if ((e = p->d_items.ensure(items_b)) || (e = p->d_qinfo.ensure(qinfo_b)) ||
-      (e = p->d_rows.ensure(rows_b)) || (e = p->d_pos.ensure(rows_b)) ||
-      (e = p->d_part_o.ensure(po_b)) || (e = p->d_part_ml.ensure(pml_b)))
+  if ((e = p->d_part_o.ensure(po_b)) || (e = p->d_part_ml.ensure(pml_b)))
     return cuda_error(e, "plan buffers");
   if (cnt_b > p->d_counters.cap) {
     if ((e = p->d_counters.ensure(cnt_b))) return cuda_error(e, "plan counters");
     if ((e = cudaMemsetAsync(p->d_counters.ptr, 0, p->d_counters.cap, s)))
       return cuda_error(e, "cudaMemsetAsync(counters)");
   }
-  // upload through pinned staging; wait for the previous upload to leave it
-  const size_t soff_b = 0;
-  const size_t sun_b = sizeof(int4) * std::max<size_t>(1, p->sched_recs.size());
-  if ((e = p->d_sched_units.ensure(sun_b)) || (e = p->d_queue.ensure(256)))
-    return cuda_error(e, "plan schedule buffers");
-  // the unit counter starts at zero (the merge kernel re-arms it after each launch)
-  if ((e = cudaMemsetAsync(p->d_queue.ptr, 0, 256, s))) return cuda_error(e, "cudaMemsetAsync(queue)");
-  const size_t mq_b = sizeof(int32_t) * std::max<size_t>(1, p->merge_queries.size());
-  if ((e = p->d_merge.ensure(mq_b))) return cuda_error(e, "plan merge list");
-  const size_t stage_b = items_b + qinfo_b + 2 * rows_b + soff_b + sun_b + mq_b;
-  if (p->upload_done) {
+  // The plan itself: one block {items | qinfo | rows | positions | unit records |
+  // merge list | unit counter (zero)}, 256-byte aligned parts, staged in pinned
+  // memory and uploaded with one copy.
+  auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+  const size_t items_n = sizeof(int4) * p->item_pairs.size();
+  const size_t qinfo_n = sizeof(int4) * n_queries;
+  const size_t rows_n = sizeof(int32_t) * n_queries;
+  const size_t sched_n = sizeof(int4) * p->sched_recs.size();
+  const size_t merge_n = sizeof(int32_t) * p->merge_queries.size();
+  const size_t o_items = 0;
+  const size_t o_qinfo = o_items + al(std::max<size_t>(items_n, 1));
+  const size_t o_rows = o_qinfo + al(std::max<size_t>(qinfo_n, 1));
+  const size_t o_pos = o_rows + al(std::max<size_t>(rows_n, 1));
+  const size_t o_sched = o_pos + al(std::max<size_t>(rows_n, 1));
+  const size_t o_merge = o_sched + al(std::max<size_t>(sched_n, 1));
+  const size_t o_queue = o_merge + al(std::max<size_t>(merge_n, 1));
+  const size_t blob_b = o_queue + 256;
+  if ((e = p->d_blob.ensure(blob_b))) return cuda_error(e, "plan buffers");
+  if (p->upload_done) {  // the staging is free once the previous upload has landed
     if ((e = cudaEventSynchronize(p->upload_done))) return cuda_error(e, "plan upload wait");
   } else if ((e = cudaEventCreateWithFlags(&p->upload_done, cudaEventDisableTiming))) {
     return cuda_error(e, "cudaEventCreate");
   }
-  if ((e = p->h_stage.ensure(stage_b))) return cuda_error(e, "cudaMallocHost(plan)");
+  if ((e = p->h_stage.ensure(blob_b))) return cuda_error(e, "cudaMallocHost(plan)");
   uint8_t* h = static_cast<uint8_t*>(p->h_stage.ptr);
-  memcpy(h, p->item_pairs.data(), sizeof(int4) * p->item_pairs.size());
-  memcpy(h + items_b, p->qinfo.data(), sizeof(int4) * n_queries);
-  memcpy(h + items_b + qinfo_b, p->rows.data(), sizeof(int32_t) * n_queries);
-  memcpy(h + items_b + qinfo_b + rows_b, p->positions.data(), sizeof(int32_t) * n_queries);
-  uint8_t* hs = h + items_b + qinfo_b + 2 * rows_b;
-  if (!p->sched_recs.empty()) memcpy(hs + soff_b, p->sched_recs.data(), sizeof(int4) * p->sched_recs.size());
-  uint8_t* hm = hs + soff_b + sun_b;
-  if (!p->merge_queries.empty()) memcpy(hm, p->merge_queries.data(), sizeof(int32_t) * p->merge_queries.size());
-  if ((e = cudaMemcpyAsync(p->d_items.ptr, h, sizeof(int4) * p->item_pairs.size(), cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(p->d_qinfo.ptr, h + items_b, sizeof(int4) * n_queries, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(p->d_rows.ptr, h + items_b + qinfo_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(p->d_pos.ptr, h + items_b + qinfo_b + rows_b, sizeof(int32_t) * n_queries, cudaMemcpyHostToDevice, s)) ||
-      (!p->sched_recs.empty() &&
-       (e = cudaMemcpyAsync(p->d_sched_units.ptr, hs + soff_b, sizeof(int4) * p->sched_recs.size(), cudaMemcpyHostToDevice, s))) ||
-      (!p->merge_queries.empty() &&
-       (e = cudaMemcpyAsync(p->d_merge.ptr, hm, sizeof(int32_t) * p->merge_queries.size(), cudaMemcpyHostToDevice, s))))
+  if (items_n) memcpy(h + o_items, p->item_pairs.data(), items_n);
+  if (qinfo_n) memcpy(h + o_qinfo, p->qinfo.data(), qinfo_n);
+  if (rows_n) memcpy(h + o_rows, p->rows.data(), rows_n);
+  if (rows_n) memcpy(h + o_pos, p->positions.data(), rows_n);
+  if (sched_n) memcpy(h + o_sched, p->sched_recs.data(), sched_n);
+  if (merge_n) memcpy(h + o_merge, p->merge_queries.data(), merge_n);
+  memset(h + o_queue, 0, 256);  // the unit counter starts at zero (the merge re-arms it)
+  if ((e = cudaMemcpyAsync(p->d_blob.ptr, h, blob_b, cudaMemcpyHostToDevice, s)))
     return cuda_error(e, "plan upload");
+  uint8_t* d = static_cast<uint8_t*>(p->d_blob.ptr);
+  p->dev_items = reinterpret_cast<const int4*>(d + o_items);
+  p->dev_qinfo = reinterpret_cast<const int4*>(d + o_qinfo);
+  p->dev_rows = reinterpret_cast<const int32_t*>(d + o_rows);
+  p->dev_pos = reinterpret_cast<const int32_t*>(d + o_pos);
+  p->dev_sched = reinterpret_cast<const int4*>(d + o_sched);
+  p->dev_merge = reinterpret_cast<const int32_t*>(d + o_merge);
+  p->dev_queue = reinterpret_cast<unsigned*>(d + o_queue);
   if ((e = cudaEventRecord(p->upload_done, s))) return cuda_error(e, "cudaEventRecord(plan)");
   p->pool_geom = g;
   p->valid = true;
@@ -675,18 +678,18 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.out = d_out;
   a.block_tables = d_bt;
   a.bt_stride = bt_stride;
-  a.items = static_cast<const int4*>(plan->d_items.ptr);
-  a.qinfo = static_cast<const int4*>(plan->d_qinfo.ptr);
+  a.items = plan->dev_items;
+  a.qinfo = plan->dev_qinfo;
   a.part_o = static_cast<float*>(plan->d_part_o.ptr);
   a.part_ml = static_cast<float2*>(plan->d_part_ml.ptr);
   a.counters = static_cast<unsigned*>(plan->d_counters.ptr);
-  a.sched_recs = static_cast<const int4*>(plan->d_sched_units.ptr);
+  a.sched_recs = plan->dev_sched;
   a.n_units = plan->n_units;
-  a.queue = static_cast<unsigned*>(plan->d_queue.ptr);
+  a.queue = plan->dev_queue;
   a.n_sched_ctas = plan->n_sched_ctas;
   a.early_prefetch = early >= 0 ? early : ((plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0);
   a.l2_ahead = l2_ahead_slabs(plan->split_tokens);
-  a.merge_queries = static_cast<const int32_t*>(plan->d_merge.ptr);
+  a.merge_queries = plan->dev_merge;
   a.n_merge_queries = static_cast<int>(plan->merge_queries.size());
   a.k_new = static_cast<const uint8_t*>(d_k_new);
   a.v_new = static_cast<const uint8_t*>(d_v_new);
@@ -750,8 +753,7 @@ int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const vo
                            s, xt, early);
   }
   int rc = do_append(pool, layer, d_k_new, d_v_new, d_bt, bt_stride,
-                     static_cast<const int32_t*>(plan->d_rows.ptr),
-                     static_cast<const int32_t*>(plan->d_pos.ptr), 0, plan->n_queries, s);
+                     plan->dev_rows, plan->dev_pos, 0, plan->n_queries, s);
   if (rc) return rc;
   return do_decode_fused(pool, plan, layer, d_q, d_out, d_bt, bt_stride, scale, nullptr, nullptr,
                          s, xt);
@@ -962,7 +964,7 @@ extern "C" int kvc_append_decode_rope(kvc_pool_t* pool, const kvc_plan_t* plan, 
   a.head_dim = g.head_dim;
   a.dtype = g.dtype;
   a.neox = neox ? 1 : 0;
-  a.positions = static_cast<const int32_t*>(plan->d_pos.ptr);
+  a.positions = plan->dev_pos;
   rope_inv_freq(freq_base, g.head_dim, a.inv_freq);
   if ((e = launch_rope(a, s, true)) != cudaSuccess) return cuda_error(e, "rope kernel");
   return append_then_decode(pool, plan, layer, q_rot, k_rot, d_v_new, d_out, d_block_tables,
