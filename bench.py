@@ -275,7 +275,11 @@ def run_b200(args, rank, world, local_rank):
         H = H * Hkv // cfg["Hkv"]
     cached = cached_lengths(cfg)
     ctx = cached + 1                                  # context includes the appended token
-    table, total_pages = paged.random_block_tables(ctx, args.page_size, cfg["seed"] + 17 * rank)
+    # --grow: every step appends one more position (a real decode loop), so pages
+    # for the extra positions are allocated up front
+    extra = (args.warmup + args.steps + 1) if args.grow else 0
+    table, total_pages = paged.random_block_tables(ctx + extra, args.page_size,
+                                                   cfg["seed"] + 17 * rank)
     pool = paged.PagedKVCache(L, total_pages, args.page_size, Hkv, D, dtype=torch.float16,
                               device=local_rank)
     pool.fill_normal(seed=1000 + rank, stddev=1.0)
@@ -312,9 +316,15 @@ def run_b200(args, rank, world, local_rank):
     plan.set_kv_stable(True)
     torch.cuda.synchronize()
 
+    grown = [0]  # steps taken so far (--grow)
+
     def step(events=None, s=None):
         # one fused launch per layer: append each sequence's new row + attend
         s = stream if s is None else s
+        if args.grow:
+            # the contexts grew by one since the last step: a new plan (host), then the layers
+            pool.plan(ctx + grown[0], H, plan=plan, stream=s)
+            grown[0] += 1
         for l in range(L):
             if events is not None:
                 events[l][0].record(s)
@@ -344,7 +354,7 @@ def run_b200(args, rank, world, local_rank):
     if code:
         raise RuntimeError(f"device error {code} ({info}) during warm-up")
     graph = None
-    if not args.no_graph and not args.launch_events:
+    if not args.no_graph and not args.launch_events and not args.grow:
         # The step's 2 x L launches are recorded once into a CUDA graph and replayed:
         # the same kernels, without the host's per-launch cost between them.
         graph = torch.cuda.CUDAGraph()
@@ -392,6 +402,12 @@ def run_b200(args, rank, world, local_rank):
         raise RuntimeError(f"device error {code} ({info}) during timing")
 
     kv_read, appended, qo = step_bytes(dict(cfg, H=H, Hkv=Hkv), ctx)
+    if args.grow:  # the timed steps ran at contexts ctx + warmup ... ctx + warmup + steps - 1
+        parts = [step_bytes(dict(cfg, H=H, Hkv=Hkv), ctx + args.warmup + i)
+                 for i in range(args.steps)]
+        kv_read, appended, qo = (sum(p[0] for p in parts) // args.steps,
+                                 sum(p[1] for p in parts) // args.steps,
+                                 sum(p[2] for p in parts) // args.steps)
     rank_bytes = kv_read + appended + qo
     # aggregate: max time over ranks, sum of bytes
     if world > 1:
@@ -506,6 +522,8 @@ def run_b200(args, rank, world, local_rank):
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
             "rope": bool(args.rope),
+            "grow": ("contexts grow by one position per step; the plan is rebuilt every step "
+                     "inside the timed region" if args.grow else False),
             "launch": ("one CUDA graph replay per step (the step's 2 x layers kernel launches)"
                        if used_graph else "direct launches from the host loop"),
             "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), "
@@ -715,6 +733,9 @@ def main():
     ap.add_argument("--one-rank-of", type=int, default=0,
                     help="profiling on one GPU: run rank 0's shard of an N-way KV-head split "
                          "with its head exchange connected to itself")
+    ap.add_argument("--grow", action="store_true",
+                    help="a real decode loop: contexts grow by one per step and the plan is "
+                         "rebuilt each step (no CUDA graph)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every kernel from the host loop instead of replaying a CUDA graph")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",

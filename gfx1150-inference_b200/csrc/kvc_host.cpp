@@ -123,17 +123,28 @@ int elem_size_of(int dtype) {
   }
 }
 
+// Growth of a buffer that already exists gets 25 % headroom (64 KiB granules):
+// plans grow a little every time a context crosses a split boundary, and a
+// reallocation (cudaFree synchronises the device) per crossing would cost far
+// more than the headroom.  First allocations are exact.
+static size_t grown_size(size_t cap, size_t bytes) {
+  if (cap == 0) return bytes;
+  const size_t want = bytes + bytes / 4;
+  return (want + 65535) & ~static_cast<size_t>(65535);
+}
+
 cudaError_t DevBuf::ensure(size_t bytes) {
   if (bytes <= cap) return cudaSuccess;
+  const size_t n = grown_size(cap, bytes);
   if (ptr) cudaFree(ptr);
   ptr = nullptr;
   cap = 0;
-  cudaError_t e = cudaMalloc(&ptr, bytes);
+  cudaError_t e = cudaMalloc(&ptr, n);
   if (e != cudaSuccess) {
     ptr = nullptr;
     return e;
   }
-  cap = bytes;
+  cap = n;
   return cudaSuccess;
 }
 
@@ -145,15 +156,16 @@ void DevBuf::release() {
 
 cudaError_t HostBuf::ensure(size_t bytes) {
   if (bytes <= cap) return cudaSuccess;
+  const size_t n = grown_size(cap, bytes);
   if (ptr) cudaFreeHost(ptr);
   ptr = nullptr;
   cap = 0;
-  cudaError_t e = cudaMallocHost(&ptr, bytes);
+  cudaError_t e = cudaMallocHost(&ptr, n);
   if (e != cudaSuccess) {
     ptr = nullptr;
     return e;
   }
-  cap = bytes;
+  cap = n;
   return cudaSuccess;
 }
 

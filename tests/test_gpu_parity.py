@@ -549,3 +549,43 @@ def test_append_decode_rope_equals_rope_then_append_decode():
         ref_k = gqa_ref.ref_rope(kn.cpu().numpy(), neox_style=neox, positions=pos.cpu().numpy(),
                                  inv_freq=gqa_ref.libm_inv_freq(500000.0, D))
         assert _maxerr(kr.cpu().numpy(), ref_k) < 2e-3
+
+
+def test_paged_decode_loop_with_growing_contexts():
+    """A serving loop: four decode steps over two layers, every step appending one
+    row per sequence at its next position and re-planning (contexts cross split
+    boundaries); each output against the oracle on the rows appended so far."""
+    rng = np.random.default_rng(23)
+    H, Hkv, D, ps, L, steps = 16, 4, 128, 16, 2, 4
+    start = np.array([510, 1, 1023, 47, 2047], dtype=np.int64)   # cached before the loop
+    table, total = paged.random_block_tables(start + steps, ps, 8)
+    pool = paged.PagedKVCache(L, total, ps, Hkv, D)
+    bt = torch.from_numpy(table).cuda()
+    n = len(start)
+    ks = [[rng.standard_normal((int(start[i]) + steps, Hkv, D), dtype=np.float32).astype(np.float16)
+           for i in range(n)] for _ in range(L)]
+    vs = [[rng.standard_normal((int(start[i]) + steps, Hkv, D), dtype=np.float32).astype(np.float16)
+           for i in range(n)] for _ in range(L)]
+    for l in range(L):  # the cached prefix
+        for i in range(n):
+            c = int(start[i])
+            pool.append(l, torch.from_numpy(ks[l][i][:c]).cuda(), torch.from_numpy(vs[l][i][:c]).cuda(),
+                        bt, torch.arange(c, dtype=torch.int32, device="cuda"),
+                        torch.full((c,), i, dtype=torch.int32, device="cuda"))
+    plan = None
+    for s in range(steps):
+        ctx = start + s + 1
+        plan = pool.plan(ctx, H, plan=plan)
+        for l in range(L):
+            q = rng.standard_normal((n, H, D), dtype=np.float32).astype(np.float16)
+            kn = np.stack([ks[l][i][ctx[i] - 1] for i in range(n)])
+            vn = np.stack([vs[l][i][ctx[i] - 1] for i in range(n)])
+            out = torch.zeros((n, H, D), dtype=torch.float16, device="cuda")
+            pool.append_decode(plan, l, torch.from_numpy(q).cuda(), torch.from_numpy(kn).cuda(),
+                               torch.from_numpy(vn).cuda(), out, bt, 0.09)
+            got = out.cpu().numpy()
+            for i in range(n):
+                c = int(ctx[i])
+                ref = gqa_ref.ref_gqa_attention(q[i:i + 1], ks[l][i][:c], vs[l][i][:c], c - 1, 0.09)
+                assert _maxerr(got[i:i + 1], ref) <= _fp16_tol(ref), (s, l, i)
+    assert ffi.device_error(0) == (0, 0)
