@@ -29,6 +29,8 @@ struct HostBuf {
 
 int set_error(int code, const char* fmt, ...);
 int cuda_error(cudaError_t e, const char* what);
+// cudaSetDevice with the library's status convention.
+int use_device(int device);
 int check_device_error(const char* what);
 int elem_size_of(int dtype);
 int make_geom(int num_layers, int num_pages, int page_size, int num_kv_heads, int head_dim,

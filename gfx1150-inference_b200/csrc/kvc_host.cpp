@@ -114,6 +114,11 @@ int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t byte
   return check_device_error(what);  // rare: read, clear and report
 }
 
+int use_device(int device) {
+  const cudaError_t e = cudaSetDevice(device);
+  return e == cudaSuccess ? KVC_OK : cuda_error(e, "cudaSetDevice");
+}
+
 int elem_size_of(int dtype) {
   switch (dtype) {
     case KVC_DTYPE_F16: return 2;
@@ -312,7 +317,7 @@ extern "C" int kvc_pool_fill_normal(kvc_pool_t* pool, int layer_begin, int layer
   if (layer_begin < 0 || layer_end > g.num_layers || layer_begin > layer_end || page_begin < 0 ||
       page_end > g.num_pages || page_begin > page_end)
     return set_error(KVC_ERR_OUT_OF_RANGE, "fill range outside the pool.");
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t elems_per_page = g.page_bytes / g.elem_size;
   const size_t elems_per_layer = g.layer_bytes / g.elem_size;
@@ -379,7 +384,7 @@ extern "C" int kvc_append(kvc_pool_t* pool, int layer, const void* d_k_new, cons
                           const int32_t* d_positions, int n, void* stream) {
   if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
   if (!d_positions) return set_error(KVC_ERR_INVALID_ARG, "positions must not be null.");
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   return do_append(pool, layer, d_k_new, d_v_new, d_block_tables, bt_stride, d_rows, d_positions,
                    0, n, static_cast<cudaStream_t>(stream));
 }
@@ -397,7 +402,7 @@ extern "C" int kvc_gather(kvc_pool_t* pool, int layer, const int32_t* d_block_ta
   if (row < 0) return set_error(KVC_ERR_OUT_OF_RANGE, "row must be non-negative.");
   if ((reinterpret_cast<uintptr_t>(d_k_out) | reinterpret_cast<uintptr_t>(d_v_out)) & 15u)
     return set_error(KVC_ERR_INVALID_ARG, "output buffers must be 16-byte aligned.");
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   GatherArgs a;
   a.k_layer = pool->k + static_cast<size_t>(layer) * g.layer_bytes;
   a.v_layer = pool->v + static_cast<size_t>(layer) * g.layer_bytes;
@@ -869,7 +874,7 @@ extern "C" int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const i
   if (!plan || !pool) return set_error(KVC_ERR_INVALID_ARG, "plan and pool must not be null.");
   if (n_queries > 0 && !h_ctx_lens)
     return set_error(KVC_ERR_INVALID_ARG, "ctx_lens must not be null.");
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   return plan_build(
       plan, pool->g, n_queries, num_heads, [&](int i) { return h_ctx_lens[i]; },
       [&](int i) { return h_rows ? h_rows[i] : i; }, pool->device,
@@ -897,7 +902,7 @@ extern "C" int kvc_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int layer, c
                           void* d_out, const int32_t* d_block_tables, int bt_stride, float scale,
                           void* stream) {
   if (!pool) return set_error(KVC_ERR_INVALID_ARG, "pool must not be null.");
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   return do_decode(pool, plan, layer, d_q, d_out, d_block_tables, bt_stride, scale,
                    static_cast<cudaStream_t>(stream));
 }
@@ -908,7 +913,7 @@ extern "C" int kvc_append_decode(kvc_pool_t* pool, const kvc_plan_t* plan, int l
                                  float scale, void* stream) {
   if (!pool || !plan) return set_error(KVC_ERR_INVALID_ARG, "pool and plan must not be null.");
   if (!plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return append_then_decode(pool, plan, layer, d_q, d_k_new, d_v_new, d_out, d_block_tables,
                             bt_stride, scale, s);
@@ -1009,7 +1014,7 @@ extern "C" int kvc_append_decode_rope(kvc_pool_t* pool, const kvc_plan_t* plan, 
   int rc = check_rope_args(plan->num_heads, g.head_dim, freq_base);
   if (rc) return rc;
   if (plan->n_queries == 0) return KVC_OK;
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   kvc_plan* p = const_cast<kvc_plan*>(plan);
   const size_t n = static_cast<size_t>(plan->n_queries);
@@ -1052,7 +1057,7 @@ extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int lay
   if (!h_q || !h_k_new || !h_v_new || !h_out)
     return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
   const PoolGeom& g = pool->g;
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t n = static_cast<size_t>(plan->n_queries);
   const size_t qb = n * plan->num_heads * g.head_dim * g.elem_size;
@@ -1268,7 +1273,7 @@ extern "C" int kvc_gqa_attention_cached(const void* h_Q, const void* h_K_new,
   if (q_len == 0) return KVC_OK;
   if (!h_Q || !h_K_new || !h_V_new || !h_Out)
     return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
-  cudaSetDevice(S.pool.device);
+  if (const int rc_dev = use_device(S.pool.device)) return rc_dev;
   const PoolGeom& g = S.pool.g;
   const size_t qb = static_cast<size_t>(q_len) * num_heads * head_dim * g.elem_size;
   const size_t kb = static_cast<size_t>(q_len) * num_kv_heads * head_dim * g.elem_size;
@@ -1301,7 +1306,7 @@ extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_
   int rc = validate_cached(S, layer_idx, q_len, start_pos, num_heads, num_kv_heads, head_dim);
   if (rc) return rc;
   if (q_len == 0) return KVC_OK;
-  cudaSetDevice(S.pool.device);
+  if (const int rc_dev = use_device(S.pool.device)) return rc_dev;
   return cached_attend(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_Q,
                        d_K_new, d_V_new, d_Out, layer_idx, q_len, start_pos, num_heads, scale,
                        causal != 0, static_cast<cudaStream_t>(stream));
@@ -1319,7 +1324,7 @@ extern "C" int kvc_cache_gather(int layer_idx, int start, int count, void* h_K_o
     return set_error(KVC_ERR_OUT_OF_RANGE, "gather range exceeds max_seq_len.");
   if (count == 0) return KVC_OK;
   if (!h_K_out || !h_V_out) return set_error(KVC_ERR_INVALID_ARG, "outputs must not be null.");
-  cudaSetDevice(S.pool.device);
+  if (const int rc_dev = use_device(S.pool.device)) return rc_dev;
   const PoolGeom& g = S.pool.g;
   const size_t rb = static_cast<size_t>(count) * g.num_kv_heads * g.head_dim * g.elem_size;
   const size_t rb_al = (rb + 255) & ~static_cast<size_t>(255);

@@ -371,7 +371,7 @@ extern "C" int kvc_offload_stats(const kvc_offload_t* off, double* h2d_bytes, do
   if (!off) return set_error(KVC_ERR_INVALID_ARG, "offload handle must not be null.");
   kvc_offload* o = const_cast<kvc_offload*>(off);
   std::lock_guard<std::mutex> lock(o->mu);
-  cudaSetDevice(o->device);
+  if (const int rc_dev = use_device(o->device)) return rc_dev;
   harvest(o, true);
   if (h2d_bytes) *h2d_bytes = o->h2d_bytes;
   if (h2d_ms) *h2d_ms = o->h2d_ms;

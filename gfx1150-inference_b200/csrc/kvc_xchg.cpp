@@ -70,7 +70,7 @@ extern "C" int kvc_xchg_create(int device, int rank, int world, size_t slot_byte
 
 extern "C" int kvc_xchg_handle(const kvc_xchg_t* x, void* handle_out) {
   if (!x || !handle_out) return set_error(KVC_ERR_INVALID_ARG, "exchange and handle_out must not be null.");
-  cudaSetDevice(x->device);
+  if (const int rc_dev = use_device(x->device)) return rc_dev;
   cudaIpcMemHandle_t h;
   cudaError_t e = cudaIpcGetMemHandle(&h, x->base);
   if (e != cudaSuccess) return cuda_error(e, "cudaIpcGetMemHandle");
@@ -172,7 +172,7 @@ extern "C" int kvc_append_decode_xchg(kvc_pool_t* pool, const kvc_plan_t* plan, 
   if (need > x->slot_bytes)
     return set_error(KVC_ERR_INVALID_ARG, "a slot holds %zu bytes, the outputs need %zu.",
                      x->slot_bytes, need);
-  cudaSetDevice(pool->device);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   XchgTarget xt{x, slot, total_heads, head_offset};
   if (!d_k_new && !d_v_new)
