@@ -1,6 +1,6 @@
 """Benchmark of the B200 KV-cache decode path (append + split-K GQA attention).
 
-Default workload (N=1 and the scaling run): BASELINE config 3, Llama-3-8B
+Default workload (N=1 and the scaling run): benchmark config 3, Llama-3-8B
 geometry batched decode — 32 layers, 32 q-heads, 8 KV heads, head_dim 128,
 32 sequences per GPU with cached lengths drawn U[1024, 8192] from a seed, one
 appended token each, fp16 paged pool of 16-token pages in a random page
@@ -509,7 +509,7 @@ def run_b200(args, rank, world, local_rank):
         "dtype": "f16 storage, f32 accumulate",
         "data": "synthetic: seeded N(0,1) K/V/q, random page permutation",
         "config": {
-            "workload": f"{cfg['workload']} (BASELINE config {args.config})"
+            "workload": f"{cfg['workload']} (benchmark config {args.config})"
                         + (f" [profiling subset: {L} layers]" if args.layers else "")
                         + (f" [profiling: one rank's shard of a {one_rank_of}-way KV-head split, "
                            "exchange connected to itself]" if one_rank_of > 1 else ""),
@@ -569,7 +569,7 @@ def run_b200(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------------
-# offload arm: KV in host memory, streamed per layer
+# offload arm (benchmark config 5): KV in host memory, streamed per layer
 # ---------------------------------------------------------------------------------
 def run_offload(args, rank, world, local_rank):
     """--offload-kv-cpu decode steps through the drop-in KVCacheManager: every
@@ -648,7 +648,7 @@ def run_offload(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "f16 storage, f32 accumulate",
         "data": "synthetic: seeded N(0,1) K/V/q (host KV filled from a tiled random block)",
-        "config": {"workload": f"{cfg['workload']} (BASELINE config {args.config})"
+        "config": {"workload": f"{cfg['workload']} (benchmark config {args.config})"
                                + (f" [subset: {L} layers]" if args.layers else ""),
                    "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D, "batch": 1,
                    "cached_len": cached, "host_kv_gb": round(kv_bytes / 1e9, 2),
@@ -706,7 +706,7 @@ def run_reference(args, rank, world):
         "vs_baseline": None,
         "dtype": "f16 storage, f32 accumulate",
         "data": "synthetic: seeded N(0,1) K/V/q",
-        "config": {"workload": f"{cfg['workload']} (BASELINE config {args.config})",
+        "config": {"workload": f"{cfg['workload']} (benchmark config {args.config})",
                    "layers": cfg["layers"], "q_heads": cfg["H"], "kv_heads": cfg["Hkv"],
                    "head_dim": cfg["D"], "sequences": cfg["batch"],
                    "ctx_tokens": int(ctx.sum())},

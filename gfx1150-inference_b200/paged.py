@@ -260,7 +260,7 @@ def pages_for(ctx_lens: Sequence[int], page_size: int) -> np.ndarray:
 
 def random_block_tables(ctx_lens: Sequence[int], page_size: int, seed: int):
     """Block tables for sequences of the given lengths over a pool with exactly
-    the pages they need, assigned in a seeded random permutation (BASELINE
+    the pages they need, assigned in a seeded random permutation (benchmark
     config 3: "paged fp16 pool of 16-token pages with a random page permutation").
     Returns (table (n, max_pages) int32 numpy, total pages)."""
     need = pages_for(ctx_lens, page_size)

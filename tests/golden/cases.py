@@ -60,7 +60,7 @@ def kv_manager_case():
 
 
 def config1_case():
-    """BASELINE config 1 (TinyLlama-1.1B geometry, one layer): 32 q-heads, 4 KV
+    """benchmark config 1 (TinyLlama-1.1B geometry, one layer): 32 q-heads, 4 KV
     heads, D=64, batch 1, 511 cached + 1 appended positions, fp32 N(0,1), scale
     1/sqrt(64), causal over 512 positions (seed 1)."""
     rng = np.random.default_rng(1)

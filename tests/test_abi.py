@@ -88,7 +88,7 @@ def test_status_code_mapping():
 
 def test_split_length_model_on_the_baseline_shapes():
     """The plan's split length (host-only model, kvc_plan_split_tokens) for the
-    BASELINE shapes on a 148-SM B200: 512 for the ragged batch and the unsharded
+    benchmark shapes on a 148-SM B200: 512 for the ragged batch and the unsharded
     70B shape, one wave of equal units for long even contexts and their KV-head
     shards, and the 4K single sequence."""
     import ctypes

@@ -1,6 +1,6 @@
 """CUDA parity tests (B200): every entry point against the pinned oracle.
 
-Tolerances (BASELINE north star and the reference's own tests):
+Tolerances (the north-star tolerances and the reference's own tests):
   fp32 storage                 max-abs <= 1e-5
   fp16 storage, fp32 accumulate max-abs <= 2e-3 * max(1, max|ref|)
                                (test_layer.py:179 uses 2e-3, test_full_model.py:104/124 1e-3)
@@ -124,7 +124,7 @@ def test_gpu_kv_cache_manager_reference_sequence():
 
 
 def test_config1_fp32_pool_within_1e5():
-    """fp32 pool, 511 cached + 1 appended, max-abs 1e-5."""
+    """benchmark config 1: fp32 pool, 511 cached + 1 appended, max-abs 1e-5."""
     c = cases.config1_case()
     P, H, Hkv, D = c["kv_len"], 32, 4, 64
     matmul_module.kv_cache_init_ex(1, P, Hkv, D, dtype=np.float32)
