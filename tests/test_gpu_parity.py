@@ -1,6 +1,6 @@
 """CUDA parity tests (B200): every entry point against the pinned oracle.
 
-Tolerances (the north-star tolerances and the reference's own tests):
+Tolerances (the path's parity targets and the reference's own tests):
   fp32 storage                 max-abs <= 1e-5
   fp16 storage, fp32 accumulate max-abs <= 2e-3 * max(1, max|ref|)
                                (test_layer.py:179 uses 2e-3, test_full_model.py:104/124 1e-3)
