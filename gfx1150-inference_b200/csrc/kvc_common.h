@@ -46,6 +46,7 @@ struct kvc_pool {
   uint8_t* v = nullptr;
   size_t cap_bytes = 0;   // bytes allocated per K (and per V), grow-only
   kvc::DevBuf io;         // staging for the host-buffer entry points
+  kvc::HostBuf io_host;   // page-locked staging of pageable host buffers
 };
 
 // Split-K decode plan for one batch of queries.
@@ -63,6 +64,10 @@ struct kvc_plan {
   std::vector<int4> sched_recs;   // 3 per scheduled unit
   std::vector<int32_t> merge_queries;
   int n_sched_ctas = 0, n_units = 0;
+  // Inputs of the last successful build (geometry, queries, contexts, rows): a
+  // build with the same inputs keeps the uploaded plan (every layer of one
+  // decode step plans the same queries).
+  std::vector<int32_t> built_from;
   kvc::DevBuf d_blob;          // items, qinfo, rows, positions, unit records, merge list, counter
   kvc::DevBuf d_part_o, d_part_ml, d_counters;
   // parts of d_blob (set by the upload)
@@ -86,6 +91,7 @@ struct kvc_plan {
     h_stage.release();
     if (upload_done) cudaEventDestroy(upload_done);
     upload_done = nullptr;
+    built_from.clear();
     valid = false;
   }
 };
@@ -128,6 +134,24 @@ void* mapped_host_ptr(void* h);
 // report a device error under `what`.
 int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t bytes,
                      const char* what);
+
+// Host buffers of one host-buffer call (q, new K rows, new V rows; out).
+// stage_host_call moves the inputs to d_in[] with the input staging kernel,
+// which lets the decode behind it start streaming KV: page-locked inputs are
+// read in place, pageable ones are first copied (on the CPU) into `pinned`.  It
+// also picks where the kernels write the output: the host buffer itself when it
+// is page-locked, else a page-locked block of `pinned` (*out_dev), which
+// finish_staged_call copies to the host buffer after the wait.  The caller's
+// previous call on the stream must have completed (every host-buffer call waits).
+struct HostCallStage {
+  void* out_dev = nullptr;      // where the kernels write the output
+  void* out_bounce = nullptr;   // page-locked copy source after the wait (or null)
+};
+int stage_host_call(kvc::HostBuf& pinned, const void* const h_in[3], const size_t in_bytes[3],
+                    uint8_t* const d_in[3], void* h_out, size_t out_bytes, cudaStream_t s,
+                    HostCallStage* st);
+int finish_staged_call(cudaStream_t s, void* h_out, const HostCallStage& st, size_t out_bytes,
+                       const char* what);
 
 int pool_alloc(kvc_pool* p, const PoolGeom& g, int device);
 void pool_release(kvc_pool* p);

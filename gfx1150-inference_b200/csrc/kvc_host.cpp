@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 #include <queue>
@@ -47,11 +48,14 @@ int cuda_error(cudaError_t e, const char* what) {
 
 void clear_error() { g_last_error.clear(); }
 
+std::atomic<uint32_t> g_device_errors{0};
+
 int check_device_error(const char* what) {
   uint32_t code = 0, info = 0;
   cudaError_t e = read_device_error(&code, &info, true);
   if (e != cudaSuccess) return cuda_error(e, what);
   if (code == KVC_DEVERR_NONE) return KVC_OK;
+  g_device_errors.fetch_add(1);
   const char* name = code == KVC_DEVERR_BAD_PAGE       ? "block table entry out of range"
                      : code == KVC_DEVERR_WAIT_LIMIT   ? "pipeline wait gave up after its time limit"
                      : code == KVC_DEVERR_BAD_POSITION ? "append position outside the block table"
@@ -112,6 +116,60 @@ int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t byte
   if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
   if ((reinterpret_cast<volatile uint32_t*>(m->host)[0]) == KVC_DEVERR_NONE) return KVC_OK;
   return check_device_error(what);  // rare: read, clear and report
+}
+
+int stage_host_call(HostBuf& pinned, const void* const h_in[3], const size_t in_bytes[3],
+                    uint8_t* const d_in[3], void* h_out, size_t out_bytes, cudaStream_t s,
+                    HostCallStage* st) {
+  auto al16 = [](size_t b) { return (b + 15) & ~static_cast<size_t>(15); };
+  const void* src[3] = {nullptr, nullptr, nullptr};
+  size_t need = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (!in_bytes[i]) continue;
+    src[i] = mapped_host_ptr(const_cast<void*>(h_in[i]));
+    if (!src[i] || (reinterpret_cast<uintptr_t>(src[i]) & 15u)) {
+      src[i] = nullptr;
+      need += al16(in_bytes[i]);
+    }
+  }
+  void* out_direct = out_bytes ? mapped_host_ptr(h_out) : nullptr;
+  const size_t out_off = al16(need);
+  const size_t total = out_off + (out_direct ? 0 : al16(out_bytes));
+  uint8_t* hp = nullptr;
+  uint8_t* dp = nullptr;
+  if (total) {
+    cudaError_t e = pinned.ensure(total);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMallocHost(call staging)");
+    hp = static_cast<uint8_t*>(pinned.ptr);
+    dp = static_cast<uint8_t*>(mapped_host_ptr(pinned.ptr));
+    if (!dp) return set_error(KVC_ERR_CUDA, "page-locked staging is not mapped on the device");
+  }
+  size_t off = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (!in_bytes[i] || src[i]) continue;
+    memcpy(hp + off, h_in[i], in_bytes[i]);
+    src[i] = dp + off;
+    off += al16(in_bytes[i]);
+  }
+  StageArgs a;
+  for (int i = 0; i < 3; ++i) {
+    a.src[i] = static_cast<const uint8_t*>(src[i]);
+    a.dst[i] = d_in[i];
+    a.bytes[i] = src[i] ? in_bytes[i] : 0;
+  }
+  cudaError_t e = launch_stage_inputs(a, s);
+  if (e != cudaSuccess) return cuda_error(e, "input staging kernel");
+  st->out_dev = out_direct ? out_direct : (out_bytes ? dp + out_off : nullptr);
+  st->out_bounce = out_direct ? nullptr : (out_bytes ? hp + out_off : nullptr);
+  return KVC_OK;
+}
+
+int finish_staged_call(cudaStream_t s, void* h_out, const HostCallStage& st, size_t out_bytes,
+                       const char* what) {
+  const int rc = finish_host_call(s, h_out, nullptr, 0, what);
+  if (rc) return rc;
+  if (st.out_bounce && out_bytes) memcpy(h_out, st.out_bounce, out_bytes);
+  return KVC_OK;
 }
 
 int use_device(int device) {
@@ -250,6 +308,8 @@ void pool_release(kvc_pool* p) {
   if (p->v) cudaFree(p->v);
   p->k = p->v = nullptr;
   p->cap_bytes = 0;
+  p->io.release();
+  p->io_host.release();
   p->g = PoolGeom();
 }
 
@@ -264,6 +324,7 @@ extern "C" int kvc_device_error(int device, int clear, uint32_t* code, uint32_t*
   if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
   e = read_device_error(code, info, clear != 0);
   if (e != cudaSuccess) return cuda_error(e, "read_device_error");
+  if (code && *code != KVC_DEVERR_NONE) g_device_errors.fetch_add(1);
   return KVC_OK;
 }
 
@@ -524,6 +585,19 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
     return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
   std::vector<int> ctxs(std::max(0, n_queries));
   for (int i = 0; i < n_queries; ++i) ctxs[i] = ctx_of(i);
+  std::vector<int32_t> inputs = {n_queries, num_heads, g.num_kv_heads, g.head_dim, g.page_size,
+                                 g.dtype, device};
+  inputs.reserve(inputs.size() + 2 * static_cast<size_t>(std::max(0, n_queries)));
+  for (int i = 0; i < n_queries; ++i) inputs.push_back(ctxs[i]);
+  for (int i = 0; i < n_queries; ++i) inputs.push_back(row_of(i));
+  // a kernel that gave up may have left the plan's unit counter armed: rebuild
+  inputs.push_back(static_cast<int32_t>(g_device_errors.load()));
+  if (p->valid && inputs == p->built_from) {
+    p->pool_geom = g;
+    return KVC_OK;
+  }
+  p->valid = false;
+  p->built_from.clear();
   const int C = choose_split_tokens(g.page_size, ctxs.data(), n_queries,
                                     g.num_kv_heads * ((num_heads / g.num_kv_heads + 7) / 8),
                                     device);
@@ -720,6 +794,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->dev_queue = reinterpret_cast<unsigned*>(d + o_queue);
   if ((e = cudaEventRecord(p->upload_done, s))) return cuda_error(e, "cudaEventRecord(plan)");
   p->pool_geom = g;
+  p->built_from.swap(inputs);
   p->valid = true;
   return KVC_OK;
 }
@@ -1064,45 +1139,21 @@ extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int lay
   const size_t kb = n * g.num_kv_heads * g.head_dim * g.elem_size;
   const size_t kb_al = (kb + 255) & ~static_cast<size_t>(255);
   const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
-  cudaError_t e = pool->io.ensure(2 * qb_al + 2 * kb_al);
+  cudaError_t e = pool->io.ensure(qb_al + 2 * kb_al);
   if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(io)");
   uint8_t* d = static_cast<uint8_t*>(pool->io.ptr);
-  uint8_t* d_q = d;
-  uint8_t* d_out = d + qb_al;
-  uint8_t* d_k = d + 2 * qb_al;
-  uint8_t* d_v = d_k + kb_al;
-  // Page-locked inputs are read by a staging kernel that lets the decode stream
-  // KV meanwhile (the staging kernel writes no pages or block tables, so the
-  // decode may start early); other inputs are copied by the copy engine.
-  const void* mq = mapped_host_ptr(const_cast<void*>(h_q));
-  const void* mk = mapped_host_ptr(const_cast<void*>(h_k_new));
-  const void* mv = mapped_host_ptr(const_cast<void*>(h_v_new));
-  const bool staged = mq && mk && mv &&
-      ((reinterpret_cast<uintptr_t>(mq) | reinterpret_cast<uintptr_t>(mk) |
-        reinterpret_cast<uintptr_t>(mv)) & 15u) == 0;
-  if (staged) {
-    StageArgs st;
-    st.src[0] = static_cast<const uint8_t*>(mq);
-    st.src[1] = static_cast<const uint8_t*>(mk);
-    st.src[2] = static_cast<const uint8_t*>(mv);
-    st.dst[0] = d_q;
-    st.dst[1] = d_k;
-    st.dst[2] = d_v;
-    st.bytes[0] = qb;
-    st.bytes[1] = kb;
-    st.bytes[2] = kb;
-    if ((e = launch_stage_inputs(st, s))) return cuda_error(e, "input staging kernel");
-  } else if ((e = cudaMemcpyAsync(d_q, h_q, qb, cudaMemcpyHostToDevice, s)) ||
-             (e = cudaMemcpyAsync(d_k, h_k_new, kb, cudaMemcpyHostToDevice, s)) ||
-             (e = cudaMemcpyAsync(d_v, h_v_new, kb, cudaMemcpyHostToDevice, s))) {
-    return cuda_error(e, "cudaMemcpyAsync(H2D)");
-  }
-  // page-locked output: the kernels write it directly, no device copy and D2H
-  void* direct = mapped_host_ptr(h_out);
-  int rc = append_then_decode(pool, plan, layer, d_q, d_k, d_v, direct ? direct : d_out,
-                              d_block_tables, bt_stride, scale, s, nullptr, staged ? 1 : -1);
+  uint8_t* const d_in[3] = {d, d + qb_al, d + qb_al + kb_al};  // q, new K rows, new V rows
+  // Inputs reach the device through the staging kernel (it writes no pages or
+  // block tables, so the decode behind it may start streaming KV early).
+  const void* h_in[3] = {h_q, h_k_new, h_v_new};
+  const size_t in_b[3] = {qb, kb, kb};
+  HostCallStage st;
+  int rc = stage_host_call(pool->io_host, h_in, in_b, d_in, h_out, qb, s, &st);
   if (rc) return rc;
-  return finish_host_call(s, h_out, direct ? nullptr : d_out, qb, "kvc_decode_host");
+  rc = append_then_decode(pool, plan, layer, d_in[0], d_in[1], d_in[2], st.out_dev, d_block_tables,
+                          bt_stride, scale, s, nullptr, 1);
+  if (rc) return rc;
+  return finish_staged_call(s, h_out, st, qb, "kvc_decode_host");
 }
 
 // ============================================================================
@@ -1211,18 +1262,24 @@ int validate_cached(const Singleton& S, int layer_idx, int q_len, int start_pos,
 }
 
 // Append q_len rows at start_pos of row 0 and attend for queries m = 0..q_len-1.
-int cached_attend(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_len,
-                  const void* d_Q, const void* d_Kn, const void* d_Vn, void* d_Out, int layer_idx,
-                  int q_len, int start_pos, int num_heads, float scale, bool causal,
-                  cudaStream_t s) {
-  const int kv_len = start_pos + q_len;
-  int rc = plan_queries(plan, pool->g, q_len, num_heads, start_pos, kv_len, causal, pool->device,
-                        s);
-  if (rc) return rc;
+// Plans the call's queries.  Run before any input staging so that the plan's
+// upload does not sit between the staging kernel and the attention kernel.
+int cached_plan(kvc_pool* pool, kvc_plan* plan, int q_len, int start_pos, int num_heads,
+                bool causal, cudaStream_t s) {
+  return plan_queries(plan, pool->g, q_len, num_heads, start_pos, start_pos + q_len, causal,
+                      pool->device, s);
+}
+
+// Appends the call's rows and attends over the planned queries.  early = 1
+// when the launch directly before is the input staging kernel.
+int cached_run(kvc_pool* pool, const kvc_plan* plan, const int32_t* d_bt, int bt_len,
+               const void* d_Q, const void* d_Kn, const void* d_Vn, void* d_Out, int layer_idx,
+               int q_len, int start_pos, float scale, cudaStream_t s, int early) {
   if (q_len == 1)  // a decode step: the row append runs inside the attention kernel
     return append_then_decode(pool, plan, layer_idx, d_Q, d_Kn, d_Vn, d_Out, d_bt, bt_len, scale,
-                              s);
-  rc = do_append(pool, layer_idx, d_Kn, d_Vn, d_bt, bt_len, nullptr, nullptr, start_pos, q_len, s);
+                              s, nullptr, early);
+  int rc =
+      do_append(pool, layer_idx, d_Kn, d_Vn, d_bt, bt_len, nullptr, nullptr, start_pos, q_len, s);
   if (rc) return rc;
   return do_decode(pool, plan, layer_idx, d_Q, d_Out, d_bt, bt_len, scale, s);
 }
@@ -1279,21 +1336,20 @@ extern "C" int kvc_gqa_attention_cached(const void* h_Q, const void* h_K_new,
   const size_t kb = static_cast<size_t>(q_len) * num_kv_heads * head_dim * g.elem_size;
   const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
   const size_t kb_al = (kb + 255) & ~static_cast<size_t>(255);
-  cudaError_t e = S.pool.io.ensure(2 * qb_al + 2 * kb_al);
+  cudaError_t e = S.pool.io.ensure(qb_al + 2 * kb_al);
   if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(io)");
   uint8_t* d = static_cast<uint8_t*>(S.pool.io.ptr);
-  uint8_t *d_q = d, *d_out = d + qb_al, *d_k = d + 2 * qb_al, *d_v = d + 2 * qb_al + kb_al;
+  uint8_t* const d_in[3] = {d, d + qb_al, d + qb_al + kb_al};  // q, new K rows, new V rows
   cudaStream_t s = S.stream;
-  if ((e = cudaMemcpyAsync(d_k, h_K_new, kb, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(d_v, h_V_new, kb, cudaMemcpyHostToDevice, s)) ||
-      (e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
-    return cuda_error(e, "cudaMemcpyAsync(H2D)");
-  void* direct = mapped_host_ptr(h_Out);
-  rc = cached_attend(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_q, d_k,
-                     d_v, direct ? static_cast<uint8_t*>(direct) : d_out, layer_idx, q_len,
-                     start_pos, num_heads, scale, causal != 0, s);
+  if ((rc = cached_plan(&S.pool, &S.plan, q_len, start_pos, num_heads, causal != 0, s))) return rc;
+  const void* h_in[3] = {h_Q, h_K_new, h_V_new};
+  const size_t in_b[3] = {qb, kb, kb};
+  HostCallStage st;
+  if ((rc = stage_host_call(S.pool.io_host, h_in, in_b, d_in, h_Out, qb, s, &st))) return rc;
+  rc = cached_run(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_in[0],
+                  d_in[1], d_in[2], st.out_dev, layer_idx, q_len, start_pos, scale, s, 1);
   if (rc) return rc;
-  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "gqa_attention_cached");
+  return finish_staged_call(s, h_Out, st, qb, "gqa_attention_cached");
 }
 
 extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_new,
@@ -1307,9 +1363,10 @@ extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_
   if (rc) return rc;
   if (q_len == 0) return KVC_OK;
   if (const int rc_dev = use_device(S.pool.device)) return rc_dev;
-  return cached_attend(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_Q,
-                       d_K_new, d_V_new, d_Out, layer_idx, q_len, start_pos, num_heads, scale,
-                       causal != 0, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = cached_plan(&S.pool, &S.plan, q_len, start_pos, num_heads, causal != 0, s))) return rc;
+  return cached_run(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_Q,
+                    d_K_new, d_V_new, d_Out, layer_idx, q_len, start_pos, scale, s, -1);
 }
 
 extern "C" int kvc_cache_gather(int layer_idx, int start, int count, void* h_K_out,
@@ -1382,23 +1439,25 @@ extern "C" int kvc_gqa_attention_ex(const void* h_Q, const void* h_K, const void
   const size_t qb = static_cast<size_t>(q_len) * num_heads * head_dim * es;
   const size_t kvb_al = (kvb + 255) & ~static_cast<size_t>(255);
   const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
-  if ((e = C.bounce.ensure(2 * kvb_al + 2 * qb_al))) return cuda_error(e, "cudaMalloc(bounce)");
+  if ((e = C.bounce.ensure(2 * kvb_al + qb_al))) return cuda_error(e, "cudaMalloc(bounce)");
   uint8_t* d = static_cast<uint8_t*>(C.bounce.ptr);
-  uint8_t *d_k = d, *d_v = d + kvb_al, *d_q = d + 2 * kvb_al, *d_out = d + 2 * kvb_al + qb_al;
+  uint8_t *d_k = d, *d_v = d + kvb_al, *d_q = d + 2 * kvb_al;
+  // the whole K/V crosses on the copy engine; q and the output like the cached call
   if (kvb > 0 && ((e = cudaMemcpyAsync(d_k, h_K, kvb, cudaMemcpyHostToDevice, s)) ||
                   (e = cudaMemcpyAsync(d_v, h_V, kvb, cudaMemcpyHostToDevice, s))))
     return cuda_error(e, "cudaMemcpyAsync(H2D K/V)");
-  if ((e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
-    return cuda_error(e, "cudaMemcpyAsync(H2D Q)");
   const int32_t* bt = static_cast<const int32_t*>(C.bt.ptr);
   if ((rc = do_append(&C.pool, 0, d_k, d_v, bt, C.bt_len, nullptr, nullptr, 0, kv_len, s)))
     return rc;
   rc = plan_queries(&C.plan, g, q_len, num_heads, start_pos, kv_len, causal != 0, device, s);
   if (rc) return rc;
-  void* direct = mapped_host_ptr(h_Out);
-  if ((rc = do_decode(&C.pool, &C.plan, 0, d_q, direct ? direct : d_out, bt, C.bt_len, scale, s)))
-    return rc;
-  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "gqa_attention");
+  const void* h_in[3] = {h_Q, nullptr, nullptr};
+  const size_t in_b[3] = {qb, 0, 0};
+  uint8_t* const d_in[3] = {d_q, nullptr, nullptr};
+  HostCallStage st;
+  if ((rc = stage_host_call(C.pool.io_host, h_in, in_b, d_in, h_Out, qb, s, &st))) return rc;
+  if ((rc = do_decode(&C.pool, &C.plan, 0, d_q, st.out_dev, bt, C.bt_len, scale, s))) return rc;
+  return finish_staged_call(s, h_Out, st, qb, "gqa_attention");
 }
 
 extern "C" int kvc_gqa_attention(const void* h_Q, const void* h_K, const void* h_V, void* h_Out,

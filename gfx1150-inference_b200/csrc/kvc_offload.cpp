@@ -46,7 +46,8 @@ struct kvc_offload {
   DevBuf bt;                // identity block table of the slot
   int bt_len = 0;
   kvc_plan plan;
-  DevBuf io;                // q / out device staging
+  DevBuf io;                // q device staging
+  HostBuf io_host;          // page-locked staging of pageable q / out
 
   struct Bounce {
     DevBuf k, v;            // token-major rows of one layer
@@ -149,6 +150,7 @@ void destroy_locked(kvc_offload* o) {
   o->mstage_v.release();
   o->bt.release();
   o->io.release();
+  o->io_host.release();
   o->plan.release();
   if (o->registered) {
     cudaHostUnregister(o->h_k);
@@ -168,6 +170,16 @@ namespace {
 // how many of its rows are final now: within a step the prefix [0, start_pos);
 // a layer of the next step [0, total).  Prefetch it into bounce `bi` unless a
 // bounce already holds it.
+// The query reaches d_q through the input staging kernel; the output goes where
+// stage_host_call puts it (the host buffer itself when page-locked).
+int stage_q(kvc_offload* o, const void* h_Q, uint8_t* d_q, size_t qb, void* h_Out, cudaStream_t s,
+            HostCallStage* st) {
+  const void* h_in[3] = {h_Q, nullptr, nullptr};
+  const size_t in_b[3] = {qb, 0, 0};
+  uint8_t* const d_in[3] = {d_q, nullptr, nullptr};
+  return stage_host_call(o->io_host, h_in, in_b, d_in, h_Out, qb, s, st);
+}
+
 int prefetch_next(kvc_offload* o, int layer, int start_pos, int total, int bi) {
   if (o->n_mirror >= o->num_layers) return KVC_OK;  // nothing is streamed
   // mirrored layers are [0, n_mirror): the next streamed one in this step, or the
@@ -218,20 +230,16 @@ int attend_mirrored(kvc_offload* o, const void* h_Q, void* h_Out, int layer, int
   if ((rc = prefetch_next(o, layer, start_pos, total, 1 - o->last_used))) return rc;
 
   const size_t qb = static_cast<size_t>(q_len) * num_heads * o->head_dim * o->es;
-  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
-  if ((e = o->io.ensure(2 * qb_al))) return cuda_error(e, "cudaMalloc(io)");
+  if ((e = o->io.ensure(qb))) return cuda_error(e, "cudaMalloc(io)");
   uint8_t* d_q = static_cast<uint8_t*>(o->io.ptr);
-  uint8_t* d_out = d_q + qb_al;
-  if ((e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
-    return cuda_error(e, "cudaMemcpyAsync(Q)");
   if ((rc = plan_queries(&o->plan, o->mirror.g, q_len, num_heads, start_pos, total, causal != 0,
                          o->device, s)))
     return rc;
-  void* direct = mapped_host_ptr(h_Out);
-  if ((rc = do_decode(&o->mirror, &o->plan, layer, d_q, direct ? direct : d_out, bt, o->bt_len,
-                      scale, s)))
+  HostCallStage st;
+  if ((rc = stage_q(o, h_Q, d_q, qb, h_Out, s, &st))) return rc;
+  if ((rc = do_decode(&o->mirror, &o->plan, layer, d_q, st.out_dev, bt, o->bt_len, scale, s)))
     return rc;
-  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "offload attend");
+  return finish_staged_call(s, h_Out, st, qb, "offload attend");
 }
 
 }  // namespace
@@ -437,13 +445,11 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
 
   // 4. compute stream: scatter the rows into the paged slot, attend, copy out.
   const size_t qb = static_cast<size_t>(q_len) * num_heads * o->head_dim * o->es;
-  const size_t qb_al = (qb + 255) & ~static_cast<size_t>(255);
-  if ((e = o->io.ensure(2 * qb_al))) return cuda_error(e, "cudaMalloc(io)");
+  if ((e = o->io.ensure(qb))) return cuda_error(e, "cudaMalloc(io)");
   uint8_t* d_q = static_cast<uint8_t*>(o->io.ptr);
-  uint8_t* d_out = d_q + qb_al;
   cudaStream_t s = o->compute;
-  if ((e = cudaMemcpyAsync(d_q, h_Q, qb, cudaMemcpyHostToDevice, s)))
-    return cuda_error(e, "cudaMemcpyAsync(Q)");
+  HostCallStage st;
+  if ((rc = stage_q(o, h_Q, d_q, qb, h_Out, s, &st))) return rc;
   if ((e = cudaStreamWaitEvent(s, B.ready, 0))) return cuda_error(e, "cudaStreamWaitEvent");
   const int32_t* bt = static_cast<const int32_t*>(o->bt.ptr);
   if ((rc = do_append(&o->slot, 0, B.k.ptr, B.v.ptr, bt, o->bt_len, nullptr, nullptr, 0, total, s)))
@@ -452,9 +458,6 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
   if ((rc = plan_queries(&o->plan, o->slot.g, q_len, num_heads, start_pos, total, causal != 0,
                          o->device, s)))
     return rc;
-  void* direct = mapped_host_ptr(h_Out);
-  if ((rc = do_decode(&o->slot, &o->plan, 0, d_q, direct ? direct : d_out, bt, o->bt_len, scale,
-                      s)))
-    return rc;
-  return finish_host_call(s, h_Out, direct ? nullptr : d_out, qb, "offload attend");
+  if ((rc = do_decode(&o->slot, &o->plan, 0, d_q, st.out_dev, bt, o->bt_len, scale, s))) return rc;
+  return finish_staged_call(s, h_Out, st, qb, "offload attend");
 }
