@@ -153,6 +153,43 @@ int stage_host_call(kvc::HostBuf& pinned, const void* const h_in[3], const size_
 int finish_staged_call(cudaStream_t s, void* h_out, const HostCallStage& st, size_t out_bytes,
                        const char* what);
 
+// Plans q_len queries at start_pos (row 0 of the block table) of a single
+// sequence; run before any input staging so the plan's upload does not sit
+// between the staging kernel and the attention kernel.
+int cached_plan(kvc_pool* pool, kvc_plan* plan, int q_len, int start_pos, int num_heads,
+                bool causal, cudaStream_t s);
+// Appends the q_len rows and attends over the planned queries; early = 1 when the
+// launch directly before writes no KV pages (input staging, RoPE).
+int cached_run(kvc_pool* pool, const kvc_plan* plan, const int32_t* d_bt, int bt_len,
+               const void* d_Q, const void* d_Kn, const void* d_Vn, void* d_Out, int layer_idx,
+               int q_len, int start_pos, float scale, cudaStream_t s, int early);
+
+// ---- layer pipeline (kvc_layer_host.cpp) ----
+struct LayerDims {
+  int layer = 0, seq = 0, pos = 0;
+  int hidden = 0, inter = 0, H = 0, Hkv = 0, D = 0;
+  float eps = 0.f, base = 0.f, scale = 0.f;
+  bool neox = false;
+};
+// Device pointers of one layer; w / type in the order q, k, v, o, gate, up, down.
+struct LayerIO {
+  const __half* x_in = nullptr;
+  __half* x_out = nullptr;
+  const __half* attn_norm = nullptr;
+  const __half* ffn_norm = nullptr;
+  const void* w[7] = {};
+  int type[7] = {};
+};
+int check_weight(int w_type, int n, int k, const char* name);
+size_t weight_size(int w_type, int n, int k);
+int check_layer(const LayerDims& d, const int* types);
+// Total bytes (256-byte aligned parts) of the seven weights; each[i] unpadded.
+size_t layer_weight_bytes(const LayerDims& d, const int* types, size_t* each);
+int run_linear(const void* x, int m, int k, int w_type, const void* const* w, const int* n,
+               void* const* out, int n_seg, int epi, const void* res, cudaStream_t s);
+int layer_forward(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_len, DevBuf& ws,
+                  const LayerIO& io, const LayerDims& d, cudaStream_t s);
+
 int pool_alloc(kvc_pool* p, const PoolGeom& g, int device);
 void pool_release(kvc_pool* p);
 int do_append(kvc_pool* pool, int layer, const void* d_k_new, const void* d_v_new,

@@ -1171,6 +1171,8 @@ struct Singleton {
   kvc_plan plan;
   cudaStream_t stream = nullptr;
   int stream_device = -1;
+  DevBuf layer_ws;           // intermediates of forward_layer_cached
+  DevBuf layer_io;           // its host inputs (activations, norms, weights) on the device
 };
 
 Singleton& singleton() {
@@ -1261,17 +1263,16 @@ int validate_cached(const Singleton& S, int layer_idx, int q_len, int start_pos,
   return KVC_OK;
 }
 
-// Append q_len rows at start_pos of row 0 and attend for queries m = 0..q_len-1.
-// Plans the call's queries.  Run before any input staging so that the plan's
-// upload does not sit between the staging kernel and the attention kernel.
+}  // namespace
+
+namespace kvc {
+
 int cached_plan(kvc_pool* pool, kvc_plan* plan, int q_len, int start_pos, int num_heads,
                 bool causal, cudaStream_t s) {
   return plan_queries(plan, pool->g, q_len, num_heads, start_pos, start_pos + q_len, causal,
                       pool->device, s);
 }
 
-// Appends the call's rows and attends over the planned queries.  early = 1
-// when the launch directly before is the input staging kernel.
 int cached_run(kvc_pool* pool, const kvc_plan* plan, const int32_t* d_bt, int bt_len,
                const void* d_Q, const void* d_Kn, const void* d_Vn, void* d_Out, int layer_idx,
                int q_len, int start_pos, float scale, cudaStream_t s, int early) {
@@ -1284,7 +1285,7 @@ int cached_run(kvc_pool* pool, const kvc_plan* plan, const int32_t* d_bt, int bt
   return do_decode(pool, plan, layer_idx, d_Q, d_Out, d_bt, bt_len, scale, s);
 }
 
-}  // namespace
+}  // namespace kvc
 
 extern "C" int kvc_cache_init(int num_layers, int max_seq_len, int num_kv_heads, int head_dim) {
   Singleton& S = singleton();
@@ -1306,6 +1307,8 @@ extern "C" int kvc_cache_free(void) {
   if (S.pool.k || S.pool.v) {
     cudaSetDevice(S.pool.device);
     pool_release(&S.pool);
+    S.layer_ws.release();
+    S.layer_io.release();
   }
   S.live = false;
   S.max_seq_len = 0;
@@ -1367,6 +1370,127 @@ extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_
   if ((rc = cached_plan(&S.pool, &S.plan, q_len, start_pos, num_heads, causal != 0, s))) return rc;
   return cached_run(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_Q,
                     d_K_new, d_V_new, d_Out, layer_idx, q_len, start_pos, scale, s, -1);
+}
+
+namespace {
+
+LayerDims layer_dims(int layer_idx, int seq_len, int pos_offset, int hidden_size,
+                     int intermediate_size, int num_heads, int num_kv_heads, int head_dim,
+                     float rms_norm_eps, float rope_freq_base, int rope_neox, float scale) {
+  LayerDims d;
+  d.layer = layer_idx;
+  d.seq = seq_len;
+  d.pos = pos_offset;
+  d.hidden = hidden_size;
+  d.inter = intermediate_size;
+  d.H = num_heads;
+  d.Hkv = num_kv_heads;
+  d.D = head_dim;
+  d.eps = rms_norm_eps;
+  d.base = rope_freq_base;
+  d.scale = scale;
+  d.neox = rope_neox != 0;
+  return d;
+}
+
+}  // namespace
+
+extern "C" int kvc_forward_layer_cached(
+    const void* h_x_in, void* h_x_out, const void* h_attn_norm_w, const void* h_wq, int wq_type,
+    const void* h_wk, int wk_type, const void* h_wv, int wv_type, const void* h_wo, int wo_type,
+    const void* h_ffn_norm_w, const void* h_wgate, int wgate_type, const void* h_wup,
+    int wup_type, const void* h_wdown, int wdown_type, int layer_idx, int seq_len, int pos_offset,
+    int hidden_size, int intermediate_size, int num_heads, int num_kv_heads, int head_dim,
+    float rms_norm_eps, float rope_freq_base, int rope_neox, float scale) {
+  const LayerDims d = layer_dims(layer_idx, seq_len, pos_offset, hidden_size, intermediate_size,
+                                 num_heads, num_kv_heads, head_dim, rms_norm_eps, rope_freq_base,
+                                 rope_neox, scale);
+  const int types[7] = {wq_type, wk_type, wv_type, wo_type, wgate_type, wup_type, wdown_type};
+  const void* h_w[7] = {h_wq, h_wk, h_wv, h_wo, h_wgate, h_wup, h_wdown};
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  int rc = check_layer(d, types);
+  if (rc) return rc;
+  if ((rc = validate_cached(S, layer_idx, seq_len, pos_offset, num_heads, num_kv_heads, head_dim)))
+    return rc;
+  if (seq_len == 0) return KVC_OK;
+  if (!h_x_in || !h_x_out || !h_attn_norm_w || !h_ffn_norm_w)
+    return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
+  for (const void* w : h_w)
+    if (!w) return set_error(KVC_ERR_INVALID_ARG, "weight buffers must not be null.");
+  if (const int rc_dev = use_device(S.pool.device)) return rc_dev;
+  cudaStream_t s = S.stream;
+  // attention.hip:629-644: the activations, the norm weights and every weight are
+  // copied to the device on each call; everything in between stays there.
+  auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+  const size_t xb = sizeof(uint16_t) * static_cast<size_t>(seq_len) * hidden_size;
+  const size_t nb = sizeof(uint16_t) * static_cast<size_t>(hidden_size);
+  size_t wb[7];
+  const size_t wtot = layer_weight_bytes(d, types, wb);
+  cudaError_t e = S.layer_io.ensure(2 * al(xb) + 2 * al(nb) + wtot);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(layer inputs)");
+  uint8_t* p = static_cast<uint8_t*>(S.layer_io.ptr);
+  LayerIO io;
+  uint8_t* d_x = p;
+  uint8_t* d_out = p + al(xb);
+  uint8_t* d_an = d_out + al(xb);
+  uint8_t* d_fn = d_an + al(nb);
+  uint8_t* d_w = d_fn + al(nb);
+  if ((e = cudaMemcpyAsync(d_x, h_x_in, xb, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(d_an, h_attn_norm_w, nb, cudaMemcpyHostToDevice, s)) ||
+      (e = cudaMemcpyAsync(d_fn, h_ffn_norm_w, nb, cudaMemcpyHostToDevice, s)))
+    return cuda_error(e, "cudaMemcpyAsync(layer inputs)");
+  for (int i = 0; i < 7; ++i) {
+    if ((e = cudaMemcpyAsync(d_w, h_w[i], wb[i], cudaMemcpyHostToDevice, s)))
+      return cuda_error(e, "cudaMemcpyAsync(weights)");
+    io.w[i] = d_w;
+    io.type[i] = types[i];
+    d_w += al(wb[i]);
+  }
+  io.x_in = reinterpret_cast<const __half*>(d_x);
+  io.x_out = reinterpret_cast<__half*>(d_out);
+  io.attn_norm = reinterpret_cast<const __half*>(d_an);
+  io.ffn_norm = reinterpret_cast<const __half*>(d_fn);
+  rc = layer_forward(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len,
+                     S.layer_ws, io, d, s);
+  if (rc) return rc;
+  return finish_host_call(s, h_x_out, d_out, xb, "forward_layer_cached");
+}
+
+extern "C" int kvc_forward_layer_cached_device(
+    const void* d_x_in, void* d_x_out, const void* d_attn_norm_w, const void* d_wq, int wq_type,
+    const void* d_wk, int wk_type, const void* d_wv, int wv_type, const void* d_wo, int wo_type,
+    const void* d_ffn_norm_w, const void* d_wgate, int wgate_type, const void* d_wup,
+    int wup_type, const void* d_wdown, int wdown_type, int layer_idx, int seq_len, int pos_offset,
+    int hidden_size, int intermediate_size, int num_heads, int num_kv_heads, int head_dim,
+    float rms_norm_eps, float rope_freq_base, int rope_neox, float scale, void* stream) {
+  const LayerDims d = layer_dims(layer_idx, seq_len, pos_offset, hidden_size, intermediate_size,
+                                 num_heads, num_kv_heads, head_dim, rms_norm_eps, rope_freq_base,
+                                 rope_neox, scale);
+  LayerIO io;
+  const int types[7] = {wq_type, wk_type, wv_type, wo_type, wgate_type, wup_type, wdown_type};
+  const void* w[7] = {d_wq, d_wk, d_wv, d_wo, d_wgate, d_wup, d_wdown};
+  Singleton& S = singleton();
+  std::lock_guard<std::mutex> lock(S.mu);
+  int rc = check_layer(d, types);
+  if (rc) return rc;
+  if ((rc = validate_cached(S, layer_idx, seq_len, pos_offset, num_heads, num_kv_heads, head_dim)))
+    return rc;
+  if (seq_len == 0) return KVC_OK;
+  if (!d_x_in || !d_x_out || !d_attn_norm_w || !d_ffn_norm_w)
+    return set_error(KVC_ERR_INVALID_ARG, "device buffers must not be null.");
+  for (int i = 0; i < 7; ++i) {
+    if (!w[i]) return set_error(KVC_ERR_INVALID_ARG, "weight buffers must not be null.");
+    io.w[i] = w[i];
+    io.type[i] = types[i];
+  }
+  io.x_in = static_cast<const __half*>(d_x_in);
+  io.x_out = static_cast<__half*>(d_x_out);
+  io.attn_norm = static_cast<const __half*>(d_attn_norm_w);
+  io.ffn_norm = static_cast<const __half*>(d_ffn_norm_w);
+  if (const int rc_dev = use_device(S.pool.device)) return rc_dev;
+  return layer_forward(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len,
+                       S.layer_ws, io, d, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int kvc_cache_gather(int layer_idx, int start, int count, void* h_K_out,

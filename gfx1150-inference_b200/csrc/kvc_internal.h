@@ -2,6 +2,7 @@
 // and the CUDA kernels (kvc_kernels.cu).  Not part of the public C ABI.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -237,5 +238,49 @@ bool decode_uses_mma(int dtype, int head_dim, int page_size);
 // Device error word (per device): read and optionally clear; its device address.
 cudaError_t read_device_error(uint32_t* code, uint32_t* info, bool clear);
 cudaError_t device_error_address(void** p);
+
+// ---- layer pipeline (forward_layer_cached, attention.hip:603-695) ----------------
+// Weight storage types: the GGML type ids forward_layer_cached takes
+// (bindings.cpp:518-557).  Weights are (n, k) row-major, each row k / per blocks.
+constexpr int kWF16 = 1, kWQ4_0 = 2, kWQ8_0 = 8, kWQ4_K = 12, kWQ6_K = 14;
+// Weights per block and bytes per block of a type (0, 0 if unknown).
+void weight_block(int w_type, int* per, int* bytes);
+
+// y = x · Wᵀ for fp16 activations x (m, k) and quantized W (n, k); fp32 sums, fp16 y.
+// Up to three matrices of one type and k in one launch (segments, e.g. q, k, v).
+// Epilogues: kEpiStore (y), kEpiSwiglu (seg 0 = gate, seg 1 = up, same n:
+// y = silu(gate) · up with both rounded to fp16 first, mlp.hip:18-31), kEpiResidual
+// (y = res + fp16(x · Wᵀ), the second residual of attention.hip:689).
+constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2;
+struct LinearSeg {
+  const uint8_t* w = nullptr;
+  __half* out = nullptr;
+  int n = 0;        // rows of W = columns of y
+  int out_ld = 0;   // elements between rows of y
+};
+struct LinearArgs {
+  const __half* x = nullptr;
+  int x_ld = 0;
+  int m = 0, k = 0;
+  int w_type = 0;
+  size_t row_bytes = 0;
+  LinearSeg seg[3];
+  int n_seg = 0;
+  int epi = kEpiStore;
+  const __half* res = nullptr;   // kEpiResidual: (m, n) with ld seg[0].out_ld
+  // set by the launcher
+  int seg_cta0[4] = {0, 0, 0, 0};  // first CTA of each segment (prefix sums)
+};
+cudaError_t launch_linear(LinearArgs& a, cudaStream_t s);
+
+// out = silu(gate) · up elementwise (gate and up of different weight types).
+cudaError_t launch_swiglu(const __half* gate, const __half* up, __half* out, size_t n,
+                          cudaStream_t s);
+
+// RMSNorm of each row of x (m, k): x / sqrt(mean(x²) + eps) · w, fp16 out
+// (rmsnorm.hip:23-74).  With res: h = fp16(x + res) is written to h_out and
+// normalised instead (the fused residual + RMSNorm of rmsnorm.hip:79-140).
+cudaError_t launch_rmsnorm(const __half* x, const __half* res, const __half* w, __half* h_out,
+                           __half* out, int m, int k, float eps, cudaStream_t s);
 
 }  // namespace kvc

@@ -49,6 +49,13 @@ _c_size = ctypes.c_size_t
 _vp = ctypes.c_void_p
 _i32p = ctypes.POINTER(ctypes.c_int32)
 
+# forward_layer_cached's 30 arguments (bindings.cpp:562-587 order; rope_neox as int)
+_LAYER_ARGS = ([_vp, _vp, _vp] + [_vp, _c_int] * 4 + [_vp] + [_vp, _c_int] * 3
+               + [_c_int] * 8 + [_c_float, _c_float, _c_int, _c_float])
+
+# GGML weight type ids (KVC_WTYPE_*)
+WTYPE_F16, WTYPE_Q4_0, WTYPE_Q8_0, WTYPE_Q4_K, WTYPE_Q6_K = 1, 2, 8, 12, 14
+
 # name -> (restype, argtypes); mirrors include/kvcache.h one to one.
 SIGNATURES = {
     "kvc_version": (_c_int, []),
@@ -123,6 +130,13 @@ SIGNATURES = {
     "kvc_xchg_destroy": (_c_int, [_vp]),
     "kvc_append_decode_xchg": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int,
                                         _c_int, _vp, _c_int, _c_float, _vp]),
+    "kvc_weight_bytes": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "kvc_linear": (_c_int, [_vp, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp]),
+    "kvc_linear_swiglu": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _vp, _vp]),
+    "kvc_linear_residual": (_c_int, [_vp, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp]),
+    "kvc_rmsnorm": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp]),
+    "kvc_forward_layer_cached": (_c_int, _LAYER_ARGS),
+    "kvc_forward_layer_cached_device": (_c_int, _LAYER_ARGS + [_vp]),
 }
 
 XCHG_HANDLE_BYTES = 64

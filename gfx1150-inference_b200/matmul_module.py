@@ -12,6 +12,10 @@ sm_100a library libkvcache.so through ``kvcache_ffi``:
                                                                          bindings.cpp:480-514
   gqa_attention(Q, K, V, Out, q_len, kv_len, num_heads, num_kv_heads, head_dim,
                 start_pos=0, scale=0.0, causal=True)                     bindings.cpp:414-447
+  forward_layer_cached(x_in, x_out, attn_norm_w, wq, wq_type, ..., rope_neox, scale)
+                                                                         bindings.cpp:562-627
+  rope(x_in, x_out, seq_len, num_heads, head_dim, pos_offset=0,
+       freq_base=10000.0, neox_style=False)                              bindings.cpp:392-412
 
 Array checks follow check_fp16_contiguous (bindings.cpp:20-38): a 2-byte float
 dtype, C-contiguous, ``Out`` writeable, and at least the expected number of
@@ -19,8 +23,9 @@ elements, else ValueError.  Extension: a pool created with
 ``kv_cache_init_ex(..., dtype=numpy.float32)`` takes float32 arrays, and
 ``gqa_attention`` takes float32 arrays when all four are float32.
 
-Only the KV-cache path lives here; the reference module's matmul, dequant,
-norm, RoPE and SwiGLU kernels are not part of this library.
+The KV-cache path and the layer that drives it live here; the reference
+module's standalone host-buffer matmul, dequant, norm and SwiGLU entry points
+(used by the per-op layer path) are not part of this library.
 """
 
 from __future__ import annotations
@@ -155,3 +160,66 @@ def kv_cache_gather(layer_idx: int, start: int, count: int):
     _ffi.check(_ffi.lib.kvc_cache_gather(int(layer_idx), int(start), int(count), _ffi.np_ptr(k),
                                          _ffi.np_ptr(v)))
     return k, v
+
+
+# GGML weight types forward_layer_cached takes: id -> (weights per block, bytes per block, name)
+_WTYPES = {1: (1, 2, "F16"), 2: (32, 18, "Q4_0"), 8: (32, 34, "Q8_0"), 12: (256, 144, "Q4_K"),
+           14: (256, 210, "Q6_K")}
+
+
+def _check_weight_buffer(buf, w_type: int, n: int, k: int, name: str):
+    """check_weight_buffer (bindings.cpp:518-557): C-contiguous buffer, known type,
+    k divisible by the type's block, at least n · k / per · bytes bytes."""
+    arr = buf if isinstance(buf, np.ndarray) else np.frombuffer(memoryview(buf), dtype=np.uint8)
+    if arr.ndim > 0 and not arr.flags["C_CONTIGUOUS"]:
+        raise ValueError(f"{name} buffer must be C-contiguous.")
+    w_type = int(w_type)
+    if w_type not in _WTYPES:
+        raise ValueError(f"{name} has unsupported ggml_type.")
+    per, nbytes, tname = _WTYPES[w_type]
+    if w_type != 1 and (k <= 0 or k % per != 0):
+        raise ValueError(f"{name} K must be divisible by {per} for {tname}.")
+    expected = n * k * 2 if w_type == 1 else n * (k // per) * nbytes
+    if arr.nbytes < expected:
+        raise ValueError(f"{name} weight buffer is smaller than required.")
+    return arr
+
+
+def forward_layer_cached(x_in, x_out, attn_norm_w, wq, wq_type: int, wk, wk_type: int, wv,
+                         wv_type: int, wo, wo_type: int, ffn_norm_w, wgate, wgate_type: int, wup,
+                         wup_type: int, wdown, wdown_type: int, layer_idx: int, seq_len: int,
+                         pos_offset: int, hidden_size: int, intermediate_size: int,
+                         num_heads: int, num_kv_heads: int, head_dim: int, rms_norm_eps: float,
+                         rope_freq_base: float, rope_neox: bool, scale: float) -> None:
+    """Execute a full transformer layer on-device with the GPU-resident KV cache
+    (bindings.cpp:562-627 ⇒ attention.hip:603-695): RMSNorm, q/k/v projections,
+    RoPE, cached GQA attention (appending the rotated K rows and the V rows at
+    pos_offset), output projection, residual + RMSNorm, SwiGLU FFN, residual.
+    fp16 activations (seq_len, hidden_size); weights of GGML types F16 / Q4_0 /
+    Q8_0 / Q4_K / Q6_K, copied to the device on every call like the reference."""
+    hidden_elems = int(seq_len) * int(hidden_size)
+    f16 = np.dtype(np.float16)
+    x_in = _check_array(x_in, "x_in", hidden_elems, f16)
+    x_out = _check_array(x_out, "x_out", hidden_elems, f16, require_writeable=True)
+    attn_norm_w = _check_array(attn_norm_w, "attn_norm_w", int(hidden_size), f16)
+    ffn_norm_w = _check_array(ffn_norm_w, "ffn_norm_w", int(hidden_size), f16)
+    q_dim = int(num_heads) * int(head_dim)
+    kv_dim = int(num_kv_heads) * int(head_dim)
+    hs, inter = int(hidden_size), int(intermediate_size)
+    ws = [
+        _check_weight_buffer(wq, wq_type, q_dim, hs, "wq"),
+        _check_weight_buffer(wk, wk_type, kv_dim, hs, "wk"),
+        _check_weight_buffer(wv, wv_type, kv_dim, hs, "wv"),
+        _check_weight_buffer(wo, wo_type, hs, q_dim, "wo"),
+        _check_weight_buffer(wgate, wgate_type, inter, hs, "wgate"),
+        _check_weight_buffer(wup, wup_type, inter, hs, "wup"),
+        _check_weight_buffer(wdown, wdown_type, hs, inter, "wdown"),
+    ]
+    p = [_ffi.np_ptr(w) for w in ws]
+    _ffi.check(_ffi.lib.kvc_forward_layer_cached(
+        _ffi.np_ptr(x_in), _ffi.np_ptr(x_out), _ffi.np_ptr(attn_norm_w),
+        p[0], int(wq_type), p[1], int(wk_type), p[2], int(wv_type), p[3], int(wo_type),
+        _ffi.np_ptr(ffn_norm_w), p[4], int(wgate_type), p[5], int(wup_type), p[6], int(wdown_type),
+        int(layer_idx), int(seq_len), int(pos_offset), hs, inter, int(num_heads),
+        int(num_kv_heads), int(head_dim), float(rms_norm_eps), float(rope_freq_base),
+        int(bool(rope_neox)), float(scale)))

@@ -391,6 +391,71 @@ KVC_API int kvc_append_decode_xchg(kvc_pool_t* pool, const kvc_plan_t* plan, int
                                    const int32_t* d_block_tables, int bt_stride, float scale,
                                    void* stream);
 
+/* ==== 5. Layer pipeline over the process-wide pool ========================== */
+
+/* Weight storage types: the GGML type ids forward_layer_cached takes
+ * (bindings.cpp:518-557).  A weight is (n, k) row-major; each row is k / per
+ * blocks: F16 (per 1, 2 bytes), Q4_0 (32, 18), Q8_0 (32, 34), Q4_K (256, 144),
+ * Q6_K (256, 210), the block layouts of gguf_parser.py:374-590. */
+#define KVC_WTYPE_F16 1
+#define KVC_WTYPE_Q4_0 2
+#define KVC_WTYPE_Q8_0 8
+#define KVC_WTYPE_Q4_K 12
+#define KVC_WTYPE_Q6_K 14
+
+/* Bytes of an (n, k) weight of w_type (the size rule of check_weight_buffer,
+ * bindings.cpp:518-557); KVC_ERR_INVALID_ARG for an unknown type or a k the
+ * type's block does not divide. */
+KVC_API int kvc_weight_bytes(int w_type, int n, int k, size_t* out);
+
+/* d_out (m, n) = d_x (m, k) · Wᵀ on the device, fp16 activations, fp32 sums,
+ * fp16 out: the projections of project_on_device (attention.hip:572-599 ⇒
+ * launch_matmul_fp16_nt_device / launch_matmul_q4_0_device / ..._q8_0 / ..._q4_k
+ * / ..._q6_k).  k a multiple of 32 and n of 16; d_x and d_w 16-byte aligned. */
+KVC_API int kvc_linear(const void* d_x, int m, int k, const void* d_w, int w_type, int n,
+                       void* d_out, void* stream);
+/* d_out (m, n) = silu(x · Wgateᵀ) · (x · Wupᵀ), both products rounded to fp16
+ * first (attention.hip:684-686 with launch_swiglu_fp16_device, mlp.hip:18-31). */
+KVC_API int kvc_linear_swiglu(const void* d_x, int m, int k, const void* d_w_gate,
+                              const void* d_w_up, int w_type, int n, void* d_out, void* stream);
+/* d_out (m, n) = d_res + fp16(x · Wᵀ) (attention.hip:687-689: the down projection
+ * and launch_residual_add_fp16_device).  d_out may alias d_res. */
+KVC_API int kvc_linear_residual(const void* d_x, int m, int k, const void* d_w, int w_type, int n,
+                                const void* d_res, void* d_out, void* stream);
+/* RMSNorm of each row of d_x (m, k): x / sqrt(mean(x²) + eps) · w (rmsnorm.hip:23-74).
+ * With d_res: h = fp16(x + res) is written to d_h_out and normalised instead
+ * (rmsnorm.hip:79-140).  fp16 throughout. */
+KVC_API int kvc_rmsnorm(const void* d_x, const void* d_res, void* d_h_out, const void* d_w,
+                        void* d_out, int m, int k, float eps, void* stream);
+
+/* Replaces launch_forward_layer_cached_fp16 (attention.h:77-105,
+ * attention.hip:603-695) behind matmul_module.forward_layer_cached
+ * (bindings.cpp:562-627): one transformer layer for seq_len tokens at positions
+ * pos_offset.. on the process-wide fp16 pool, with the reference's argument order.
+ * Host buffers: x_in / x_out (seq_len, hidden_size), the two norm weights
+ * (hidden_size), and the seven weights of the given types (q, k, v: (H·D | Hkv·D,
+ * hidden); o: (hidden, H·D); gate, up: (intermediate, hidden); down: (hidden,
+ * intermediate)).  Like the reference, the activations and all weights are copied
+ * to the device on every call and the result back before it returns.  The pool
+ * receives the rotated K rows and the V rows at (layer_idx, pos_offset..). */
+KVC_API int kvc_forward_layer_cached(
+    const void* h_x_in, void* h_x_out, const void* h_attn_norm_w, const void* h_wq, int wq_type,
+    const void* h_wk, int wk_type, const void* h_wv, int wv_type, const void* h_wo, int wo_type,
+    const void* h_ffn_norm_w, const void* h_wgate, int wgate_type, const void* h_wup,
+    int wup_type, const void* h_wdown, int wdown_type, int layer_idx, int seq_len, int pos_offset,
+    int hidden_size, int intermediate_size, int num_heads, int num_kv_heads, int head_dim,
+    float rms_norm_eps, float rope_freq_base, int rope_neox, float scale);
+
+/* kvc_forward_layer_cached on device buffers (weights resident in HBM), work
+ * enqueued on `stream`, no host synchronisation.  x_out may alias x_in. */
+KVC_API int kvc_forward_layer_cached_device(
+    const void* d_x_in, void* d_x_out, const void* d_attn_norm_w, const void* d_wq, int wq_type,
+    const void* d_wk, int wk_type, const void* d_wv, int wv_type, const void* d_wo, int wo_type,
+    const void* d_ffn_norm_w, const void* d_wgate, int wgate_type, const void* d_wup,
+    int wup_type, const void* d_wdown, int wdown_type, int layer_idx, int seq_len, int pos_offset,
+    int hidden_size, int intermediate_size, int num_heads, int num_kv_heads, int head_dim,
+    float rms_norm_eps, float rope_freq_base, int rope_neox, float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

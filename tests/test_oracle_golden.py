@@ -151,3 +151,53 @@ def test_rope_restatement_matches_reference():
         again = gqa_ref.ref_rope(c["x"], freq_base=c["freq_base"], neox_style=c["neox"],
                                  positions=pos)
         np.testing.assert_array_equal(again, got)
+
+
+# ---- layer pipeline oracle (oracle/layer_ref.py) vs the reference's numpy code ----
+_LAYER_TYPES = {"q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14}
+
+
+@pytest.mark.parametrize("name", sorted(_LAYER_TYPES))
+@pytest.mark.parametrize("kind", ["deq", "deqr"])
+def test_dequantizers_bit_exact(name, kind):
+    """gguf_parser.py dequantize_*_cpu outputs on quantizer-made and on random blocks."""
+    import layer_ref
+    from make_layer_golden import OUT
+
+    g = np.load(OUT)
+    raw, out = g[f"{kind}_{name}_raw"], g[f"{kind}_{name}_out"]
+    mine = layer_ref.dequantize(raw, _LAYER_TYPES[name], 4, 512).reshape(-1)
+    assert np.array_equal(mine.view(np.uint16), out.view(np.uint16))
+
+
+def test_layer_oracle_matches_reference_composition():
+    """Prefill of 4 tokens then a decode step through layer_forward equals the
+    reference's CPU layer check composed from its own functions (bit-exact)."""
+    import math
+
+    import layer_ref as L
+    from make_layer_golden import LAYER as C, OUT
+
+    g = np.load(OUT)
+    t = C["types"]
+    lw = L.LayerWeights(g["layer_attn_norm"], *[(g[f"layer_w_{n}"], t[n]) for n in "qkvo"],
+                        g["layer_ffn_norm"],
+                        *[(g[f"layer_w_{n}"], t[n]) for n in ("gate", "up", "down")])
+    kc = np.zeros((16, C["Hkv"], C["D"]), np.float16)
+    vc = np.zeros_like(kc)
+    kw = dict(num_heads=C["H"], num_kv_heads=C["Hkv"], head_dim=C["D"], inter=C["inter"],
+              eps=C["eps"], rope_base=C["base"], neox=C["neox"], scale=1 / math.sqrt(C["D"]))
+    x = g["layer_x"]
+    out = np.concatenate([L.layer_forward(x[:4], lw, kc, vc, 0, **kw),
+                          L.layer_forward(x[4:5], lw, kc, vc, 4, **kw)])
+    assert np.array_equal(out, g["layer_out"])
+    assert np.array_equal(kc[:5], g["layer_k_rot"]) and np.array_equal(vc[:5], g["layer_v"])
+
+
+def test_weight_sizes_match_block_layouts():
+    import layer_ref as L
+
+    assert L.weight_bytes(L.Q4_0, 4096, 4096) == 4096 * 128 * 18
+    assert L.weight_bytes(L.Q6_K, 1024, 4096) == 1024 * 16 * 210
+    with pytest.raises(ValueError):
+        L.weight_bytes(L.Q4_K, 16, 96)
