@@ -270,7 +270,12 @@ struct LinearArgs {
   const __half* res = nullptr;   // kEpiResidual: (m, n) with ld seg[0].out_ld
   // set by the launcher
   int seg_cta0[4] = {0, 0, 0, 0};  // first CTA of each segment (prefix sums)
+  int stages = 0;                  // staged kernel: ring depth
+  uint32_t stage_row_bytes = 0;    // staged kernel: weight bytes of one row per stage
+  int stage_tok = 0;               // staged kernel: token rows of x per stage (min(8·MT, m))
+  uint32_t* err = nullptr;         // the device error word (bounded waits)
 };
+constexpr int kMaxLinStages = 16;
 cudaError_t launch_linear(LinearArgs& a, cudaStream_t s);
 
 // out = silu(gate) · up elementwise (gate and up of different weight types).

@@ -87,6 +87,21 @@ def test_linear_matches_oracle(w_type, m):
     assert _maxerr(got, ref) <= tol, (w_type, m, _maxerr(got, ref))
 
 
+@pytest.mark.parametrize("w_type", TYPES)
+@pytest.mark.parametrize("m", [1, 13, 40])
+def test_linear_staged_multi_stage(w_type, m):
+    """k = 4096: whole stages for every type (the bulk-copy ring path), several of
+    them per CTA, partial token tiles."""
+    rng = np.random.default_rng(300 + w_type * 3 + m)
+    n, k = 48, 4096
+    x = (rng.standard_normal((m, k), dtype=np.float32) * 0.5).astype(np.float16)
+    raw = L.random_weight(rng, w_type, n, k)
+    got = _linear_dev(x, raw, w_type, n)
+    ref = L.linear(x, raw, w_type, n)
+    tol = 2e-3 * max(1.0, float(np.abs(ref.astype(np.float32)).max()))
+    assert _maxerr(got, ref) <= tol, (w_type, m, _maxerr(got, ref))
+
+
 @pytest.mark.parametrize("w_type", [L.Q4_0, L.Q4_K, L.Q6_K])
 def test_linear_large_grid(w_type):
     """Llama-3-8B row counts (the grid's row-tiles-per-CTA choices) at m = 1 and 3."""
