@@ -678,6 +678,159 @@ TRAFFIC_PER_LAUNCH = {
 # ---------------------------------------------------------------------------------
 # reference arm: the reference algorithm on the host cores
 # ---------------------------------------------------------------------------------
+# Weight types of a layer: (q, k, v, o, gate, up, down) GGML ids; q4_k_m is the
+# usual Q4_K_M mix (Q6_K for v and down).
+LAYER_TYPES = {"q4_0": (2,) * 7, "q8_0": (8,) * 7, "f16": (1,) * 7,
+               "q4_k_m": (12, 12, 14, 12, 12, 12, 14)}
+
+
+def run_layer(args, rank, world, local_rank):
+    """Whole-layer decode (forward_layer_cached, the layer the KV path serves):
+    Llama-3-8B geometry (hidden 4096, intermediate 14336, 32 q-heads, 8 KV heads,
+    head_dim 128, 32 layers, each with its own weights of the chosen types), one
+    sequence with 4,095 cached positions (prefilled untimed in 512-token chunks),
+    then K timed decode steps of all 32 layers on device buffers.  value =
+    tokens/s; the roofline counts weight bytes + KV bytes read + appended rows per
+    layer against the measured HBM copy bandwidth; e2e = one layer through the
+    reference's host-buffer call (activations and all weights copied per call)."""
+    import torch
+
+    import kvcache_ffi as ffi
+    import matmul_module
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import layer_ref  # seeded random GGML blocks (input generator only)
+
+    torch.cuda.set_device(local_rank)
+    L, hid, inter, H, Hkv, D = (args.layers or 32), 4096, 14336, 32, 8, 128
+    types = LAYER_TYPES[args.layer_step]
+    shapes = [(H * D, hid), (Hkv * D, hid), (Hkv * D, hid), (hid, H * D), (inter, hid),
+              (inter, hid), (hid, inter)]
+    rng = np.random.default_rng(11)
+    host_w = [layer_ref.random_weight(rng, t, n, k) for t, (n, k) in zip(types, shapes)]
+    dev_w = [[torch.from_numpy(w).cuda() for w in host_w]]
+    for _ in range(L - 1):   # distinct weights per layer (no L2 reuse across layers)
+        dev_w.append([w.clone() for w in dev_w[0]])
+    an = (1.0 + 0.05 * torch.randn(hid, device="cuda")).half()
+    fn = (1.0 + 0.05 * torch.randn(hid, device="cuda")).half()
+    ctx0 = 4095
+    S = ctx0 + args.warmup + args.steps + 8
+    matmul_module.kv_cache_init(L, S, Hkv, D)
+    st = torch.cuda.current_stream().cuda_stream
+    scale = 1.0 / math.sqrt(D)
+
+    def layer(l, x, out, seq, pos):
+        w = dev_w[l]
+        ffi.check(ffi.lib.kvc_forward_layer_cached_device(
+            x.data_ptr(), out.data_ptr(), an.data_ptr(), w[0].data_ptr(), types[0],
+            w[1].data_ptr(), types[1], w[2].data_ptr(), types[2], w[3].data_ptr(), types[3],
+            fn.data_ptr(), w[4].data_ptr(), types[4], w[5].data_ptr(), types[5], w[6].data_ptr(),
+            types[6], l, seq, pos, hid, inter, H, Hkv, D, 1e-5, ROPE_BASE, 0, scale, st))
+
+    xp = (torch.randn((512, hid), device="cuda") * 0.5).half()
+    op = torch.empty_like(xp)
+    for l in range(L):
+        pos = 0
+        while pos < ctx0:
+            n = min(512, ctx0 - pos)
+            layer(l, xp[:n], op[:n], n, pos)
+            pos += n
+    torch.cuda.synchronize()
+    x = (torch.randn((1, hid), device="cuda") * 0.5).half()
+    y = torch.empty_like(x)
+    pos = ctx0
+
+    def step(p):
+        a, b = x, y
+        for l in range(L):
+            layer(l, a, b, 1, p)
+            a, b = b, a
+
+    for _ in range(args.warmup):
+        step(pos)
+        pos += 1
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    if sampler:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pos_t0 = pos
+    e0.record()
+    for _ in range(args.steps):
+        step(pos)
+        pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    code, info = ffi.device_error(local_rank)
+    if code:
+        raise RuntimeError(f"device error {code} ({info}) in the timed layer steps")
+    ms = e0.elapsed_time(e1) / args.steps
+    wbytes = sum(w.numel() for w in dev_w[0])
+    kv_read = sum((p + 1) * Hkv * D * 2 * 2 for p in range(pos_t0, pos)) / args.steps
+    act = (hid * 2 * 2 + (H + 2 * Hkv) * D * 2 * 2 + inter * 2 * 2) * 2   # activations, loosely
+    layer_bytes = wbytes + kv_read + 2 * Hkv * D * 2 + act
+    peak, peak_kind = load_peaks()
+    us_layer = ms * 1e3 / L
+    achieved = layer_bytes / (us_layer * 1e-6) / 1e9
+
+    # e2e: the reference's host-buffer call on layer 0 (weights copied every call)
+    e2e = None
+    if not args.no_e2e:
+        xh = x.cpu().numpy()
+        yh = np.empty_like(xh)
+        an_h, fn_h = an.cpu().numpy(), fn.cpu().numpy()
+
+        def host_layer(p):
+            matmul_module.forward_layer_cached(
+                xh, yh, an_h, host_w[0], types[0], host_w[1], types[1], host_w[2], types[2],
+                host_w[3], types[3], fn_h, host_w[4], types[4], host_w[5], types[5], host_w[6],
+                types[6], 0, 1, p, hid, inter, H, Hkv, D, 1e-5, ROPE_BASE, False, scale)
+
+        host_layer(pos)   # untimed
+        t0 = time.perf_counter()
+        n_e2e = max(1, args.e2e_steps)
+        for i in range(n_e2e):
+            host_layer(pos + 1 + i)
+        dt = (time.perf_counter() - t0) / n_e2e
+        e2e = {"value": round(1.0 / (dt * L), 2), "unit": "tokens/s", "us_per_layer": round(dt * 1e6, 1),
+               "h2d_bytes_per_step": int((wbytes + 2 * hid * 2 + hid * 2) * L),
+               "d2h_bytes_per_step": int(hid * 2 * L),
+               "call": "matmul_module.forward_layer_cached per layer (host x, norms and all weights copied per call, like the reference)"}
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        # the oracle layer (numpy, fp32) on one layer at 512 cached positions: bounded sample
+        lw = layer_ref.LayerWeights(an.cpu().numpy(), *[(host_w[i], types[i]) for i in range(4)],
+                                    fn.cpu().numpy(), *[(host_w[i], types[i]) for i in range(4, 7)])
+        kc = np.zeros((ctx0 + 2, Hkv, D), np.float16)
+        vc = np.zeros_like(kc)
+        t0 = time.perf_counter()
+        layer_ref.layer_forward(x.cpu().numpy(), lw, kc, vc, ctx0, H, Hkv, D, inter, 1e-5, ROPE_BASE,
+                                False, scale)
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(1.0 / (dt * L), 4), "unit": "tokens/s", "cores": os.cpu_count(),
+               "kind": "port", "sample": f"one layer, numpy oracle (dequantize + fp32 matmuls), {dt:.2f} s"}
+    return {
+        "metric": "forward_layer_cached decode tokens/s (Llama-3-8B geometry, batch 1, 4K context)",
+        "value": round(1e3 / ms, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "us_per_layer": round(us_layer, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 activations, GGML weights, f32 accumulate",
+        "data": "synthetic: seeded random GGML blocks, N(0,1) activations",
+        "config": {"workload": f"llama3-8b-layer-decode-{args.layer_step}", "layers": L,
+                   "hidden": hid, "intermediate": inter, "q_heads": H, "kv_heads": Hkv,
+                   "head_dim": D, "weight_types": list(types), "cached_len": ctx0,
+                   "weight_bytes_per_layer": int(wbytes),
+                   "l2": "weights per layer differ; 32 layers of weights >> L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_kind": peak_kind, "bytes_per_layer": int(layer_bytes)},
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+        "gpu_launches": L * args.steps * 10,
+    }
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -749,6 +902,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--layer-step", choices=sorted(LAYER_TYPES), default=None,
+                    help="time the whole layer (forward_layer_cached) instead of the KV path")
     ap.add_argument("--launch-events", action="store_true",
                     help="diagnostics: record events around every launch (serialises launches)")
     args = ap.parse_args()
@@ -772,7 +927,9 @@ def main():
                 "nccl", timeout=datetime.timedelta(seconds=120),
                 device_id=torch.device("cuda", local_rank))
         try:
-            if args.config == "5":
+            if args.layer_step:
+                res = run_layer(args, rank, world, local_rank) if rank == 0 else None
+            elif args.config == "5":
                 res = run_offload(args, rank, world, local_rank)
             else:
                 res = run_b200(args, rank, world, local_rank)

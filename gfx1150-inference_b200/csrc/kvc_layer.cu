@@ -522,6 +522,8 @@ __global__ void __launch_bounds__(256) linear_tma_kernel(const LinearArgs a) {
   constexpr int UK = WTraits<WT>::kUnitK;
   constexpr int SK = stage_k(WT);             // weights (k) per stage
   constexpr int US = SK / UK;                 // units per stage
+  constexpr int kLinBatch = (RT == 1 && (WT == kWQ4_0 || WT == kWQ8_0)) ? 4 : 2;
+  static_assert((US / kLinWarps) % kLinBatch == 0, "units per warp and stage");
   constexpr uint32_t XRS = SK * 2 + 16;       // shared-memory stride of a token row
   __shared__ float red[kLinWarps][TOK][R + 1];
   __shared__ __align__(8) uint64_t full[kMaxLinStages];
@@ -592,30 +594,39 @@ __global__ void __launch_bounds__(256) linear_tma_kernel(const LinearArgs a) {
       dead = true;
       break;
     }
+    // Shared-memory rows of the stage.  Tiles past n and token rows past m hold no
+    // copy: they are read anyway (within the stage) and their results never stored,
+    // so every pointer stays a plain shared-memory pointer.
     const uint8_t* buf = ring + slot * stage_bytes;
     const uint8_t* wr[RT][2];
 #pragma unroll
     for (int t = 0; t < RT; ++t) {
-      wr[t][0] = tile_w[t] != nullptr ? buf + static_cast<size_t>(t * 16 + gid) * WRS : nullptr;
-      wr[t][1] = tile_w[t] != nullptr ? buf + static_cast<size_t>(t * 16 + gid + 8) * WRS : nullptr;
+      wr[t][0] = buf + static_cast<size_t>(t * 16 + gid) * WRS;
+      wr[t][1] = buf + static_cast<size_t>(t * 16 + gid + 8) * WRS;
     }
     BFrag<MT> load_b;
     load_b.tig = tig;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      const int tk = mt * 8 + gid;
-      load_b.row[mt] = tk < valid_tok
-                           ? reinterpret_cast<const __half*>(buf + static_cast<size_t>(R) * WRS +
-                                                             static_cast<size_t>(tk) * XRS)
-                           : nullptr;
+      const int tk = min(mt * 8 + gid, valid_tok - 1);
+      load_b.row[mt] = reinterpret_cast<const __half*>(buf + static_cast<size_t>(R) * WRS +
+                                                       static_cast<size_t>(tk) * XRS);
     }
-#pragma unroll 1
-    for (int ul = warp; ul < US; ul += kLinWarps) {
-      Raw<RT> cur;
-      uint32_t bf[kChunks<WT>][MT][2];
-      load_unit<WT, RT>(cur, wr, ul, tig);
-      load_b.template unit<WT>(unit_k0<WT>(ul), bf);
-      compute_unit<WT, RT, MT>(cur, ul, bf, acc);
+    // this warp's units of the stage, loads first (all of them are independent)
+    constexpr int UPW = US / kLinWarps;
+#pragma unroll
+    for (int i0 = 0; i0 < UPW; i0 += kLinBatch) {
+      Raw<RT> cur[kLinBatch];
+      uint32_t bf[kLinBatch][kChunks<WT>][MT][2];
+#pragma unroll
+      for (int i = 0; i < kLinBatch; ++i) {
+        const int ul = warp + kLinWarps * (i0 + i);
+        load_unit<WT, RT>(cur[i], wr, ul, tig);
+        load_b.template unit<WT>(unit_k0<WT>(ul), bf[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < kLinBatch; ++i)
+        compute_unit<WT, RT, MT>(cur[i], warp + kLinWarps * (i0 + i), bf[i], acc);
     }
     done = st + 1;
     __syncthreads();   // every warp is done with the stage
@@ -631,7 +642,10 @@ __global__ void __launch_bounds__(256) linear_tma_kernel(const LinearArgs a) {
   reduce_store<RT, MT>(a, p, red, acc, warp, gid, tig);
 }
 
-// One CTA per row: fp32 sum of squares, then x / sqrt(mean + eps) · w.
+// One CTA per row: fp32 sum of squares, then x / sqrt(mean + eps) · w.  Rows of up
+// to 256 · 8 · kNormVec elements are held in registers (16-byte loads, one read
+// of x, res and w each); longer rows take the element loop.
+constexpr int kNormVec = 8;
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__ x,
                                                       const __half* __restrict__ res,
                                                       const __half* __restrict__ w,
@@ -640,6 +654,68 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__
                                                       float eps) {
   __shared__ float part[8];
   const size_t row = static_cast<size_t>(blockIdx.x) * k;
+  const bool vec = k % 8 == 0 && k <= 256 * 8 * kNormVec &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                     reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(res) |
+                     reinterpret_cast<uintptr_t>(h_out)) & 15u) == 0;
+  auto block_sum = [&](float ss) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += part[i];
+    return tot;
+  };
+  if (vec) {
+    const int n8 = k / 8;
+    uint4 v[kNormVec];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+      const int c = threadIdx.x + 256 * j;
+      if (c < n8) {
+        v[j] = reinterpret_cast<const uint4*>(x + row)[c];
+        if (res != nullptr) {
+          const uint4 r = reinterpret_cast<const uint4*>(res + row)[c];
+          __half2* hv = reinterpret_cast<__half2*>(&v[j]);
+          const __half2* hr = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 a = __half22float2(hv[e]), b = __half22float2(hr[e]);
+            hv[e] = __floats2half2_rn(a.x + b.x, a.y + b.y);
+          }
+          reinterpret_cast<uint4*>(h_out + row)[c] = v[j];
+        }
+        const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a = __half22float2(hv[e]);
+          ss += a.x * a.x + a.y * a.y;
+        }
+      }
+    }
+    const float rms = sqrtf(block_sum(ss) / static_cast<float>(k) + eps);
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+      const int c = threadIdx.x + 256 * j;
+      if (c < n8) {
+        const uint4 wv = reinterpret_cast<const uint4*>(w)[c];
+        const __half2* hv = reinterpret_cast<const __half2*>(&v[j]);
+        const __half2* hw = reinterpret_cast<const __half2*>(&wv);
+        uint4 o;
+        __half2* ho = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a = __half22float2(hv[e]), b = __half22float2(hw[e]);
+          ho[e] = __floats2half2_rn(a.x / rms * b.x, a.y / rms * b.y);
+        }
+        reinterpret_cast<uint4*>(out + row)[c] = o;
+      }
+    }
+    return;
+  }
   const __half* xr = x + row;
   float ss = 0.f;
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
@@ -651,14 +727,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __half* __restrict__
     }
     ss += v * v;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += part[i];
-  const float rms = sqrtf(tot / static_cast<float>(k) + eps);
+  const float rms = sqrtf(block_sum(ss) / static_cast<float>(k) + eps);
   const __half* src = res != nullptr ? h_out + row : xr;
   for (int i = threadIdx.x; i < k; i += blockDim.x)
     out[row + i] = __float2half_rn(__half2float(src[i]) / rms * __half2float(w[i]));
