@@ -831,6 +831,134 @@ def run_layer(args, rank, world, local_rank):
     }
 
 
+def run_layer_batch(args, rank, world, local_rank):
+    """Whole-model batched decode (paged.BatchDecoder over kvc_forward_layer_paged):
+    benchmark config 3's batch (32 sequences, cached lengths U[1024, 8192] from seed
+    2024, paged fp16 pool of 16-position pages in a random permutation, N(0,1) KV)
+    through 32 Llama-3-8B layers, each with its own weights of the chosen types.  A
+    step is one new token for every sequence through every layer, in a real decode
+    loop: contexts grow by one per step and the plan is rebuilt on the host every
+    step, inside the timed region.  value = tokens/s (batch / step time); the
+    roofline counts weights + KV read + appended rows per step against the
+    measured HBM copy bandwidth.  e2e = the same step with the new tokens'
+    activations copied from page-locked host memory and the last layer's output
+    copied back every step."""
+    import torch
+
+    import kvcache_ffi as ffi
+    import paged
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import layer_ref  # seeded random GGML blocks (input generator) and the CPU baseline
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS["3"]
+    L, hid, inter = (args.layers or cfg["layers"]), 4096, 14336
+    H, Hkv, D, B = cfg["H"], cfg["Hkv"], cfg["D"], cfg["batch"]
+    types = LAYER_TYPES[args.layer_step]
+    shapes = [(H * D, hid), (Hkv * D, hid), (Hkv * D, hid), (hid, H * D), (inter, hid),
+              (inter, hid), (hid, inter)]
+    rng = np.random.default_rng(11)
+    host_w = [layer_ref.random_weight(rng, t, n, k) for t, (n, k) in zip(types, shapes)]
+    dev_w = [[torch.from_numpy(w).to(dev) for w in host_w]]
+    for _ in range(L - 1):   # distinct weights per layer (no L2 reuse across layers)
+        dev_w.append([w.clone() for w in dev_w[0]])
+    an = (1.0 + 0.05 * torch.randn(hid, device=dev)).half()
+    fn = (1.0 + 0.05 * torch.randn(hid, device=dev)).half()
+    layers = [paged.DeviceLayerWeights(an, fn, w, types, hid, inter) for w in dev_w]
+    cached = cached_lengths(cfg)
+    extra = args.warmup + args.steps + max(1, args.e2e_steps) + 2
+    table, total_pages = paged.random_block_tables(cached + extra, PAGE, cfg["seed"] + 17 * rank)
+    pool = paged.PagedKVCache(L, total_pages, PAGE, Hkv, D, dtype=torch.float16, device=local_rank)
+    pool.fill_normal(seed=1000 + rank, stddev=1.0)
+    bt = torch.from_numpy(table).to(dev)
+    dec = paged.BatchDecoder(pool, layers, bt, H, cached, 1e-5, ROPE_BASE)
+    x = (torch.randn((B, hid), device=dev) * 0.5).half()
+    for _ in range(args.warmup):
+        dec.step(x)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    if sampler:
+        sampler.start()
+    ctx_t0 = dec.ctx.copy()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dec.step(x)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    code, info = ffi.device_error(local_rank)
+    if code:
+        raise RuntimeError(f"device error {code} ({info}) in the timed batched steps")
+    ms = e0.elapsed_time(e1) / args.steps
+    wbytes = sum(w.numel() for w in dev_w[0])
+    # positions attended per step: step j reads ctx_t0 + j + 1 positions per sequence
+    kv_read = sum(int((ctx_t0 + j + 1).sum()) for j in range(args.steps)) / args.steps
+    kv_read *= Hkv * D * 2 * 2 * L
+    appended = B * Hkv * D * 2 * 2 * L
+    step_b = wbytes * L + kv_read + appended
+    peak, peak_kind = load_peaks()
+    achieved = step_b / (ms * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+        n_e2e = max(1, args.e2e_steps)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            yh.copy_(dec.step(xh.to(dev, non_blocking=True)))
+        torch.cuda.synchronize()
+        dt = (time.perf_counter() - t0) / n_e2e
+        e2e = {"value": round(B / dt, 2), "unit": "tokens/s", "ms_per_step": round(dt * 1e3, 3),
+               "h2d_bytes_per_step": int(B * hid * 2), "d2h_bytes_per_step": int(B * hid * 2),
+               "call": "paged.BatchDecoder.step per step: host activations in, host output out "
+                       "(page-locked), plan rebuilt per step"}
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        # the numpy oracle layer for ONE token of one sequence at the batch's mean
+        # context; the reference decodes the batch one sequence at a time, so a step
+        # costs B x layers such calls
+        ctx_m = int(cached.mean())
+        lw = layer_ref.LayerWeights(an.cpu().numpy(), *[(host_w[i], types[i]) for i in range(4)],
+                                    fn.cpu().numpy(), *[(host_w[i], types[i]) for i in range(4, 7)])
+        kc = np.zeros((ctx_m + 1, Hkv, D), np.float16)
+        vc = np.zeros_like(kc)
+        t0 = time.perf_counter()
+        layer_ref.layer_forward(x[:1].cpu().numpy(), lw, kc, vc, ctx_m, H, Hkv, D, inter, 1e-5,
+                                ROPE_BASE, False, 1.0 / math.sqrt(D))
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(1.0 / (dt * L), 4), "unit": "tokens/s", "cores": os.cpu_count(),
+               "kind": "port",
+               "sample": f"one layer of one sequence at {ctx_m} cached positions, numpy oracle "
+                         f"(dequantize + fp32 matmuls), {dt:.2f} s; x {L} layers per token"}
+    dec.close()
+    return {
+        "metric": "batched decode tokens/s through the whole layer (Llama-3-8B geometry, "
+                  "config-3 batch: 32 ragged sequences)",
+        "value": round(B * 1e3 / ms, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "us_per_layer": round(ms * 1e3 / L, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 activations and KV, GGML weights, f32 accumulate",
+        "data": "synthetic: seeded random GGML blocks, N(0,1) KV pool and activations",
+        "config": {"workload": f"llama3-8b-batched-layer-decode-{args.layer_step}", "layers": L,
+                   "hidden": hid, "intermediate": inter, "q_heads": H, "kv_heads": Hkv,
+                   "head_dim": D, "sequences": B, "weight_types": list(types),
+                   "cached_tokens_at_start": int(ctx_t0.sum()), "page_size": PAGE,
+                   "weight_bytes_per_layer": int(wbytes),
+                   "l2": "weights per layer differ; KV and weights per step >> L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_kind": peak_kind, "bytes_per_step": int(step_b)},
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+        "gpu_launches": L * args.steps * 11,
+    }
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -904,6 +1032,9 @@ def main():
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--layer-step", choices=sorted(LAYER_TYPES), default=None,
                     help="time the whole layer (forward_layer_cached) instead of the KV path")
+    ap.add_argument("--layer-batch", action="store_true",
+                    help="with --layer-step: config 3's 32-sequence batch through the whole "
+                         "layer (paged.BatchDecoder) instead of one sequence")
     ap.add_argument("--launch-events", action="store_true",
                     help="diagnostics: record events around every launch (serialises launches)")
     args = ap.parse_args()
@@ -927,7 +1058,9 @@ def main():
                 "nccl", timeout=datetime.timedelta(seconds=120),
                 device_id=torch.device("cuda", local_rank))
         try:
-            if args.layer_step:
+            if args.layer_step and args.layer_batch:
+                res = run_layer_batch(args, rank, world, local_rank) if rank == 0 else None
+            elif args.layer_step:
                 res = run_layer(args, rank, world, local_rank) if rank == 0 else None
             elif args.config == "5":
                 res = run_offload(args, rank, world, local_rank)

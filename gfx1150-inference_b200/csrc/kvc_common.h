@@ -79,6 +79,7 @@ struct kvc_plan {
   const int32_t* dev_merge = nullptr;
   unsigned int* dev_queue = nullptr;
   kvc::DevBuf d_rope;          // rotated q and new K rows (kvc_append_decode_rope)
+  kvc::DevBuf d_layer;         // activations of kvc_forward_layer_paged
   kvc::HostBuf h_stage;
   cudaEvent_t upload_done = nullptr;
 
@@ -88,6 +89,7 @@ struct kvc_plan {
     d_part_ml.release();
     d_counters.release();
     d_rope.release();
+    d_layer.release();
     h_stage.release();
     if (upload_done) cudaEventDestroy(upload_done);
     upload_done = nullptr;
@@ -189,6 +191,11 @@ int run_linear(const void* x, int m, int k, int w_type, const void* const* w, co
                void* const* out, int n_seg, int epi, const void* res, cudaStream_t s);
 int layer_forward(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_len, DevBuf& ws,
                   const LayerIO& io, const LayerDims& d, cudaStream_t s);
+// The same layer for a decode batch on a paged pool: token i is query i of the
+// plan (one new row per sequence, at the plan's position ctx_i - 1); d.seq, d.H,
+// d.Hkv and d.D come from the plan and the pool.  Activations live in the plan.
+int layer_forward_paged(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_stride,
+                        const LayerIO& io, const LayerDims& d, cudaStream_t s);
 
 int pool_alloc(kvc_pool* p, const PoolGeom& g, int device);
 void pool_release(kvc_pool* p);

@@ -113,10 +113,16 @@ size_t layer_weight_bytes(const LayerDims& d, const int* types, size_t* each) {
   return tot;
 }
 
-int layer_forward(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_len, DevBuf& ws,
-                  const LayerIO& io, const LayerDims& d, cudaStream_t s) {
-  if (pool->g.dtype != KVC_DTYPE_F16)
-    return set_error(KVC_ERR_INVALID_ARG, "forward_layer_cached needs an fp16 KV pool.");
+namespace {
+
+// The layer around its attention step: RMSNorm, the q/k/v projections, then
+// attend(q, k, v, qr, kr, attn) — which rotates q and the new K rows into qr / kr,
+// appends them with the V rows and attends into attn — then the output
+// projection, residual + RMSNorm, gate/up with the SwiGLU and the down
+// projection with the second residual.  d.seq rows of io.x_in, one per token.
+template <class Attend>
+int layer_steps(DevBuf& ws, const LayerIO& io, const LayerDims& d, cudaStream_t s,
+                Attend&& attend) {
   const int seq = d.seq, qd = d.H * d.D, kd = d.Hkv * d.D;
   if (seq == 0) return KVC_OK;
   const size_t hb = sizeof(__half) * seq * d.hidden, qb = sizeof(__half) * seq * qd;
@@ -152,29 +158,8 @@ int layer_forward(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_le
       i = j;
     }
   }
-  // 3. the attention plan first: its upload must not sit between RoPE and the decode
-  if ((rc = cached_plan(pool, plan, seq, d.pos, d.H, true, s))) return rc;
-  // 4. RoPE on q and the new K rows (attention.hip:655-660)
-  RopeArgs ra{};
-  ra.src[0] = reinterpret_cast<const uint8_t*>(q);
-  ra.dst[0] = reinterpret_cast<uint8_t*>(qr);
-  ra.heads[0] = d.H;
-  ra.src[1] = reinterpret_cast<const uint8_t*>(k);
-  ra.dst[1] = reinterpret_cast<uint8_t*>(kr);
-  ra.heads[1] = d.Hkv;
-  ra.n_tokens = seq;
-  ra.head_dim = d.D;
-  ra.dtype = KVC_DTYPE_F16;
-  ra.neox = d.neox ? 1 : 0;
-  ra.pos0 = d.pos;
-  ra.positions = nullptr;
-  rope_inv_freq(d.base, d.D, ra.inv_freq);
-  const bool one = seq == 1;
-  if ((e = launch_rope(ra, s, one))) return cuda_error(e, "rope kernel");
-  // 5. append the rotated K rows and V rows, attend (attention.hip:663-668)
-  if ((rc = cached_run(pool, plan, d_bt, bt_len, qr, kr, v, attn, d.layer, seq, d.pos, d.scale, s,
-                       one ? 1 : -1)))
-    return rc;
+  // 3-5. RoPE, append, attention (attention.hip:655-668)
+  if ((rc = attend(q, k, v, qr, kr, attn))) return rc;
   // 6. output projection (attention.hip:671)
   {
     const void* w[1] = {io.w[3]};
@@ -211,6 +196,64 @@ int layer_forward(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_le
     if ((rc = run_linear(act, seq, d.inter, io.type[6], w, n, out, 1, kEpiResidual, h, s))) return rc;
   }
   return KVC_OK;
+}
+
+// RoPE arguments for q (d.H heads) and the new K rows (d.Hkv heads) of d.seq tokens.
+RopeArgs rope_args(const LayerDims& d, const __half* q, const __half* k, __half* qr, __half* kr) {
+  RopeArgs ra{};
+  ra.src[0] = reinterpret_cast<const uint8_t*>(q);
+  ra.dst[0] = reinterpret_cast<uint8_t*>(qr);
+  ra.heads[0] = d.H;
+  ra.src[1] = reinterpret_cast<const uint8_t*>(k);
+  ra.dst[1] = reinterpret_cast<uint8_t*>(kr);
+  ra.heads[1] = d.Hkv;
+  ra.n_tokens = d.seq;
+  ra.head_dim = d.D;
+  ra.dtype = KVC_DTYPE_F16;
+  ra.neox = d.neox ? 1 : 0;
+  rope_inv_freq(d.base, d.D, ra.inv_freq);
+  return ra;
+}
+
+}  // namespace
+
+int layer_forward(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_len, DevBuf& ws,
+                  const LayerIO& io, const LayerDims& d, cudaStream_t s) {
+  if (pool->g.dtype != KVC_DTYPE_F16)
+    return set_error(KVC_ERR_INVALID_ARG, "forward_layer_cached needs an fp16 KV pool.");
+  return layer_steps(ws, io, d, s, [&](const __half* q, const __half* k, const __half* v,
+                                       __half* qr, __half* kr, __half* attn) -> int {
+    // the attention plan first: its upload must not sit between RoPE and the decode
+    int rc = cached_plan(pool, plan, d.seq, d.pos, d.H, true, s);
+    if (rc) return rc;
+    // RoPE on q and the new K rows at pos_offset.. (attention.hip:655-660)
+    RopeArgs ra = rope_args(d, q, k, qr, kr);
+    ra.pos0 = d.pos;
+    ra.positions = nullptr;
+    const bool one = d.seq == 1;
+    cudaError_t e = launch_rope(ra, s, one);
+    if (e) return cuda_error(e, "rope kernel");
+    // append the rotated K rows and V rows, attend (attention.hip:663-668)
+    return cached_run(pool, plan, d_bt, bt_len, qr, kr, v, attn, d.layer, d.seq, d.pos, d.scale,
+                      s, one ? 1 : -1);
+  });
+}
+
+int layer_forward_paged(kvc_pool* pool, kvc_plan* plan, const int32_t* d_bt, int bt_stride,
+                        const LayerIO& io, const LayerDims& d, cudaStream_t s) {
+  return layer_steps(plan->d_layer, io, d, s, [&](const __half* q, const __half* k,
+                                                  const __half* v, __half* qr, __half* kr,
+                                                  __half* attn) -> int {
+    // RoPE at each query's own position (the plan's ctx - 1), as a programmatic
+    // dependent that lets the decode behind it start streaming KV; it writes only
+    // qr / kr.  Then the fused append + attention of every sequence.
+    RopeArgs ra = rope_args(d, q, k, qr, kr);
+    ra.positions = plan->dev_pos;
+    cudaError_t e = launch_rope(ra, s, true);
+    if (e) return cuda_error(e, "rope kernel");
+    return append_then_decode(pool, plan, d.layer, qr, kr, v, attn, d_bt, bt_stride, d.scale, s,
+                              nullptr, 1);
+  });
 }
 
 }  // namespace kvc
@@ -266,4 +309,61 @@ extern "C" int kvc_rmsnorm(const void* d_x, const void* d_res, void* d_h_out, co
                                  static_cast<__half*>(d_out), m, k, eps,
                                  static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KVC_OK : cuda_error(e, "rmsnorm kernel");
+}
+
+extern "C" int kvc_forward_layer_paged(
+    kvc_pool_t* pool, const kvc_plan_t* plan, int layer_idx, const void* d_x_in, void* d_x_out,
+    const void* d_attn_norm_w, const void* d_wq, int wq_type, const void* d_wk, int wk_type,
+    const void* d_wv, int wv_type, const void* d_wo, int wo_type, const void* d_ffn_norm_w,
+    const void* d_wgate, int wgate_type, const void* d_wup, int wup_type, const void* d_wdown,
+    int wdown_type, const int32_t* d_block_tables, int bt_stride, int hidden_size,
+    int intermediate_size, float rms_norm_eps, float rope_freq_base, int rope_neox, float scale,
+    void* stream) {
+  if (!pool || !plan) return set_error(KVC_ERR_INVALID_ARG, "pool and plan must not be null.");
+  if (!plan->valid) return set_error(KVC_ERR_INVALID_ARG, "plan has not been built.");
+  const PoolGeom& g = pool->g;
+  if (g.dtype != KVC_DTYPE_F16)
+    return set_error(KVC_ERR_INVALID_ARG, "the layer pipeline needs an fp16 KV pool.");
+  if (layer_idx < 0 || layer_idx >= g.num_layers)
+    return set_error(KVC_ERR_OUT_OF_RANGE, "layer_idx out of range for the KV pool.");
+  if (plan->head_dim != g.head_dim || plan->num_kv_heads != g.num_kv_heads ||
+      plan->page_size != g.page_size)
+    return set_error(KVC_ERR_INVALID_ARG, "plan was built for a pool of another geometry.");
+  LayerDims d;
+  d.layer = layer_idx;
+  d.seq = plan->n_queries;
+  d.pos = 0;
+  d.hidden = hidden_size;
+  d.inter = intermediate_size;
+  d.H = plan->num_heads;
+  d.Hkv = g.num_kv_heads;
+  d.D = g.head_dim;
+  d.eps = rms_norm_eps;
+  d.base = rope_freq_base;
+  d.scale = scale;
+  d.neox = rope_neox != 0;
+  const int types[7] = {wq_type, wk_type, wv_type, wo_type, wgate_type, wup_type, wdown_type};
+  const void* w[7] = {d_wq, d_wk, d_wv, d_wo, d_wgate, d_wup, d_wdown};
+  int rc = check_layer(d, types);
+  if (rc) return rc;
+  if (!(rope_freq_base > 0.0f))
+    return set_error(KVC_ERR_INVALID_ARG, "rope_freq_base must be positive.");
+  for (int32_t c : plan->positions)
+    if (c < 0) return set_error(KVC_ERR_INVALID_ARG, "a query with an empty context has no new row.");
+  if (d.seq == 0) return KVC_OK;
+  if (!d_x_in || !d_x_out || !d_attn_norm_w || !d_ffn_norm_w || !d_block_tables)
+    return set_error(KVC_ERR_INVALID_ARG, "device buffers must not be null.");
+  LayerIO io;
+  for (int i = 0; i < 7; ++i) {
+    if (!w[i]) return set_error(KVC_ERR_INVALID_ARG, "weight buffers must not be null.");
+    io.w[i] = w[i];
+    io.type[i] = types[i];
+  }
+  io.x_in = static_cast<const __half*>(d_x_in);
+  io.x_out = static_cast<__half*>(d_x_out);
+  io.attn_norm = static_cast<const __half*>(d_attn_norm_w);
+  io.ffn_norm = static_cast<const __half*>(d_ffn_norm_w);
+  if (const int rc_dev = use_device(pool->device)) return rc_dev;
+  return layer_forward_paged(pool, const_cast<kvc_plan*>(plan), d_block_tables, bt_stride, io, d,
+                             static_cast<cudaStream_t>(stream));
 }

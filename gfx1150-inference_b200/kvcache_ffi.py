@@ -137,6 +137,10 @@ SIGNATURES = {
     "kvc_rmsnorm": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp]),
     "kvc_forward_layer_cached": (_c_int, _LAYER_ARGS),
     "kvc_forward_layer_cached_device": (_c_int, _LAYER_ARGS + [_vp]),
+    "kvc_forward_layer_paged": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, _c_int,
+                                         _vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _vp, _c_int,
+                                         _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_float,
+                                         _c_float, _c_int, _c_float, _vp]),
 }
 
 XCHG_HANDLE_BYTES = 64

@@ -213,6 +213,30 @@ class PagedKVCache:
             int(h_v.data_ptr()), int(h_out.data_ptr()), _i32(block_tables),
             int(block_tables.shape[-1]), float(scale), _sp(stream)))
 
+    def forward_layer(self, plan: DecodePlan, layer: int, x: torch.Tensor, out: torch.Tensor,
+                      weights: "DeviceLayerWeights", block_tables: torch.Tensor,
+                      eps: float = 1e-5, freq_base: float = 10000.0, neox: bool = False,
+                      scale: Optional[float] = None, stream=None):
+        """One transformer layer for the plan's queries (kvc_forward_layer_paged):
+        x / out (n_queries, hidden) fp16, token i being query i's new token at
+        position ctx_i - 1 of its block-table row.  out may be x."""
+        n = plan.n_queries * weights.hidden
+        sc = default_scale(self.head_dim) if scale is None else float(scale)
+        w = [int(t.data_ptr()) for t in weights.w]
+        for t in weights.w:
+            if not t.is_cuda or not t.is_contiguous():
+                raise ValueError("weights must be contiguous CUDA tensors")
+        ty = weights.types
+        ffi.check(ffi.lib.kvc_forward_layer_paged(
+            self.handle, plan.handle, layer, _dev(x, "x", torch.float16, n),
+            _dev(out, "out", torch.float16, n),
+            _dev(weights.attn_norm, "attn_norm", torch.float16, weights.hidden), w[0], ty[0],
+            w[1], ty[1], w[2], ty[2], w[3], ty[3],
+            _dev(weights.ffn_norm, "ffn_norm", torch.float16, weights.hidden), w[4], ty[4],
+            w[5], ty[5], w[6], ty[6], _i32(block_tables), int(block_tables.shape[-1]),
+            weights.hidden, weights.intermediate, float(eps), float(freq_base), int(bool(neox)),
+            sc, _sp(stream)))
+
     def gather(self, layer: int, block_tables: torch.Tensor, row: int, start: int, count: int,
                stream=None):
         k = torch.empty((count, self.num_kv_heads, self.head_dim), dtype=self.dtype,
@@ -233,6 +257,87 @@ class PagedKVCache:
             self.close()
         except Exception:
             pass
+
+
+@dataclass
+class DeviceLayerWeights:
+    """One transformer layer's weights resident on the GPU: the two RMSNorm
+    weights ((hidden,) fp16) and the seven GGML-typed weights (raw block bytes,
+    kvc_weight_bytes long) in the order q, k, v, o, gate, up, down, with their
+    type ids (KVC_WTYPE_*), as forward_layer_cached takes them."""
+    attn_norm: torch.Tensor
+    ffn_norm: torch.Tensor
+    w: Sequence[torch.Tensor]
+    types: Sequence[int]
+    hidden: int
+    intermediate: int
+
+
+class BatchDecoder:
+    """The decode loop of generate_batch_ids (src/inference.py:435-447) on the
+    paged pool: the reference decodes its prompts one after another, one
+    forward_layer_cached call per (sequence, layer, token); here every sequence
+    of the batch advances by one token per step, one kvc_forward_layer_paged
+    call per layer for the whole batch.  Sequence i owns block-table row i;
+    ``ctx_lens[i]`` counts its cached positions.  The embedding lookup, the
+    final norm, the LM head and sampling stay with the caller."""
+
+    def __init__(self, cache: PagedKVCache, layers: Sequence[DeviceLayerWeights],
+                 block_tables: torch.Tensor, num_heads: int, ctx_lens: Sequence[int],
+                 eps: float = 1e-5, freq_base: float = 10000.0, neox: bool = False,
+                 scale: Optional[float] = None):
+        if len(layers) != cache.num_layers:
+            raise ValueError("one DeviceLayerWeights per pool layer is required")
+        if block_tables.dim() != 2 or block_tables.shape[0] < len(ctx_lens):
+            raise ValueError("block_tables needs one row per sequence")
+        self.cache, self.layers, self.bt = cache, list(layers), block_tables
+        self.num_heads = int(num_heads)
+        self.ctx = np.asarray(ctx_lens, dtype=np.int64).copy()
+        self.eps, self.freq_base, self.neox, self.scale = eps, freq_base, neox, scale
+        self.plan = DecodePlan()
+        self.capacity = int(block_tables.shape[1]) * cache.page_size
+
+    def prefill(self, seq: int, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """Run tokens x (n, hidden) of sequence `seq` at positions ctx_lens[seq]..
+        through every layer (causal over the cached prefix and the chunk itself);
+        returns the last layer's output (n, hidden)."""
+        n = int(x.shape[0])
+        if n == 0:
+            return x
+        p0 = int(self.ctx[seq])
+        if p0 + n > self.capacity:
+            raise IndexError("prefill exceeds the sequence's block-table capacity")
+        self.cache.plan(np.arange(p0 + 1, p0 + n + 1), self.num_heads, rows=[seq] * n,
+                        plan=self.plan, stream=stream)
+        y = self._layers(x, stream)
+        self.ctx[seq] += n
+        return y
+
+    def step(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """One decode step: token i of x (batch, hidden) is sequence i's next token
+        at position ctx_lens[i]; returns the last layer's output (batch, hidden)."""
+        b = len(self.ctx)
+        if int(x.shape[0]) != b:
+            raise ValueError(f"x must hold one token per sequence ({b})")
+        if int(self.ctx.max(initial=0)) + 1 > self.capacity:
+            raise IndexError("a sequence would exceed its block-table capacity")
+        self.cache.plan(self.ctx + 1, self.num_heads, plan=self.plan, stream=stream)
+        y = self._layers(x, stream)
+        self.ctx += 1
+        return y
+
+    def _layers(self, x: torch.Tensor, stream) -> torch.Tensor:
+        cur = x.contiguous()
+        bufs = (torch.empty_like(cur), torch.empty_like(cur))   # x itself is never written
+        for layer, lw in enumerate(self.layers):
+            nxt = bufs[layer % 2]
+            self.cache.forward_layer(self.plan, layer, cur, nxt, lw, self.bt, self.eps,
+                                     self.freq_base, self.neox, self.scale, stream)
+            cur = nxt
+        return cur
+
+    def close(self):
+        self.plan.close()
 
 
 # -- layout helpers -------------------------------------------------------------------

@@ -456,6 +456,26 @@ KVC_API int kvc_forward_layer_cached_device(
     int hidden_size, int intermediate_size, int num_heads, int num_kv_heads, int head_dim,
     float rms_norm_eps, float rope_freq_base, int rope_neox, float scale, void* stream);
 
+/* One decode step of one layer for a BATCH of sequences on a paged pool: the
+ * batched counterpart of kvc_forward_layer_cached_device, for the decode loop of
+ * generate_batch_ids (src/inference.py:435-447), which the reference runs one
+ * sequence at a time through forward_layer_cached (attention.hip:603-695).
+ * Token i of d_x_in / d_x_out ((n, hidden_size) fp16, n = the plan's query
+ * count) is the new token of query i of `plan` (kvc_plan_decode): it is rotated
+ * at position ctx_i - 1, its K/V row is appended there in block-table row
+ * rows[i], and it attends over positions [0, ctx_i).  Head counts come from the
+ * plan (q-heads) and the fp16 pool (KV heads, head_dim); weights as in
+ * kvc_forward_layer_cached.  The activations live in a workspace of the plan, so
+ * calls sharing a plan must be ordered on one stream.  x_out may alias x_in. */
+KVC_API int kvc_forward_layer_paged(
+    kvc_pool_t* pool, const kvc_plan_t* plan, int layer_idx, const void* d_x_in, void* d_x_out,
+    const void* d_attn_norm_w, const void* d_wq, int wq_type, const void* d_wk, int wk_type,
+    const void* d_wv, int wv_type, const void* d_wo, int wo_type, const void* d_ffn_norm_w,
+    const void* d_wgate, int wgate_type, const void* d_wup, int wup_type, const void* d_wdown,
+    int wdown_type, const int32_t* d_block_tables, int bt_stride, int hidden_size,
+    int intermediate_size, float rms_norm_eps, float rope_freq_base, int rope_neox, float scale,
+    void* stream);
+
 #ifdef __cplusplus
 }
 #endif
