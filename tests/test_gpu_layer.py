@@ -133,6 +133,25 @@ def test_linear_epilogues(w_type, m):
     assert _maxerr(got, ref) <= 2e-3 * max(1.0, float(np.abs(ref.astype(np.float32)).max()))
 
 
+@pytest.mark.parametrize("w_type", [L.F16, L.Q4_0, L.Q8_0, L.Q4_K])
+@pytest.mark.parametrize("m", [9, 20, 32])
+def test_linear_batch_tokens_long_k(w_type, m):
+    """9-32 tokens (the 32-token tiles a batched decode step uses) at the down
+    projection's k = 14336, n = 208 (13 row tiles); store and residual epilogues."""
+    rng = np.random.default_rng(400 + w_type + m)
+    n, k = 208, 14336
+    x = (rng.standard_normal((m, k), dtype=np.float32) * 0.5).astype(np.float16)
+    raw = L.random_weight(rng, w_type, n, k)
+    ref = L.linear(x, raw, w_type, n)
+    got = _linear_dev(x, raw, w_type, n)
+    tol = 2e-3 * max(1.0, float(np.abs(ref.astype(np.float32)).max()))
+    assert _maxerr(got, ref) <= tol, (w_type, m, _maxerr(got, ref))
+    res = (rng.standard_normal((m, n), dtype=np.float32)).astype(np.float16)
+    got = _linear_dev(x, raw, w_type, n, "residual", res=res)
+    ref = L.residual_add(res, ref)
+    assert _maxerr(got, ref) <= 2e-3 * max(1.0, float(np.abs(ref.astype(np.float32)).max()))
+
+
 def test_linear_rejects_bad_shapes():
     x = torch.zeros((1, 256), dtype=torch.float16, device="cuda")
     w = torch.zeros(4096, dtype=torch.uint8, device="cuda")

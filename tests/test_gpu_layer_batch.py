@@ -85,14 +85,14 @@ def _tol_rows(ref):
 
 @pytest.mark.parametrize("neox", [False, True])
 def test_forward_layer_paged_matches_oracle(neox):
-    """Two layers, four sequences with ragged cached prefixes (0 .. 150 positions,
+    """Two layers, twelve sequences with ragged cached prefixes (0 .. 150 positions,
     pages in a random permutation): a causal prefill chunk per sequence through the
-    same entry point (queries sharing a block-table row), then two batched decode
-    steps.  Every row against the oracle run on that sequence alone; the pool rows
-    against the oracle's cache."""
+    same entry point (queries sharing a block-table row; chunks of 1-150 tokens),
+    then two batched decode steps of 12 tokens.  Every row against the oracle run
+    on that sequence alone; the pool rows against the oracle's cache."""
     rng = np.random.default_rng(2024 + neox)
     n_layers = 2
-    pre = [36, 0, 89, 150]
+    pre = [36, 0, 89, 150, 17, 25, 31, 5, 64, 9, 1, 40]
     steps = 2
     table, total = paged.random_block_tables([p + steps for p in pre], PS, seed=3)
     pool = paged.PagedKVCache(n_layers, total, PS, HKV, D)
