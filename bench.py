@@ -684,6 +684,17 @@ LAYER_TYPES = {"q4_0": (2,) * 7, "q8_0": (8,) * 7, "f16": (1,) * 7,
                "q4_k_m": (12, 12, 14, 12, 12, 12, 14)}
 
 
+def layer_launches(types) -> int:
+    """Kernel launches of one decode layer call: two RMSNorms, one projection launch
+    per run of equal q/k/v types, RoPE, the fused append + decode and its split merge,
+    the output projection, gate + up (one SwiGLU launch for equal types, else two
+    projections and the SwiGLU kernel) and the down projection."""
+    q, k, v, _, gate, up, _ = types
+    qkv = 1 + (k != q) + (v != k)
+    ffn = 1 if gate == up else 3
+    return 7 + qkv + ffn
+
+
 def run_layer(args, rank, world, local_rank):
     """Whole-layer decode (forward_layer_cached, the layer the KV path serves):
     Llama-3-8B geometry (hidden 4096, intermediate 14336, 32 q-heads, 8 KV heads,
@@ -827,7 +838,7 @@ def run_layer(args, rank, world, local_rank):
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_kind": peak_kind, "bytes_per_layer": int(layer_bytes)},
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-        "gpu_launches": L * args.steps * 10,
+        "gpu_launches": L * args.steps * layer_launches(types),
     }
 
 
@@ -955,7 +966,7 @@ def run_layer_batch(args, rank, world, local_rank):
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_kind": peak_kind, "bytes_per_step": int(step_b)},
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-        "gpu_launches": L * args.steps * 11,
+        "gpu_launches": L * args.steps * layer_launches(types),
     }
 
 
