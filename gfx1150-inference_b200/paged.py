@@ -222,11 +222,13 @@ class PagedKVCache:
         position ctx_i - 1 of its block-table row.  out may be x."""
         n = plan.n_queries * weights.hidden
         sc = default_scale(self.head_dim) if scale is None else float(scale)
-        w = [int(t.data_ptr()) for t in weights.w]
+        if len(weights.w) != 7 or len(weights.types) != 7:
+            raise ValueError("a layer has seven weights: q, k, v, o, gate, up, down")
         for t in weights.w:
             if not t.is_cuda or not t.is_contiguous():
                 raise ValueError("weights must be contiguous CUDA tensors")
-        ty = weights.types
+        w = [int(t.data_ptr()) for t in weights.w]
+        ty = [int(t) for t in weights.types]
         ffi.check(ffi.lib.kvc_forward_layer_paged(
             self.handle, plan.handle, layer, _dev(x, "x", torch.float16, n),
             _dev(out, "out", torch.float16, n),
