@@ -7,6 +7,11 @@
 // fused decode kernel for one token; append then attend for a prefill chunk) →
 // output projection → residual + RMSNorm → gate/up projections with the SwiGLU in
 // their epilogue → down projection with the residual in its epilogue.
+//
+// The same layer runs for a batch of sequences on a paged pool
+// (kvc_forward_layer_paged, the batched form of generate_batch_ids'
+// one-sequence-at-a-time loop, inference.py:435-447): one token per query of a
+// decode plan, rotated at the plan's positions, appended into its block-table row.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
