@@ -245,302 +245,469 @@ def cpu_sample(cfg, ctx, min_seconds=10.0, max_reps=50):
 # ---------------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------------
-def run_b200(args, rank, world, local_rank):
-    import torch
+class DecodeWorkload:
+    """One benchmark configuration (2, 3 or 4) set up on this rank's GPU, and its
+    decode step: per layer, append each sequence's new K/V row at its last
+    position and attend over the whole context (one fused launch + split merge).
 
-    import kvcache_ffi as ffi
-    import paged
+    shard "seq": this rank holds its own ``batch`` sequences, all KV heads (no
+    collective).  shard "heads" with world > 1: KV heads [r*Hkv/N, (r+1)*Hkv/N)
+    of every sequence and their q-heads; each layer's outputs are exchanged
+    (``xchg`` "p2p": the merge kernel stores them into every rank's exchange slot
+    over NVLink; "nccl": all-gather).  ``one_rank_of`` > 1 on one GPU: rank 0's
+    shard of that split with its exchange connected to itself (profiling).
+    ``grow_extra`` positions per sequence are paged in for growing decode loops.
+    Contents: seeded N(0,1) pages, q and new rows."""
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    cfg = dict(CONFIGS[args.config])
-    if args.layers:
-        cfg["layers"] = args.layers  # profiling subset only (the bench line names it)
-    L, H, Hkv, D, B = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["batch"]
-    shard = args.shard or ("heads" if args.config == "4" else "seq")
-    H_full = H
-    if shard == "heads" and world > 1:
-        # KV-head sharding: this rank owns KV heads [r*Hkv/n, (r+1)*Hkv/n) and their
-        # q-heads; the per-head outputs are all-gathered after every layer.
-        h0, h1 = paged.shard_heads(Hkv, world, rank)
-        Hkv = h1 - h0
-        H = H * Hkv // cfg["Hkv"]
-    one_rank_of = args.one_rank_of if world == 1 else 0
-    if one_rank_of > 1:
-        # profiling mode: rank 0's shard of a one_rank_of-way KV-head split on this one
-        # GPU, its head exchange connected to itself (same kernels and launches as a
-        # real rank, no peers to wait for)
-        h0, h1 = paged.shard_heads(Hkv, one_rank_of, 0)
-        Hkv = h1 - h0
-        H = H * Hkv // cfg["Hkv"]
-    cached = cached_lengths(cfg)
-    ctx = cached + 1                                  # context includes the appended token
-    # --grow: every step appends one more position (a real decode loop), so pages
-    # for the extra positions are allocated up front
-    extra = (args.warmup + args.steps + 1) if args.grow else 0
-    table, total_pages = paged.random_block_tables(ctx + extra, args.page_size,
-                                                   cfg["seed"] + 17 * rank)
-    pool = paged.PagedKVCache(L, total_pages, args.page_size, Hkv, D, dtype=torch.float16,
-                              device=local_rank)
-    pool.fill_normal(seed=1000 + rank, stddev=1.0)
-    bt = torch.from_numpy(table).to(dev)
-    g = torch.Generator(device=dev)
-    g.manual_seed(7 + rank)
-    q = torch.randn((L, B, H, D), generator=g, device=dev, dtype=torch.float32).half()
-    kn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
-    vn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
-    out = torch.empty_like(q)
-    gathered = None
-    if shard == "heads" and world > 1:
-        import sharding
+    def __init__(self, config="3", layers=0, rank=0, world=1, local_rank=0, shard="seq",
+                 xchg="p2p", page_size=PAGE, grow_extra=0, rope=False, one_rank_of=0,
+                 kv_stable=True):
+        import torch
 
-        # every rank ends each layer with all heads of every sequence
-        gathered = torch.empty((L, B, H_full, D), dtype=torch.float16, device=dev)
-        hsd = sharding.HeadShardedDecode(pool, H_full, cfg["Hkv"], transport=args.xchg,
-                                         num_queries=B)
-    self_xchg = None
-    if one_rank_of > 1:
-        self_xchg = ctypes.c_void_p()
-        ffi.check(ffi.lib.kvc_xchg_create(local_rank, 0, 1, B * H_full * D * 2, 2,
-                                          ctypes.byref(self_xchg)))
-        base = ctypes.c_void_p()
-        ffi.check(ffi.lib.kvc_xchg_base(self_xchg, ctypes.byref(base)))
-        ffi.check(ffi.lib.kvc_xchg_connect_ptrs(self_xchg, (ctypes.c_void_p * 1)(base.value)))
-    pos = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
-    rows = torch.arange(B, dtype=torch.int32, device=dev)
-    scale = 1.0 / math.sqrt(D)
-    stream = torch.cuda.current_stream()
-    plan = pool.plan(ctx, H, stream=stream)
-    # block tables are static and pages are written only by the decode kernels
-    # themselves, so each launch may start streaming KV before the previous one ends
-    plan.set_kv_stable(True)
-    torch.cuda.synchronize()
+        import kvcache_ffi as ffi
+        import paged
 
-    grown = [0]  # steps taken so far (--grow)
+        self.torch, self.ffi = torch, ffi
+        dev = torch.device("cuda", local_rank)
+        self.dev, self.local_rank, self.rank, self.world = dev, local_rank, rank, world
+        cfg = dict(CONFIGS[config])
+        if layers:
+            cfg["layers"] = layers  # profiling / test subset (the bench line names it)
+        self.cfg, self.config = cfg, config
+        L, H, Hkv, D, B = cfg["layers"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["batch"]
+        self.H_full, self.Hkv_full = H, Hkv
+        self.shard = shard if world > 1 else "seq"
+        self.xchg = xchg
+        self.head_offset = 0
+        if self.shard == "heads":
+            h0, h1 = paged.shard_heads(Hkv, world, rank)
+            self.head_offset = h0 * (H // Hkv)
+            Hkv = h1 - h0
+            H = H * Hkv // cfg["Hkv"]
+        self.one_rank_of = one_rank_of if world == 1 else 0
+        if self.one_rank_of > 1:
+            h0, h1 = paged.shard_heads(Hkv, self.one_rank_of, 0)
+            Hkv = h1 - h0
+            H = H * Hkv // cfg["Hkv"]
+        self.L, self.H, self.Hkv, self.D, self.B = L, H, Hkv, D, B
+        self.page_size = page_size
+        self.rope = rope
+        cached = cached_lengths(cfg)
+        self.ctx = cached + 1                           # context includes the appended token
+        table, self.total_pages = paged.random_block_tables(self.ctx + grow_extra, page_size,
+                                                            cfg["seed"] + 17 * rank)
+        self.grow_extra = grow_extra
+        self.pool = paged.PagedKVCache(L, self.total_pages, page_size, Hkv, D,
+                                       dtype=torch.float16, device=local_rank)
+        self.pool.fill_normal(seed=1000 + rank, stddev=1.0)
+        self.bt = torch.from_numpy(table).to(dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(7 + rank)
+        self.q = torch.randn((L, B, H, D), generator=g, device=dev, dtype=torch.float32).half()
+        self.kn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
+        self.vn = torch.randn((L, B, Hkv, D), generator=g, device=dev, dtype=torch.float32).half()
+        self.out = torch.empty_like(self.q)
+        self.gathered = None
+        self.hsd = None
+        if self.shard == "heads":
+            import sharding
 
-    def step(events=None, s=None):
-        # one fused launch per layer: append each sequence's new row + attend
-        s = stream if s is None else s
-        if args.grow:
-            # the contexts grew by one since the last step: a new plan (host), then the layers
-            pool.plan(ctx + grown[0], H, plan=plan, stream=s)
-            grown[0] += 1
-        for l in range(L):
+            # every rank ends each layer with all heads of every sequence
+            self.hsd = sharding.HeadShardedDecode(self.pool, self.H_full, self.Hkv_full,
+                                                  transport=xchg, num_queries=B)
+            if xchg == "nccl":
+                self.gathered = torch.empty((L, B, self.H_full, D), dtype=torch.float16,
+                                            device=dev)
+        self.self_xchg = None
+        if self.one_rank_of > 1:
+            import ctypes
+
+            self.self_xchg = ctypes.c_void_p()
+            ffi.check(ffi.lib.kvc_xchg_create(local_rank, 0, 1, B * self.H_full * D * 2, 2,
+                                              ctypes.byref(self.self_xchg)))
+            base = ctypes.c_void_p()
+            ffi.check(ffi.lib.kvc_xchg_base(self.self_xchg, ctypes.byref(base)))
+            ffi.check(ffi.lib.kvc_xchg_connect_ptrs(self.self_xchg,
+                                                    (ctypes.c_void_p * 1)(base.value)))
+        self.scale = 1.0 / math.sqrt(D)
+        self.stream = torch.cuda.current_stream()
+        self.grown = 0
+        self.plan = self.pool.plan(self.ctx, H, stream=self.stream)
+        # block tables are static and pages are written only by the decode kernels
+        # themselves, so each launch may start streaming KV before the previous one ends
+        self.plan.set_kv_stable(kv_stable)
+        torch.cuda.synchronize()
+
+    @property
+    def p2p(self) -> bool:
+        return (self.hsd is not None and self.xchg == "p2p") or self.self_xchg is not None
+
+    def launches_per_step(self) -> int:
+        return (3 if self.p2p or (self.rope and self.hsd is None) else 2) * self.L
+
+    def current_ctx(self):
+        return self.ctx + self.grown
+
+    def step(self, s=None, grow=False, events=None, results=None):
+        """One decode step over all layers on stream ``s``.  grow: the contexts grow
+        by one position first (a new plan on the host, then the layers).  results:
+        a dict that receives layer -> a copy of that layer's (all-heads) output."""
+        s = self.stream if s is None else s
+        if grow:
+            if self.grown >= self.grow_extra:
+                raise RuntimeError("the workload was set up for fewer growing steps")
+            self.grown += 1
+            self.pool.plan(self.ctx + self.grown, self.H, plan=self.plan, stream=s)
+        for l in range(self.L):
             if events is not None:
                 events[l][0].record(s)
-            if self_xchg is not None:
-                pool.append_decode_xchg(plan, l, q[l], kn[l], vn[l], self_xchg, l & 1, H_full, 0,
-                                        bt, scale, stream=s)
-            elif gathered is None and args.rope:
+            res = self.out[l]
+            if self.self_xchg is not None:
+                self.pool.append_decode_xchg(self.plan, l, self.q[l], self.kn[l], self.vn[l],
+                                             self.self_xchg, l & 1, self.H_full, 0, self.bt,
+                                             self.scale, stream=s)
+            elif self.hsd is None and self.rope:
                 # rotate q and the new K row (RoPE at each sequence's position) first
-                pool.append_decode_rope(plan, l, q[l], kn[l], vn[l], out[l], bt, scale,
-                                        ROPE_BASE, False, stream=s)
-            elif gathered is None:
-                pool.append_decode(plan, l, q[l], kn[l], vn[l], out[l], bt, scale, stream=s)
+                self.pool.append_decode_rope(self.plan, l, self.q[l], self.kn[l], self.vn[l],
+                                             self.out[l], self.bt, self.scale, ROPE_BASE, False,
+                                             stream=s)
+            elif self.hsd is None:
+                self.pool.append_decode(self.plan, l, self.q[l], self.kn[l], self.vn[l],
+                                        self.out[l], self.bt, self.scale, stream=s)
             else:
                 # fused append + attention on this rank's heads; p2p: the merge kernel
                 # pushes the heads to every rank (result in an exchange slot), nccl:
                 # all-gather + copy into gathered[l]
-                hsd.append_decode(plan, l, q[l], kn[l], vn[l],
-                                  gathered[l] if args.xchg == "nccl" else None, bt, scale,
-                                  stream=s)
+                res = self.hsd.append_decode(
+                    self.plan, l, self.q[l], self.kn[l], self.vn[l],
+                    self.gathered[l] if self.xchg == "nccl" else None, self.bt, self.scale,
+                    stream=s)
             if events is not None:
                 events[l][1].record(s)
+            if results is not None and self.self_xchg is None:
+                with self.torch.cuda.stream(s):
+                    results[l] = res.clone()
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    code, info = ffi.device_error(local_rank)
+    def step_bytes(self, ctx=None):
+        """Algorithmic bytes of one step on this rank: (KV read, appended, q + out)."""
+        return step_bytes(dict(self.cfg, H=self.H, Hkv=self.Hkv),
+                          self.current_ctx() if ctx is None else ctx)
+
+    def close(self):
+        if self.hsd is not None:
+            self.hsd.close()  # collective: exchange buffers freed after every rank is done
+            self.hsd = None
+        if self.self_xchg is not None:
+            self.torch.cuda.synchronize()
+            self.ffi.lib.kvc_xchg_destroy(self.self_xchg)
+            self.self_xchg = None
+        self.plan.close()
+        self.pool.close()
+
+
+def _max_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    return float(t.item())
+
+
+def timed_passes(wl, steps, passes, grow=False, graph=None, events=None):
+    """``passes`` timed passes of exactly ``steps`` steps each, every pass
+    bracketed by a barrier and a device synchronisation, timed with CUDA events
+    on the launching stream.  Returns [(ms, bytes of the pass on this rank)]."""
+    torch = wl.torch
+    out = []
+    for p in range(passes):
+        parts = []
+        if wl.world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(wl.stream)
+        for i in range(steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                wl.step(grow=grow, events=events[i] if events else None)
+            if grow:
+                parts.append(sum(wl.step_bytes()))
+        t1.record(wl.stream)
+        torch.cuda.synchronize()
+        if wl.world > 1:
+            torch.distributed.barrier()
+        nbytes = sum(parts) if grow else steps * sum(wl.step_bytes())
+        out.append((t0.elapsed_time(t1), nbytes))
+    return out
+
+
+def _check_device(wl, what):
+    code, info = wl.ffi.device_error(wl.local_rank)
     if code:
-        raise RuntimeError(f"device error {code} ({info}) during warm-up")
+        raise RuntimeError(f"device error {code} ({info}) {what}")
+
+
+def _pass_figures(wl, passes_res):
+    """The median pass by throughput: (ms of the pass, max over ranks; bytes of the
+    pass summed over ranks; this rank's bytes of the pass)."""
+    figs = []
+    for ms, nb in passes_res:
+        figs.append((_max_over_ranks(ms, wl.world, wl.dev),
+                     _sum_over_ranks(float(nb), wl.world, wl.dev), float(nb)))
+    figs.sort(key=lambda f: f[1] / f[0], reverse=True)
+    return figs[len(figs) // 2]
+
+
+def exchange_parity(wl, layers=None):
+    """Head-sharded runs: run one step directly, keep the exchanged (all-heads)
+    outputs of a few layers, and compare them with this rank's own heads decoded
+    without the exchange (kvc_decode on the same pool and plan), all-gathered over
+    NCCL.  True on every rank when each layer agrees within the fp16 bound."""
+    torch = wl.torch
+    import sharding
+
+    layers = layers or sorted({0, wl.L // 2, wl.L - 1})
+    got = {}
+    wl.step(results=got)
+    torch.cuda.synchronize()
+    _check_device(wl, "in the exchange check")
+    worst = 0.0
+    for l in layers:
+        loc = torch.empty_like(wl.q[l])
+        wl.pool.decode(wl.plan, l, wl.q[l], loc, wl.bt, wl.scale)
+        full = torch.empty((wl.B, wl.H_full, wl.D), dtype=loc.dtype, device=loc.device)
+        sharding.gather_head_outputs(loc, full)
+        ref = full.float()
+        d = (got[l].float() - ref).abs().amax(dim=(1, 2))
+        m = ref.abs().amax(dim=(1, 2)).clamp_min(1e-30)
+        worst = max(worst, float((d / m).max().item()))
+    worst = _max_over_ranks(worst, wl.world, wl.dev)
+    return worst <= 2e-3, worst
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+
+    import kvcache_ffi as ffi
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    shard = args.shard or ("heads" if world > 1 or args.config == "4" else "seq")
+    cfg0 = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg0["layers"] = args.layers
+    # upper bound of the timed passes (each pass >= its bytes at 7 TB/s per GPU), so
+    # the growing loop's pages can be laid out before anything runs
+    ctx0 = cached_lengths(cfg0) + 1
+    t_min = sum(step_bytes(cfg0, ctx0)) / max(1, world if shard == "heads" else 1) / 7.0e12
+    max_passes = max(1, min(args.max_passes,
+                            math.ceil(args.min_timed_s / max(1e-6, args.steps * t_min)) + 1))
+    grow_steps = (args.warmup + max_passes * args.steps + 2) if not args.no_grow else 0
+    wl = DecodeWorkload(args.config, layers=args.layers, rank=rank, world=world,
+                        local_rank=local_rank, shard=shard, xchg=args.xchg,
+                        page_size=args.page_size, grow_extra=grow_steps, rope=args.rope,
+                        one_rank_of=args.one_rank_of)
+    L = wl.L
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+
+    # ---- fixed step: the same step replayed (one CUDA graph per step) ----
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    _check_device(wl, "during warm-up")
     graph = None
-    if not args.no_graph and not args.launch_events and not args.grow:
-        # The step's 2 x L launches are recorded once into a CUDA graph and replayed:
-        # the same kernels, without the host's per-launch cost between them.
+    if not args.no_graph and not args.launch_events:
+        # The step's launches are recorded once into a CUDA graph and replayed: the
+        # same kernels, without the host's per-launch cost between them.
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            step(s=torch.cuda.current_stream())
+            wl.step(s=torch.cuda.current_stream())
         graph.replay()  # one untimed replay
         torch.cuda.synchronize()
-        code, info = ffi.device_error(local_rank)
-        if code:
-            raise RuntimeError(f"device error {code} ({info}) in the captured step")
-
-    # Per-launch events would serialise consecutive launches (they overlap by
-    # programmatic dependent launch), so they are only recorded on request.
+        _check_device(wl, "in the captured step")
     evs = ([[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
             for _ in range(args.steps)] if args.launch_events else None)
-    sampler = ClockSampler(local_rank) if not args.no_clocks else None
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
+    # calibrate: one pass, then as many passes as fill min_timed_s
+    first = timed_passes(wl, args.steps, 1, graph=graph, events=evs)
+    pass_ms = _max_over_ranks(first[0][0], world, dev)
+    passes = max(1, min(max_passes, math.ceil(args.min_timed_s * 1e3 / max(pass_ms, 1e-3))))
     if sampler:
         sampler.start()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_stop = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for s in range(args.steps):
-        if graph is not None:
-            graph.replay()
-        else:
-            step(evs[s] if evs else None)
-    t_stop.record(stream)
-    torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
-    if world > 1:
-        torch.distributed.barrier()
-    elapsed_ms = t_start.elapsed_time(t_stop)
-    used_graph = graph is not None
-    hsd_p2p = (gathered is not None and args.xchg == "p2p") or self_xchg is not None
+    fixed_res = timed_passes(wl, args.steps, passes, graph=graph, events=evs)
+    fixed_clocks = sampler.stop() if sampler else None
+    _check_device(wl, "during timing")
     if graph is not None:
         graph.reset()  # released before any collective teardown (it may hold NCCL calls)
         graph = None
-    dec_ms = ([evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(args.steps) for l in range(L)]
-              if evs else None)
-    code, info = ffi.device_error(local_rank)
-    if code:
-        raise RuntimeError(f"device error {code} ({info}) during timing")
+    f_ms, f_bytes, f_local = _pass_figures(wl, fixed_res)
+    fixed = {"value": round(f_bytes / (f_ms / 1e3) / 1e9, 1),
+             "ms_per_step": round(f_ms / args.steps, 4), "passes": passes,
+             "launch": ("one CUDA graph replay per step (the step's launches)"
+                        if not args.no_graph and not args.launch_events
+                        else "direct launches from the host loop")}
+    dec_ms = ([evs[i][l][0].elapsed_time(evs[i][l][1]) for i in range(args.steps)
+               for l in range(L)] if evs else None)
+    kv_read = wl.step_bytes()[0]
+    # roofline of the dominant kernel: this rank's bytes per decode launch (one layer)
+    # over the launch's average duration in the headline measurement
+    dec_bytes = f_local / (args.steps * L)
+    dec_avg_ms = float(np.mean(dec_ms)) if dec_ms else f_ms / (args.steps * L)
+    dec_from = ("per-launch CUDA events" if dec_ms else
+                "CUDA events around the fixed-step timed passes / launches (launches overlap)")
 
-    kv_read, appended, qo = step_bytes(dict(cfg, H=H, Hkv=Hkv), ctx)
-    if args.grow:  # the timed steps ran at contexts ctx + warmup ... ctx + warmup + steps - 1
-        parts = [step_bytes(dict(cfg, H=H, Hkv=Hkv), ctx + args.warmup + i)
-                 for i in range(args.steps)]
-        kv_read, appended, qo = (sum(p[0] for p in parts) // args.steps,
-                                 sum(p[1] for p in parts) // args.steps,
-                                 sum(p[2] for p in parts) // args.steps)
-    rank_bytes = kv_read + appended + qo
-    # aggregate: max time over ranks, sum of bytes
-    if world > 1:
-        t = torch.tensor([elapsed_ms, float(rank_bytes)], dtype=torch.float64, device=dev)
-        tmax = t[:1].clone()
-        torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
-        tsum = t[1:].clone()
-        torch.distributed.all_reduce(tsum, op=torch.distributed.ReduceOp.SUM)
-        elapsed_ms, job_bytes = float(tmax.item()), float(tsum.item())
-    else:
-        job_bytes = float(rank_bytes)
-    ms_per_step = elapsed_ms / args.steps
-    value = job_bytes / (ms_per_step / 1e3) / 1e9
+    # ---- growing decode loop: contexts +1 per step, plan rebuilt every step ----
+    grow = None
+    clocks = fixed_clocks
+    if not args.no_grow:
+        for _ in range(args.warmup):
+            wl.step(grow=True)
+        torch.cuda.synchronize()
+        _check_device(wl, "during the growing loop's warm-up")
+        sampler = ClockSampler(local_rank) if not args.no_clocks else None
+        if sampler:
+            sampler.start()
+        grow_res = timed_passes(wl, args.steps, passes, grow=True)
+        clocks = sampler.stop() if sampler else fixed_clocks
+        _check_device(wl, "during the growing loop")
+        g_ms, g_bytes, g_local = _pass_figures(wl, grow_res)
+        if not dec_ms:
+            dec_bytes = g_local / (args.steps * L)
+            dec_avg_ms = g_ms / (args.steps * L)
+            dec_from = ("CUDA events around the growing loop's timed passes / launches "
+                        "(launches overlap)")
+        grow = {"value": round(g_bytes / (g_ms / 1e3) / 1e9, 1),
+                "ms_per_step": round(g_ms / args.steps, 4), "passes": passes,
+                "ctx_tokens_per_gpu_last": int(wl.current_ctx().sum()),
+                "launch": "direct launches from the host loop; the plan is rebuilt on the "
+                          "host every step inside the timed region"}
+
+    # ---- exchange check (head-sharded runs) ----
+    xparity = None
+    if wl.hsd is not None:
+        ok, worst = exchange_parity(wl)
+        xparity = {"exchange_parity_ok": bool(ok), "worst_rel_err": worst,
+                   "checked": "layers 0, L/2, L-1: exchanged all-heads outputs vs every "
+                              "rank's own heads decoded without the exchange, all-gathered"}
+
+    headline = grow if grow is not None else fixed
+    value = headline["value"]
+    ms_per_step = headline["ms_per_step"]
+    # what the line reports about this rank's workload (before any variant replaces it)
+    L, H, Hkv, D, B, cfg = wl.L, wl.H, wl.Hkv, wl.D, wl.B, wl.cfg
+    info = wl.plan.info()
+    launches = wl.launches_per_step() * args.steps * passes * (2 if grow is not None else 1)
 
     # ---- e2e: reference-facing host-buffer call, per layer, copies inside ----
-    e2e = None
-    if not args.no_e2e:
-        hq = q.cpu().pin_memory()
-        hk = kn.cpu().pin_memory()
-        hv = vn.cpu().pin_memory()
-        ho = torch.empty_like(hq).pin_memory()
-        e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    e2e = run_e2e(wl, args) if not args.no_e2e else None
 
-        if gathered is not None:
-            hg = torch.empty(tuple(gathered.shape), dtype=torch.float16).pin_memory()
-            qd, kd, vd = torch.empty_like(q[0]), torch.empty_like(kn[0]), torch.empty_like(vn[0])
-            od = torch.empty_like(gathered[0])
-
-        def e2e_step():
-            for l in range(L):
-                if gathered is None:
-                    pool.decode_host(plan, l, hq[l], hk[l], hv[l], ho[l], bt, scale, stream=stream)
-                    continue
-                # sharded: rank inputs in, fused decode, all-gather, all heads out, wait
-                qd.copy_(hq[l], non_blocking=True)
-                kd.copy_(hk[l], non_blocking=True)
-                vd.copy_(hv[l], non_blocking=True)
-                res = hsd.append_decode(plan, l, qd, kd, vd,
-                                        od if args.xchg == "nccl" else None, bt, scale,
-                                        stream=stream)
-                hg[l].copy_(res, non_blocking=True)
-                stream.synchronize()
-
-        for _ in range(min(2, args.warmup)):
-            e2e_step()
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-        h2d = L * B * (H * D + 2 * Hkv * D) * 2
-        d2h = L * B * (H_full if gathered is not None else H) * D * 2
-        e2e = {"value": round(job_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
-               "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "call": ("kvc_decode_host (pinned host q/k_new/v_new/out, per layer, waits)"
-                        if gathered is None else
-                        "HeadShardedDecode.append_decode (pinned H2D of this rank's q/k/v, "
-                        "fused decode, NCCL all-gather, D2H of all heads, per layer, waits)")}
-
-    if gathered is not None:
-        hsd.close()  # collective: the exchange buffers are freed after every rank is done
-    if self_xchg is not None:
-        torch.cuda.synchronize()
-        ffi.lib.kvc_xchg_destroy(self_xchg)
+    # ---- extra lines of the same run (N > 1): the other sharding / transport ----
+    extra = {}
+    if world > 1 and wl.hsd is not None and not args.no_variants:
+        wl.close()
+        wl = None
+        torch.cuda.empty_cache()
+        for name, kw in (("seq_sharded", dict(shard="seq")),
+                         ("heads_nccl", dict(shard="heads", xchg="nccl"))):
+            v = DecodeWorkload(args.config, layers=args.layers, rank=rank, world=world,
+                               local_rank=local_rank, page_size=args.page_size,
+                               **dict(dict(xchg=args.xchg), **kw))
+            for _ in range(args.warmup):
+                v.step()
+            torch.cuda.synchronize()
+            _check_device(v, f"during the {name} warm-up")
+            g2 = None
+            if not args.no_graph:
+                g2 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g2):
+                    v.step(s=torch.cuda.current_stream())
+                g2.replay()
+                torch.cuda.synchronize()
+            r = timed_passes(v, args.steps, max(1, passes // 2), graph=g2)
+            if g2 is not None:
+                g2.reset()
+                g2 = None
+            ms, nb, _ = _pass_figures(v, r)
+            extra[name] = {"value": round(nb / (ms / 1e3) / 1e9, 1),
+                           "ms_per_step": round(ms / args.steps, 4),
+                           "scaling": "weak" if name == "seq_sharded" else "strong",
+                           "what": ("each rank its own 32 sequences, no collective"
+                                    if name == "seq_sharded" else
+                                    "KV-head split, NCCL all-gather of head outputs per layer "
+                                    "+ strided copy")}
+            v.close()
+            torch.cuda.empty_cache()
 
     if rank != 0:
+        if wl is not None:
+            wl.close()
         return None
 
     peak, peak_kind = load_peaks()
-    # average launch duration over the timed region (timed region / launches; with
-    # --launch-events, the mean of per-launch event pairs instead)
-    dec_avg_ms = float(np.mean(dec_ms)) if dec_ms else elapsed_ms / (args.steps * L)
-    dec_bytes = (kv_read + appended + qo) / L           # per launch (one layer)
     achieved = dec_bytes / (dec_avg_ms / 1e3) / 1e9
     res = {
         "metric": METRIC,
-        "value": round(value, 1),
+        "value": value,
         "unit": "GB/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 4),
+        "ms_per_step": ms_per_step,
         "steps_per_s": round(1e3 / ms_per_step, 2),
         "pct_of_peak": round(100.0 * value / (peak * world), 2),
         "higher_is_better": True,
-        "scaling": "strong" if gathered is not None else "weak",
+        "scaling": "strong" if shard == "heads" and world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "f16 storage, f32 accumulate",
         "data": "synthetic: seeded N(0,1) K/V/q, random page permutation",
         "config": {
             "workload": f"{cfg['workload']} (benchmark config {args.config})"
                         + (f" [profiling subset: {L} layers]" if args.layers else "")
-                        + (f" [profiling: one rank's shard of a {one_rank_of}-way KV-head split, "
-                           "exchange connected to itself]" if one_rank_of > 1 else ""),
-            "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D,
-            "sequences_per_gpu": B, "global_batch": B if gathered is not None else B * world,
+                        + (f" [profiling: one rank's shard of a {args.one_rank_of}-way KV-head "
+                           "split, exchange connected to itself]" if args.one_rank_of > 1 else ""),
+            "layers": L, "q_heads": cfg["H"], "kv_heads": cfg["Hkv"], "head_dim": cfg["D"],
+            "q_heads_per_gpu": H, "kv_heads_per_gpu": Hkv,
+            "sequences_per_gpu": cfg["batch"],
+            "global_batch": cfg["batch"] if shard == "heads" else cfg["batch"] * world,
             "cached_len": (f"U[{cfg['lens'][1]},{cfg['lens'][2]}] seed {cfg['seed']}"
                            if cfg["lens"][0] == "uniform" else int(cfg["lens"][1])),
-            "ctx_tokens_per_gpu": int(ctx.sum()), "page_size": args.page_size,
-            "pool_gb_per_gpu": round(2 * L * total_pages * Hkv * args.page_size * D * 2 / 1e9, 2),
+            "ctx_tokens_per_gpu_start": int(ctx0.sum()), "page_size": args.page_size,
             "kv_bytes_read_per_step_per_gpu": kv_read,
             "l2": "inputs larger than L2 (pool >> 126 MB), no flush",
             "rope": bool(args.rope),
-            "grow": ("contexts grow by one position per step; the plan is rebuilt every step "
-                     "inside the timed region" if args.grow else False),
-            "launch": ("one CUDA graph replay per step (the step's 2 x layers kernel launches)"
-                       if used_graph else "direct launches from the host loop"),
+            "timed": (f"{passes} passes of exactly {args.steps} steps each, each pass between a "
+                      "barrier and a device sync; value = the median pass (max over ranks)"),
+            "headline": ("growing decode loop (contexts +1 per step, plan rebuilt every step "
+                         "inside the timed region)" if grow is not None else
+                         "fixed step replayed"),
             "parallelism": (f"KV-head-sharded x{world} ({Hkv} KV heads per GPU), "
                             + ("NCCL all-gather" if args.xchg == "nccl" else
                                "merge kernel pushes outputs to every rank over NVLink (p2p)")
                             + f", {B * H * D * 2} B of head outputs per GPU per layer"
-                            if gathered is not None else
+                            if shard == "heads" and world > 1 else
                             f"sequence-sharded x{world} (independent batches, no collective)"),
         },
+        "fixed_step": fixed,
         "roofline": {
             "bound": "hbm",
             "kernel": "decode_persistent_kernel (append fused) + merge_splits_kernel",
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
             "unit": "GB/s", "frac": round(achieved / peak, 4),
             "bytes_per_launch": int(dec_bytes), "avg_launch_us": round(dec_avg_ms * 1e3, 2),
-            "duration_from": ("per-launch CUDA events" if dec_ms else
-                              "CUDA events around the timed region / launches (launches overlap)"),
+            "duration_from": dec_from,
             "traffic": (TRAFFIC_PER_LAUNCH.get(args.config)
                         if not args.layers and world == 1 and args.page_size == PAGE else None),
             "traffic_from": "ncu dram__bytes_read.sum + dram__bytes_write.sum, decode kernel",
@@ -548,24 +715,93 @@ def run_b200(args, rank, world, local_rank):
         # per layer: the decode kernel and its split merge (PDL); with the p2p head
         # exchange the merge also pushes the outputs and a one-warp kernel
         # publishes and waits for the peers' epochs
-        "gpu_launches": (3 if hsd_p2p or (args.rope and gathered is None) else 2) * L * args.steps,
-        "plan": {"ctas_per_launch": plan.info().n_ctas, "splits": plan.info().n_items},
+        "gpu_launches": launches,
+        "plan": {"ctas_per_launch": info.n_ctas, "splits": info.n_items},
     }
+    if grow is not None:
+        res["grow"] = grow
+    if xparity is not None:
+        res.update(xparity)
+    if extra:
+        res["variants"] = extra
     if e2e:
         res["e2e"] = e2e
     if clocks:
         res["clocks"] = clocks
-    if not args.no_cpu_baseline:
-        gbs, dt, thr, reps = cpu_sample(cfg, ctx, min_seconds=args.cpu_seconds)
+    if not args.no_cpu_baseline and world == 1:
+        gbs, dt, thr, reps = cpu_sample(cfg, ctx0, min_seconds=args.cpu_seconds)
         res["cpu_baseline"] = {
             "value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-            "sample": f"1 of {L} layers x {B} sequences, {reps} reps, {dt * 1e3:.1f} ms/layer; "
-                      "oracle/gqa_online.c (reference kernel's algorithm, OpenMP)",
+            "sample": f"1 of {L} layers x {cfg['batch']} sequences, {reps} reps, "
+                      f"{dt * 1e3:.1f} ms/layer; oracle/gqa_online.c (reference kernel's "
+                      "algorithm, OpenMP)",
             "steps_per_s_extrapolated": round(1.0 / (dt * L), 4),
         }
-    plan.close()
-    pool.close()
+    if wl is not None:
+        wl.close()
     return res
+
+
+def run_e2e(wl, args):
+    """The same metric through the reference-facing host-buffer call: per layer,
+    H2D of q and the new rows from pinned host memory, append, attend, D2H of the
+    output and a wait (kvc_decode_host, launch_gqa_attention_cached_fp16's
+    semantics).  Head-sharded: this rank's inputs in, fused decode + exchange,
+    all heads out."""
+    torch = wl.torch
+    hq = wl.q.cpu().pin_memory()
+    hk = wl.kn.cpu().pin_memory()
+    hv = wl.vn.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+    steps = max(1, min(args.steps, args.e2e_steps))
+    sharded = wl.hsd is not None
+    if sharded:
+        hg = torch.empty((wl.L, wl.B, wl.H_full, wl.D), dtype=torch.float16).pin_memory()
+        qd, kd, vd = (torch.empty_like(wl.q[0]), torch.empty_like(wl.kn[0]),
+                      torch.empty_like(wl.vn[0]))
+        od = torch.empty((wl.B, wl.H_full, wl.D), dtype=torch.float16, device=wl.dev)
+    # the e2e step runs at the workload's current contexts (a fresh plan)
+    wl.pool.plan(wl.current_ctx(), wl.H, plan=wl.plan, stream=wl.stream)
+    s = wl.stream
+
+    def e2e_step():
+        for l in range(wl.L):
+            if not sharded:
+                wl.pool.decode_host(wl.plan, l, hq[l], hk[l], hv[l], ho[l], wl.bt, wl.scale,
+                                    stream=s)
+                continue
+            qd.copy_(hq[l], non_blocking=True)
+            kd.copy_(hk[l], non_blocking=True)
+            vd.copy_(hv[l], non_blocking=True)
+            res = wl.hsd.append_decode(wl.plan, l, qd, kd, vd,
+                                       od if wl.xchg == "nccl" else None, wl.bt, wl.scale,
+                                       stream=s)
+            hg[l].copy_(res, non_blocking=True)
+            s.synchronize()
+
+    for _ in range(min(2, args.warmup)):
+        e2e_step()
+    if wl.world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        e2e_step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / steps, wl.world, wl.dev)
+    job_bytes = _sum_over_ranks(float(sum(wl.step_bytes())), wl.world, wl.dev)
+    h2d = wl.L * wl.B * (wl.H * wl.D + 2 * wl.Hkv * wl.D) * 2
+    d2h = wl.L * wl.B * (wl.H_full if sharded else wl.H) * wl.D * 2
+    return {"value": round(job_bytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "steps": steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "call": ("kvc_decode_host (pinned host q/k_new/v_new/out, per layer, waits)"
+                     if not sharded else
+                     "HeadShardedDecode.append_decode (pinned H2D of this rank's q/k/v, "
+                     "fused decode + exchange, D2H of all heads, per layer, waits)")}
 
 
 # ---------------------------------------------------------------------------------
@@ -666,10 +902,11 @@ def run_offload(args, rank, world, local_rank):
     }
 
 
-# DRAM traffic per decode launch (dram__bytes_read.sum + dram__bytes_write.sum)
-# from the committed ncu captures; None until captured for a workload.
-# DRAM bytes (read + write) of one decode_persistent_kernel launch, from an ncu
-# capture of the same per-launch shape (profiles/decode_persistent_kernel_*.md).
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# decode_persistent_kernel launch of config 3, measured by
+#   ncu --set full --clock-control none -k regex:"decode_persistent|merge_splits" -s 8 -c 2 \
+#       -o prof python bench.py --layers 2 --steps 3 --warmup 3 --no-cpu-baseline --no-e2e --no-clocks
+# (a 2-layer subset with the same per-launch shape); None for other workloads.
 TRAFFIC_PER_LAUNCH = {
     "3": 566_632_960 + 7_981_824,
 }
@@ -1025,9 +1262,15 @@ def main():
     ap.add_argument("--one-rank-of", type=int, default=0,
                     help="profiling on one GPU: run rank 0's shard of an N-way KV-head split "
                          "with its head exchange connected to itself")
-    ap.add_argument("--grow", action="store_true",
-                    help="a real decode loop: contexts grow by one per step and the plan is "
-                         "rebuilt each step (no CUDA graph)")
+    ap.add_argument("--no-grow", action="store_true",
+                    help="skip the growing decode loop (contexts +1 per step, plan rebuilt every "
+                         "step); the headline is then the replayed fixed step")
+    ap.add_argument("--min-timed-s", type=float, default=1.0,
+                    help="repeat the timed pass of --steps steps until about this many seconds "
+                         "are timed (value = the median pass)")
+    ap.add_argument("--max-passes", type=int, default=40)
+    ap.add_argument("--no-variants", action="store_true",
+                    help="N > 1: skip the sequence-sharded and NCCL-transport lines")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every kernel from the host loop instead of replaying a CUDA graph")
     ap.add_argument("--xchg", choices=["p2p", "nccl"], default="p2p",

@@ -217,6 +217,32 @@ int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const vo
 // Split length (positions) for a batch: see kvc_host.cpp.
 int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
                         int device);
+// SM count of `device`; 148 when the query fails (its error is cleared).
+int device_sms(int device);
+// The split partition of a batch, shared by every planner (kvc_plan_decode and
+// kvc_decode_noalloc cut a batch identically): returns the split length C and
+// sets refine[i] (n_queries entries) to how many of query i's full splits are cut
+// into quarters.  ups = work units per split (KV heads x q-head chunks).
+int split_partition(int page_size, const int* ctxs, int n_queries, int ups, int device,
+                    int* refine);
+// The splits of query q (context ctx, split length C, `refine` of its last full
+// splits quartered), in position order: emit(int4{q, split, first, end}) for each.
+// An empty context has one empty split.  Returns the number of splits.
+template <typename Emit>
+int emit_splits(int q, int ctx, int C, int refine, Emit&& emit) {
+  const int base = ctx > 0 ? (ctx + C - 1) / C : 1;
+  const int full = ctx > 0 ? ctx / C : 0;
+  int k = 0;
+  for (int b = 0; b < base; ++b) {
+    const int tb = b * C, te = ctx < (b + 1) * C ? ctx : (b + 1) * C;
+    if (b >= full - refine && b < full) {
+      for (int j = 0; j < 4; ++j, ++k) emit(make_int4(q, k, tb + j * (C / 4), tb + (j + 1) * (C / 4)));
+    } else {
+      emit(make_int4(q, k++, tb, te < tb ? tb : te));
+    }
+  }
+  return k;
+}
 // Plan for q_len queries m = 0..q_len-1 of one sequence (block-table row 0)
 // whose context is min(kv_len, start_pos + m + 1) if causal, else kv_len
 // (attention.hip:75).

@@ -564,16 +564,69 @@ int split_tokens_model(int page_size, const int* ctx, int n_queries, int units_p
   return best;
 }
 
+int device_sms(int device) {
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();  // the query's error must not surface as a later launch failure
+    sms = 148;
+  }
+  return sms;
+}
+
 int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
                         int device) {
   const int forced = split_tokens_for(page_size);
   if (forced > 0) return round_split(forced, page_size);
-  int sms = 148;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
-    cudaGetLastError();
-    sms = 148;
+  return split_tokens_model(page_size, ctx, n_queries, units_per_split, device_sms(device));
+}
+
+// Tail refinement: with even contexts (nothing but full splits), a multi-wave
+// plan whose last wave would keep fewer than 60 % of the warps busy has that
+// many full splits (the queries' last ones, round-robin) cut into quarters, so
+// the end of the longest-first list is short units that every warp can take.
+// Measured on config 4 (4,096 full units on 1,184 warps): +7 %; ragged batches
+// already end in short splits and only pay the extra units (config 3: -4 % to
+// -9 %), so they are left alone.  KVC_TAIL_REFINE = n overrides the count.
+int split_partition(int page_size, const int* ctxs, int n_queries, int ups, int device,
+                    int* refine) {
+  const int C = choose_split_tokens(page_size, ctxs, n_queries, ups, device);
+  for (int i = 0; i < n_queries; ++i) refine[i] = 0;
+  static const int forced = [] {
+    const char* e = getenv("KVC_TAIL_REFINE");
+    return e ? std::max(0, atoi(e)) : -1;
+  }();
+  int n_refine = forced;
+  if (n_refine < 0) {
+    n_refine = 0;
+    const int64_t warps = static_cast<int64_t>(device_sms(device)) * kPersistWarps;
+    int64_t full_units = 0, partial_pos = 0;
+    for (int i = 0; i < n_queries; ++i) {
+      full_units += static_cast<int64_t>(std::max(0, ctxs[i]) / C) * ups;
+      partial_pos += static_cast<int64_t>(std::max(0, ctxs[i]) % C) * ups;
+    }
+    const int64_t r = full_units % warps;
+    if (full_units > warps && r > 0 && r < (warps * 6) / 10 &&
+        partial_pos * 20 < static_cast<int64_t>(C) * warps)
+      n_refine = static_cast<int>((r + ups - 1) / ups);
   }
-  return split_tokens_model(page_size, ctx, n_queries, units_per_split, sms);
+  const int q4 = C / 4;
+  if (n_refine > 0 && q4 >= page_size && q4 % page_size == 0) {
+    int left = n_refine;
+    for (int round = 0; left > 0; ++round) {
+      bool any = false;
+      for (int i = 0; i < n_queries && left > 0; ++i) {
+        const int full = std::max(0, ctxs[i]) / C;
+        if (round < full) {
+          refine[i]++;
+          left--;
+          any = true;
+        }
+      }
+      if (!any) break;
+    }
+  }
+  return C;
 }
 
 // Build the split list on the host.  ctx_of(i) / row_of(i) describe query i.
@@ -598,85 +651,23 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   }
   p->valid = false;
   p->built_from.clear();
-  const int C = choose_split_tokens(g.page_size, ctxs.data(), n_queries,
-                                    g.num_kv_heads * ((num_heads / g.num_kv_heads + 7) / 8),
-                                    device);
+  const int ups = g.num_kv_heads * ((num_heads / g.num_kv_heads + 7) / 8);
+  std::vector<int> refine(std::max(0, n_queries), 0);  // full splits to quarter, per query
+  const int C = split_partition(g.page_size, ctxs.data(), n_queries, ups, device, refine.data());
   p->items.clear();
   p->qinfo.clear();
   p->rows.clear();
   p->positions.clear();
   int slot = 0, max_ctx = 0, max_splits = 0;
-  // Tail refinement: with even contexts (nothing but full splits), a multi-wave
-  // plan whose last wave would keep fewer than 60 % of the warps busy has that
-  // many full splits (the queries' last ones, round-robin) cut into quarters, so
-  // the end of the longest-first list is short units that every warp can take.
-  // Measured on config 4 (4,096 full units on 1,184 warps): +7 %; ragged batches
-  // already end in short splits and only pay the extra units (config 3: -4 % to
-  // -9 %), so they are left alone.  KVC_TAIL_REFINE = n overrides the count.
-  const int ups = g.num_kv_heads * ((num_heads / g.num_kv_heads + 7) / 8);
-  std::vector<int> refine(std::max(0, n_queries), 0);  // full splits to quarter, per query
-  {
-    static const int forced = [] {
-      const char* e = getenv("KVC_TAIL_REFINE");
-      return e ? std::max(0, atoi(e)) : -1;
-    }();
-    int n_refine = forced;
-    if (n_refine < 0) {
-      n_refine = 0;
-      int sms = 148;
-      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
-        cudaGetLastError();
-        sms = 148;
-      }
-      const int64_t warps = static_cast<int64_t>(sms) * kPersistWarps;
-      int64_t full_units = 0, partial_pos = 0;
-      for (int i = 0; i < n_queries; ++i) {
-        full_units += static_cast<int64_t>(std::max(0, ctxs[i]) / C) * ups;
-        partial_pos += static_cast<int64_t>(std::max(0, ctxs[i]) % C) * ups;
-      }
-      const int64_t r = full_units % warps;
-      if (full_units > warps && r > 0 && r < (warps * 6) / 10 &&
-          partial_pos * 20 < static_cast<int64_t>(C) * warps)
-        n_refine = static_cast<int>((r + ups - 1) / ups);
-    }
-    const int q4 = C / 4;
-    if (n_refine > 0 && q4 >= g.page_size && q4 % g.page_size == 0) {
-      int left = n_refine;
-      for (int round = 0; left > 0; ++round) {
-        bool any = false;
-        for (int i = 0; i < n_queries && left > 0; ++i) {
-          const int full = std::max(0, ctxs[i]) / C;
-          if (round < full) {
-            refine[i]++;
-            left--;
-            any = true;
-          }
-        }
-        if (!any) break;
-      }
-    }
-  }
   for (int i = 0; i < n_queries; ++i) {
     const int ctx = ctxs[i];
     const int row = row_of(i);
     if (ctx < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
     if (row < 0) return set_error(KVC_ERR_INVALID_ARG, "block-table row must be non-negative.");
-    const int base = ctx > 0 ? (ctx + C - 1) / C : 1;
-    const int full = ctx / C;
-    const int ns = base + 3 * refine[i];
+    const int ns = emit_splits(i, ctx, C, refine[i], [&](const int4& it) { p->items.push_back(it); });
     p->qinfo.push_back(make_int4(row, ctx, slot, ns));
     p->rows.push_back(row);
     p->positions.push_back(ctx - 1);
-    int k = 0;
-    for (int b = 0; b < base; ++b) {
-      const int tb = b * C, te = std::min((b + 1) * C, ctx);
-      if (b >= full - refine[i] && b < full) {
-        for (int j = 0; j < 4; ++j, ++k)
-          p->items.push_back(make_int4(i, k, tb + j * (C / 4), tb + (j + 1) * (C / 4)));
-      } else {
-        p->items.push_back(make_int4(i, k++, tb, te));
-      }
-    }
     slot += ns;
     max_ctx = std::max(max_ctx, ctx);
     max_splits = std::max(max_splits, ns);
@@ -696,8 +687,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   // first (items are sorted by length); the kernel hands them out dynamically.
   // Each unit is a self-contained 3 x int4 record.
   {
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    const int sms = device_sms(device);
     const int group = num_heads / g.num_kv_heads;
     const int nhc = (group + 7) / 8;
     const int per_item = g.num_kv_heads * nhc;

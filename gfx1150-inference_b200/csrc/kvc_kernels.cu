@@ -261,9 +261,12 @@ __global__ void __launch_bounds__(256) fill_normal_kernel(const FillArgs a) {
 
 cudaError_t launch_fill_normal(const FillArgs& a, cudaStream_t s) {
   if (a.n_elems == 0) return cudaSuccess;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = 0;
+  }
+  const int sms = device_sms(dev);
   const size_t want = (a.n_elems + 255) / 256;
   const unsigned blocks = static_cast<unsigned>(want < static_cast<size_t>(sms) * 16 ? want : sms * 16);
   fill_normal_kernel<<<blocks, 256, 0, s>>>(a);
@@ -1373,14 +1376,15 @@ cudaError_t launch_decode(const DecodeArgs& a, int dtype, int layout, cudaStream
 // kvc_decode_noalloc: the decode for callers that cannot allocate device memory.
 //
 // Some hosts of this library (a runtime that owns every device allocation
-// through its own arena, a plugin that may not call cudaMalloc, code recorded
-// into a graph by a framework that forbids allocation) can still hand over
-// their KV pages, q and out, but cannot let the library allocate its plan and
-// split scratch.  This entry point keeps both in g_noalloc_scratch, a
+// through its own arena, a plugin that may not call cudaMalloc) can still hand
+// over their KV pages, q and out, but cannot let the library allocate its plan
+// and split scratch.  This entry point keeps both in g_noalloc_scratch, a
 // file-scope device array of kNoAllocScratchBytes that every GPU loading the
 // library holds until the process exits, and stages the plan in static host
 // buffers.  It calls no cudaMalloc / cudaFree or other allocating routine.
-// Requests that do not fit are rejected with KVC_ERR_INVALID_ARG.
+// Requests that do not fit are rejected with KVC_ERR_INVALID_ARG, and so is a
+// call on a stream that is being captured (the plan is uploaded from pageable
+// host memory, which a capture cannot record).
 // =====================================================================================
 
 
@@ -1390,18 +1394,17 @@ constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
 constexpr int kNoAllocMaxQueries = 4096;
 constexpr int kNoAllocMaxItems = 16384;
 constexpr int kNoAllocMaxUnits = 65536;
-constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-uint8_t* g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
 
 // Host staging (static, no heap).  Layout mirrors the device scratch.
 int4 h_items[kNoAllocMaxItems];
 int4 h_qinfo[kNoAllocMaxQueries];
 int4 h_recs[3 * kNoAllocMaxUnits];
 int32_t h_merge[kNoAllocMaxQueries];
+int h_refine[kNoAllocMaxQueries];
 int32_t h_order[kNoAllocMaxItems];
 int4 h_item_pairs[2 * kNoAllocMaxItems];
 
@@ -1437,38 +1440,45 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   if ((reinterpret_cast<uintptr_t>(d_q) | reinterpret_cast<uintptr_t>(d_out)) & 3u)
     return set_error(KVC_ERR_INVALID_ARG, "q and out must be 4-byte aligned.");
 
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Before any other CUDA call: a capturing stream is refused without touching it
+  // (the capture stays valid).
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &cap);
+  if (e != cudaSuccess) return cuda_error(e, "cudaStreamIsCapturing");
+  if (cap != cudaStreamCaptureStatusNone)
+    return set_error(KVC_ERR_INVALID_ARG,
+                     "kvc_decode_noalloc cannot run on a stream that is being captured: its plan "
+                     "is uploaded from pageable host memory.");
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return set_error(KVC_ERR_INVALID_ARG, "device index %d is beyond kvc_decode_noalloc's table.", dev);
-  // Set-up, once per device with that device current: the device address of the
-  // scratch array (its host-side name is only a stand-in, not a device pointer).
-  if (!g_noalloc_dev_ptr[dev]) {
-    void* p = nullptr;
-    if ((e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) != cudaSuccess)
-      return cuda_error(e, "cudaGetSymbolAddress(noalloc scratch)");
-    g_noalloc_dev_ptr[dev] = static_cast<uint8_t*>(p);
-  }
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  // The device address of the scratch array on the current device (its host-side
+  // name is only a stand-in, not a device pointer).  Looked up on every call: the
+  // lookup allocates nothing, and a call after cudaDeviceReset finds the array at
+  // its new address.
+  void* scratch = nullptr;
+  if ((e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch)) != cudaSuccess)
+    return cuda_error(e, "cudaGetSymbolAddress(noalloc scratch)");
 
-  // ---- split list (the same partition as kvc_plan_decode) ----
-  const int C = choose_split_tokens(page_size, h_ctx_lens, n_queries,
-                                    num_kv_heads * ((num_heads / num_kv_heads + 7) / 8), dev);
-  int n_items = 0, slot = 0, max_ctx = 0, max_splits = 0;
+  // ---- split list: the same partition as kvc_plan_decode ----
+  for (int i = 0; i < n_queries; ++i) {
+    if (h_ctx_lens[i] < 0)
+      return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
+    if (static_cast<int64_t>(h_ctx_lens[i]) > static_cast<int64_t>(bt_stride) * page_size)
+      return set_error(KVC_ERR_OUT_OF_RANGE, "a context length exceeds the block-table width.");
+  }
+  const int C = split_partition(page_size, h_ctx_lens, n_queries,
+                                num_kv_heads * ((num_heads / num_kv_heads + 7) / 8), dev, h_refine);
+  int n_items = 0, slot = 0, max_splits = 0;
   for (int i = 0; i < n_queries; ++i) {
     const int ctx = h_ctx_lens[i];
-    if (ctx < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
-    if (static_cast<int64_t>(ctx) > static_cast<int64_t>(bt_stride) * page_size)
-      return set_error(KVC_ERR_OUT_OF_RANGE, "a context length exceeds the block-table width.");
-    const int ns = ctx > 0 ? (ctx + C - 1) / C : 1;
-    if (n_items + ns > kNoAllocMaxItems)
+    const int base = ctx > 0 ? (ctx + C - 1) / C : 1;
+    if (n_items + base + 3 * h_refine[i] > kNoAllocMaxItems)
       return set_error(KVC_ERR_INVALID_ARG, "kvc_decode_noalloc accepts at most %d splits.",
                        kNoAllocMaxItems);
+    const int ns = emit_splits(i, ctx, C, h_refine[i], [&](const int4& it) { h_items[n_items++] = it; });
     h_qinfo[i] = make_int4(i, ctx, slot, ns);
-    for (int k = 0; k < ns; ++k)
-      h_items[n_items++] = make_int4(i, k, k * C, std::min((k + 1) * C, ctx));
     slot += ns;
-    max_ctx = std::max(max_ctx, ctx);
     max_splits = std::max(max_splits, ns);
   }
   for (int k = 0; k < n_items; ++k) h_order[k] = k;
@@ -1491,8 +1501,7 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   const size_t off_items = 256;
   const size_t off_qinfo = align256(off_items + sizeof(int4) * 2 * n_items);
   const size_t off_recs = align256(off_qinfo + sizeof(int4) * n_queries);
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sms(dev);
   const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
   const size_t off_merge = align256(off_recs + sizeof(int4) * 3 * n_units);
   const size_t plan_bytes = align256(off_merge + sizeof(int32_t) * n_queries);
@@ -1524,8 +1533,7 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   }
 
   // ---- upload (pageable host source: the call returns once it is staged) ----
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* base = g_noalloc_dev_ptr[dev];
+  uint8_t* base = static_cast<uint8_t*>(scratch);
   // the unit counter starts at zero (this call's merge kernel re-arms it too)
   if ((e = cudaMemsetAsync(base + off_queue, 0, 256, s)))
     return cuda_error(e, "kvc_decode_noalloc counter reset");
@@ -1570,7 +1578,6 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   a.page_size = page_size;
   a.num_pages = num_pages;
   a.scale_log2 = scale * kLog2e;
-  (void)max_ctx;
   if ((e = launch_decode(a, dtype, kLayoutCore, s)) != cudaSuccess)
     return cuda_error(e, "kvc_decode_noalloc kernels");
   return KVC_OK;

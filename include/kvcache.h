@@ -235,22 +235,23 @@ KVC_API int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int layer,
 
 /* No counterpart in the reference.  kvc_decode for callers that cannot allocate
  * device memory (runtimes that own every device allocation through their own
- * arena, plugins that may not call cudaMalloc, code recorded by frameworks that
- * forbid allocation).  The caller passes one layer's K and V pages (the pool's
- * layout, e.g. kvc_pool_info's base + layer * bytes_per_layer), int32 block
- * tables (query i uses row i), HOST context lengths, q and out; the plan and the
- * split partials live in a fixed 16 MiB device array inside the library that
- * every GPU loading it holds until the process exits.  No cudaMalloc / cudaFree
- * or other allocating routine is called.  fp16/bf16 pages, head_dim in
- * {32,64,96,128,160,192,256}, page_size a multiple of 16; at most 4096 queries,
- * 16384 splits and 65536 work units, and the plan + partials must fit 16 MiB:
- * larger requests fail with KVC_ERR_INVALID_ARG.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress); make that first
- * call before any stream capture.  All calls on a device share its array, and
- * each call overwrites it, so calls whose kernels overlap on that GPU (for
- * example on two streams) race: serialise them on one stream.  The plan is
- * staged through pageable host memory, so a call first waits for the work
- * already queued on its stream. */
+ * arena, plugins that may not call cudaMalloc).  The caller passes one layer's K
+ * and V pages (the pool's layout, e.g. kvc_pool_info's base + layer *
+ * bytes_per_layer), int32 block tables (query i uses row i), HOST context
+ * lengths, q and out; the plan and the split partials live in a fixed 16 MiB
+ * device array inside the library that every GPU loading it holds until the
+ * process exits.  No cudaMalloc / cudaFree or other allocating routine is called.
+ * fp16/bf16 pages, head_dim in {32,64,96,128,160,192,256}, page_size a multiple
+ * of 16; at most 4096 queries, 16384 splits and 65536 work units, and the plan +
+ * partials must fit 16 MiB: larger requests fail with KVC_ERR_INVALID_ARG.  The
+ * split partition is kvc_plan_decode's for the same batch.  Every call looks up
+ * the array's device address on the current device (cudaGetSymbolAddress), so a
+ * call after cudaDeviceReset uses the array's new address.  All calls on a
+ * device share its array, and each call overwrites it, so calls whose kernels
+ * overlap on that GPU (for example on two streams) race: serialise them on one
+ * stream.  The plan is staged through pageable host memory, so a call first
+ * waits for the work already queued on its stream, and a call on a stream that
+ * is being captured returns KVC_ERR_INVALID_ARG without enqueuing anything. */
 KVC_API int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, int num_pages,
                                int page_size, int num_kv_heads, int head_dim, int dtype,
                                const int32_t* d_block_tables, int bt_stride,
@@ -303,7 +304,7 @@ KVC_API int kvc_host_free(void* ptr);
  * (num_layers, max_seq_len, num_kv_heads, head_dim) (src/kv_cache.py:97, :133-135
  * and the mmap arrays of :100-132).  The caller keeps ownership of h_k / h_v.
  * When the memory is neither pinned nor registrable, copies go through pinned
- * bounce buffers. */
+ * bounce buffers.  device < 0 selects the calling thread's current device. */
 KVC_API int kvc_offload_create(void* h_k, void* h_v, int num_layers, int max_seq_len,
                        int num_kv_heads, int head_dim, int dtype, int flags, int device,
                        kvc_offload_t** out);
@@ -311,11 +312,14 @@ KVC_API int kvc_offload_destroy(kvc_offload_t* off);
 
 /* Offload-mode attend, the replacement of KVCacheManager.attend's offload branch
  * (src/kv_cache.py:219-239) plus launch_gqa_attention_fp16 (attention.hip:228-284):
- * writes the q_len new rows into the host pools at (layer_idx, start_pos), makes
- * rows [0, start_pos+q_len) of the layer resident on the GPU (reusing the copy
- * prefetched during the previous call when it is still valid), attends, copies
- * h_Out back, and starts prefetching the next layer.  Results are bit-identical
- * to the GPU-resident pool's for the same inputs. */
+ * writes the q_len new rows into the host pools at (layer_idx, start_pos) (or,
+ * when h_K_new and h_V_new are both null, takes them as written there already,
+ * which is what KVCacheManager's own host append does before it calls
+ * gqa_attention), makes rows [0, start_pos+q_len) of the layer resident on the
+ * GPU (reusing the copy prefetched during the previous call for the rows below
+ * start_pos, which are the cached history), attends, copies h_Out back, and
+ * starts prefetching the next layer.  Results are bit-identical to the
+ * GPU-resident pool's for the same inputs. */
 KVC_API int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const void* h_K_new,
                        const void* h_V_new, void* h_Out, int layer_idx, int q_len,
                        int start_pos, int num_heads, float scale, int causal);
