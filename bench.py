@@ -808,13 +808,16 @@ def run_e2e(wl, args):
 # offload arm (benchmark config 5): KV in host memory, streamed per layer
 # ---------------------------------------------------------------------------------
 def run_offload(args, rank, world, local_rank):
-    """--offload-kv-cpu decode steps through the drop-in KVCacheManager: every
-    layer's cached K/V is streamed from (registered) host memory to the GPU on a
-    copy stream while the previous layer attends.  Each attend call returns
+    """--offload-kv-cpu decode steps the way the reference's KVCacheManager runs
+    them in its cpu mode (src/kv_cache.py:133-135, :219-239): K and V live in two
+    host arrays (layers, max_seq_len, Hkv, D); per layer the new row is written
+    there, then ``matmul_module.gqa_attention`` gets the layer's views, which the
+    drop-in serves from its streaming engine (the layer's rows are copied to the
+    GPU on a copy stream while the previous layer attends).  Each call returns
     after its output is on the host, so host wall time is device-complete time."""
     import torch
 
-    from kv_cache import KVCacheManager
+    import matmul_module
 
     torch.cuda.set_device(local_rank)
     cfg = dict(CONFIGS[args.config])
@@ -831,11 +834,12 @@ def run_offload(args, rank, world, local_rank):
         raise SystemExit(f"offload replicas need {need / 1e9:.1f} GB of host RAM for {world} ranks; "
                          f"this node has {ram / 1e9:.1f} GB (run fewer ranks or --layers)")
     t0 = time.perf_counter()
-    kv = KVCacheManager(L, S, Hkv, D, offload_to_cpu=True, max_kv_bytes=1 << 50,
-                        offload_mirror_bytes=int(args.mirror_gb * 1e9))
+    matmul_module.set_offload_mirror_bytes(int(args.mirror_gb * 1e9))
+    k_host = np.empty((L, S, Hkv, D), dtype=np.float16)   # kv_cache.py:133-135
+    v_host = np.empty((L, S, Hkv, D), dtype=np.float16)
     rng = np.random.default_rng(cfg["seed"])
     block = rng.standard_normal(1 << 23, dtype=np.float32).astype(np.float16)
-    for arr, shift in ((kv._k_host, 0), (kv._v_host, 12345)):
+    for arr, shift in ((k_host, 0), (v_host, 12345)):
         flat = arr.reshape(-1)
         step = block.size
         for o in range(0, flat.size, step):
@@ -850,21 +854,25 @@ def run_offload(args, rank, world, local_rank):
 
     def step():
         for l in range(L):
-            kv.attend(q[l], kn[l], vn[l], out, layer_idx=l, q_len=1, start_pos=cached,
-                      num_heads=H, scale=scale, causal=True)
+            # KVCacheManager.attend, cpu mode: host append, then the layer's views
+            k_host[l][cached:S] = kn[l]
+            v_host[l][cached:S] = vn[l]
+            matmul_module.gqa_attention(q[l], k_host[l], v_host[l], out, 1, S, H, Hkv, D,
+                                        cached, scale, True)
 
     t1 = time.perf_counter()
     for _ in range(args.warmup):
         step()
-    first = kv.offload_stats()
+    first = matmul_module.offload_stats(k_host)
+    assert first["engines"] == 1, "the host arrays were not served by the streaming engine"
     warm_s = time.perf_counter() - t1
     torch.cuda.synchronize()
     ts = time.perf_counter()
     for _ in range(args.steps):
         step()
     elapsed = time.perf_counter() - ts
-    st = kv.offload_stats()
-    kv.close()
+    st = matmul_module.offload_stats(k_host)
+    del k_host, v_host  # releases the engine (and unregisters the host arrays)
     kv_bytes = L * S * Hkv * D * 2 * 2
     h2d = st["h2d_bytes"] - first["h2d_bytes"]
     h2d_ms = st["h2d_ms"] - first["h2d_ms"]
@@ -888,7 +896,9 @@ def run_offload(args, rank, world, local_rank):
                                + (f" [subset: {L} layers]" if args.layers else ""),
                    "layers": L, "q_heads": H, "kv_heads": Hkv, "head_dim": D, "batch": 1,
                    "cached_len": cached, "host_kv_gb": round(kv_bytes / 1e9, 2),
-                   "timing": "host wall clock; every attend call waits for its output"},
+                   "timing": "host wall clock; every attend call waits for its output",
+                   "call": "matmul_module.gqa_attention on the layer views of (layers, S, Hkv, D) "
+                           "host arrays after the host append (KVCacheManager's cpu mode)"},
         "hbm_mirror": {"budget_gb": args.mirror_gb, "layers": st["mirror_layers"],
                        "uploaded_gb_per_step": round((st["mirror_bytes"] - first["mirror_bytes"])
                                                      / args.steps / 1e9, 6)},

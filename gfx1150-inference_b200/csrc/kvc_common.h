@@ -29,6 +29,19 @@ struct HostBuf {
 
 int set_error(int code, const char* fmt, ...);
 int cuda_error(cudaError_t e, const char* what);
+
+// ---- host-side waits and fault injection ----
+// Every wait of the host for the library's own GPU work polls (cudaStreamQuery /
+// cudaEventQuery) against a wall-clock limit (kvc_set_host_wait_limit, 60 s by
+// default) and returns KVC_ERR_TIMEOUT with `what` in the message when it runs out.
+int wait_stream(cudaStream_t s, const char* what);
+int wait_event(cudaEvent_t e, const char* what);
+// kvc_test_inject_failure: true when this call at `site` (KVC_FAULT_*) is to fail.
+bool injected_failure(int site);
+// cudaMalloc / cudaHostAlloc / cudaHostRegister that honour kvc_test_inject_failure.
+cudaError_t dev_alloc(void** p, size_t n);
+cudaError_t host_alloc(void** p, size_t n, unsigned flags);
+cudaError_t host_register(void* p, size_t n);
 // cudaSetDevice with the library's status convention.
 int use_device(int device);
 int check_device_error(const char* what);

@@ -13,10 +13,12 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <mutex>
 #include <queue>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "kvcache.h"
@@ -47,6 +49,78 @@ int cuda_error(cudaError_t e, const char* what) {
 }
 
 void clear_error() { g_last_error.clear(); }
+
+// ---- bounded host waits ------------------------------------------------------
+std::atomic<double> g_wait_limit_s{60.0};
+
+namespace {
+template <typename Query>
+int bounded_wait(Query query, const char* what) {
+  const double limit = g_wait_limit_s.load();
+  if (injected_failure(KVC_FAULT_WAIT))
+    return set_error(KVC_ERR_TIMEOUT, "%s did not complete within %.3f s (injected)", what, limit);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (unsigned i = 0;; ++i) {
+    const cudaError_t e = query();
+    if (e == cudaSuccess) return KVC_OK;
+    if (e != cudaErrorNotReady) return cuda_error(e, what);
+    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (dt > limit)
+      return set_error(KVC_ERR_TIMEOUT, "%s did not complete within %.3f s", what, limit);
+    // spin first (most waits end within microseconds), then yield, then sleep
+    if (i >= 4096) {
+      std::this_thread::sleep_for(std::chrono::microseconds(dt > 0.01 ? 200 : 20));
+    } else if (i >= 256) {
+      std::this_thread::yield();
+    }
+  }
+}
+}  // namespace
+
+int wait_stream(cudaStream_t s, const char* what) {
+  return bounded_wait([s] { return cudaStreamQuery(s); }, what);
+}
+
+int wait_event(cudaEvent_t ev, const char* what) {
+  return bounded_wait([ev] { return cudaEventQuery(ev); }, what);
+}
+
+// ---- host-side fault injection (kvc_test_inject_failure) ----------------------
+namespace {
+constexpr int kFaultSites = 5;
+std::mutex g_fault_mu;
+int g_fault_skip[kFaultSites] = {};
+int g_fault_count[kFaultSites] = {};
+std::atomic<int> g_fault_armed{0};
+}  // namespace
+
+bool injected_failure(int site) {
+  if (g_fault_armed.load(std::memory_order_relaxed) == 0 || site <= 0 || site >= kFaultSites)
+    return false;
+  std::lock_guard<std::mutex> lock(g_fault_mu);
+  if (g_fault_count[site] <= 0) return false;
+  if (g_fault_skip[site] > 0) {
+    g_fault_skip[site]--;
+    return false;
+  }
+  if (--g_fault_count[site] == 0) g_fault_armed.fetch_sub(1);
+  return true;
+}
+
+cudaError_t dev_alloc(void** p, size_t n) {
+  if (injected_failure(KVC_FAULT_DEVICE_ALLOC)) return cudaErrorMemoryAllocation;
+  return cudaMalloc(p, n);
+}
+
+cudaError_t host_alloc(void** p, size_t n, unsigned flags) {
+  if (injected_failure(KVC_FAULT_HOST_ALLOC)) return cudaErrorMemoryAllocation;
+  return cudaHostAlloc(p, n, flags);
+}
+
+cudaError_t host_register(void* p, size_t n) {
+  if (injected_failure(KVC_FAULT_HOST_REGISTER)) return cudaErrorNotPermitted;
+  return cudaHostRegister(p, n, cudaHostRegisterDefault);
+}
 
 std::atomic<uint32_t> g_device_errors{0};
 
@@ -90,7 +164,7 @@ cudaError_t error_mirror(ErrMirror** out) {
   ErrMirror& m = g_mirror[dev];
   if (!m.host) {
     void* h = nullptr;
-    if ((e = cudaMallocHost(&h, 64)) != cudaSuccess) return e;
+    if ((e = host_alloc(&h, 64, cudaHostAllocDefault)) != cudaSuccess) return e;
     if ((e = device_error_address(&m.dev)) != cudaSuccess) {
       cudaFreeHost(h);
       return e;
@@ -113,7 +187,7 @@ int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t byte
   // sees at least every error raised before its own kernels finished.
   if ((e = cudaMemcpyAsync(m->host, m->dev, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s)))
     return cuda_error(e, "cudaMemcpyAsync(error word)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  if (const int rc = wait_stream(s, what)) return rc;
   if ((reinterpret_cast<volatile uint32_t*>(m->host)[0]) == KVC_DEVERR_NONE) return KVC_OK;
   return check_device_error(what);  // rare: read, clear and report
 }
@@ -202,7 +276,7 @@ cudaError_t DevBuf::ensure(size_t bytes) {
   if (ptr) cudaFree(ptr);
   ptr = nullptr;
   cap = 0;
-  cudaError_t e = cudaMalloc(&ptr, n);
+  cudaError_t e = dev_alloc(&ptr, n);
   if (e != cudaSuccess) {
     ptr = nullptr;
     return e;
@@ -223,7 +297,7 @@ cudaError_t HostBuf::ensure(size_t bytes) {
   if (ptr) cudaFreeHost(ptr);
   ptr = nullptr;
   cap = 0;
-  cudaError_t e = cudaMallocHost(&ptr, n);
+  cudaError_t e = host_alloc(&ptr, n, cudaHostAllocDefault);
   if (e != cudaSuccess) {
     ptr = nullptr;
     return e;
@@ -285,12 +359,12 @@ int pool_alloc(kvc_pool* p, const PoolGeom& g, int device) {
     if (p->v) cudaFree(p->v);
     p->k = p->v = nullptr;
     p->cap_bytes = 0;
-    e = cudaMalloc(&p->k, bytes);
+    e = dev_alloc(reinterpret_cast<void**>(&p->k), bytes);
     if (e != cudaSuccess) {
       p->k = nullptr;
       return cuda_error(e, "cudaMalloc(K pool)");
     }
-    e = cudaMalloc(&p->v, bytes);
+    e = dev_alloc(reinterpret_cast<void**>(&p->v), bytes);
     if (e != cudaSuccess) {
       cudaFree(p->k);
       p->k = p->v = nullptr;
@@ -316,6 +390,25 @@ void pool_release(kvc_pool* p) {
 }  // namespace kvc
 
 extern "C" int kvc_version(void) { return 1; }
+
+extern "C" int kvc_set_host_wait_limit(double seconds) {
+  if (!(seconds > 0.0) || seconds > 86400.0)
+    return set_error(KVC_ERR_INVALID_ARG, "the host wait limit must be in (0, 86400] seconds.");
+  kvc::g_wait_limit_s.store(seconds);
+  return KVC_OK;
+}
+
+extern "C" int kvc_test_inject_failure(int site, int skip, int count) {
+  if (site <= 0 || site >= kvc::kFaultSites || skip < 0 || count < 0)
+    return set_error(KVC_ERR_INVALID_ARG, "unknown fault site %d or negative counts.", site);
+  std::lock_guard<std::mutex> lock(kvc::g_fault_mu);
+  const bool was = kvc::g_fault_count[site] > 0, now = count > 0;
+  kvc::g_fault_skip[site] = skip;
+  kvc::g_fault_count[site] = count;
+  if (now && !was) kvc::g_fault_armed.fetch_add(1);
+  if (!now && was) kvc::g_fault_armed.fetch_sub(1);
+  return KVC_OK;
+}
 
 extern "C" const char* kvc_last_error(void) { return g_last_error.c_str(); }
 
@@ -759,7 +852,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   const size_t blob_b = o_queue + 256;
   if ((e = p->d_blob.ensure(blob_b))) return cuda_error(e, "plan buffers");
   if (p->upload_done) {  // the staging is free once the previous upload has landed
-    if ((e = cudaEventSynchronize(p->upload_done))) return cuda_error(e, "plan upload wait");
+    if (const int rc = wait_event(p->upload_done, "plan upload")) return rc;
   } else if ((e = cudaEventCreateWithFlags(&p->upload_done, cudaEventDisableTiming))) {
     return cuda_error(e, "cudaEventCreate");
   }
@@ -1203,7 +1296,7 @@ int ensure_identity_table(DevBuf* bt, int* bt_len, int pages, cudaStream_t s) {
   for (int i = 0; i < pages; ++i) ids[i] = i;
   if ((e = cudaMemcpyAsync(bt->ptr, ids.data(), sizeof(int32_t) * pages, cudaMemcpyHostToDevice, s)))
     return cuda_error(e, "cudaMemcpy(block table)");
-  if ((e = cudaStreamSynchronize(s))) return cuda_error(e, "cudaStreamSynchronize");
+  if (const int rc = wait_stream(s, "block table upload")) return rc;
   *bt_len = pages;
   return KVC_OK;
 }
@@ -1227,7 +1320,10 @@ int cache_init_locked(Singleton& S, int num_layers, int max_seq_len, int num_kv_
     S.live = false;
     return rc;
   }
-  if ((rc = ensure_identity_table(&S.bt, &S.bt_len, pages, S.stream))) return rc;
+  if ((rc = ensure_identity_table(&S.bt, &S.bt_len, pages, S.stream))) {
+    S.live = false;
+    return rc;
+  }
   S.max_seq_len = max_seq_len;
   S.live = true;
   return KVC_OK;
@@ -1585,7 +1681,7 @@ extern "C" int kvc_host_alloc(size_t bytes, void** out) {
   if (!out) return set_error(KVC_ERR_INVALID_ARG, "out must not be null.");
   *out = nullptr;
   if (bytes == 0) return set_error(KVC_ERR_INVALID_ARG, "bytes must be positive.");
-  cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocPortable);
+  cudaError_t e = host_alloc(out, bytes, cudaHostAllocPortable);
   if (e != cudaSuccess) {
     *out = nullptr;
     return cuda_error(e, "cudaHostAlloc");

@@ -79,15 +79,22 @@ struct kvc_offload {
 
 namespace {
 
-void harvest(kvc_offload* o, bool wait) {
+// Add up the copy-engine time of completed copies; wait (bounded) for the ones in
+// flight when `wait`.
+int harvest(kvc_offload* o, bool wait) {
   while (o->t_tail != o->t_head) {
     const int i = o->t_tail % kTimingRing;
-    if (wait) cudaEventSynchronize(o->t_stop[i]);
-    if (cudaEventQuery(o->t_stop[i]) != cudaSuccess) break;
+    if (wait) {
+      if (const int rc = wait_event(o->t_stop[i], "offload copy")) return rc;
+    } else if (cudaEventQuery(o->t_stop[i]) != cudaSuccess) {
+      cudaGetLastError();  // cudaErrorNotReady is not an error of the next call
+      break;
+    }
     float ms = 0.f;
     if (cudaEventElapsedTime(&ms, o->t_start[i], o->t_stop[i]) == cudaSuccess) o->h2d_ms += ms;
     o->t_tail++;
   }
+  return KVC_OK;
 }
 
 // H2D of rows [r0, r1) of `layer` into bounce `bi`, on the copy stream.
@@ -98,7 +105,9 @@ int copy_rows(kvc_offload* o, int bi, int layer, int r0, int r1) {
   const size_t n = static_cast<size_t>(r1 - r0) * o->row_bytes;
   const uint8_t* hk = o->h_k + static_cast<size_t>(layer) * o->layer_bytes + off;
   const uint8_t* hv = o->h_v + static_cast<size_t>(layer) * o->layer_bytes + off;
-  if (o->t_head - o->t_tail >= kTimingRing) harvest(o, true);
+  if (o->t_head - o->t_tail >= kTimingRing) {
+    if (const int rc = harvest(o, true)) return rc;
+  }
   const int ti = o->t_head % kTimingRing;
   cudaError_t e;
   if ((e = cudaEventRecord(o->t_start[ti], o->copy)) ||
@@ -126,10 +135,13 @@ int start_fill(kvc_offload* o, int bi, int layer, int rows) {
   return KVC_OK;
 }
 
-void destroy_locked(kvc_offload* o) {
+// Waits (bounded) for the engine's streams, then frees everything.  When a wait
+// runs out nothing is freed (the GPU may still use it) and the status says so.
+int destroy_locked(kvc_offload* o) {
   cudaSetDevice(o->device);
-  if (o->copy) cudaStreamSynchronize(o->copy);
-  if (o->compute) cudaStreamSynchronize(o->compute);
+  int rc = KVC_OK;
+  if (o->copy && (rc = wait_stream(o->copy, "offload copy stream"))) return rc;
+  if (o->compute && (rc = wait_stream(o->compute, "offload compute stream"))) return rc;
   for (auto& B : o->b) {
     B.k.release();
     B.v.release();
@@ -160,16 +172,13 @@ void destroy_locked(kvc_offload* o) {
   if (o->copy) cudaStreamDestroy(o->copy);
   if (o->compute) cudaStreamDestroy(o->compute);
   o->copy = o->compute = nullptr;
+  return KVC_OK;
 }
 
 }  // namespace
 
 namespace {
 
-// The next layer after `layer` that is streamed (not mirrored), cyclically, and
-// how many of its rows are final now: within a step the prefix [0, start_pos);
-// a layer of the next step [0, total).  Prefetch it into bounce `bi` unless a
-// bounce already holds it.
 // The query reaches d_q through the input staging kernel; the output goes where
 // stage_host_call puts it (the host buffer itself when page-locked).
 int stage_q(kvc_offload* o, const void* h_Q, uint8_t* d_q, size_t qb, void* h_Out, cudaStream_t s,
@@ -180,6 +189,10 @@ int stage_q(kvc_offload* o, const void* h_Q, uint8_t* d_q, size_t qb, void* h_Ou
   return stage_host_call(o->io_host, h_in, in_b, d_in, h_Out, qb, s, st);
 }
 
+// The next layer after `layer` that is streamed (not mirrored), cyclically, and
+// how many of its rows are final now: within a step the prefix [0, start_pos);
+// a layer of the next step [0, total).  Prefetch it into bounce `bi` unless a
+// bounce already holds it.
 int prefetch_next(kvc_offload* o, int layer, int start_pos, int total, int bi) {
   if (o->n_mirror >= o->num_layers) return KVC_OK;  // nothing is streamed
   // mirrored layers are [0, n_mirror): the next streamed one in this step, or the
@@ -256,8 +269,10 @@ extern "C" int kvc_offload_create(void* h_k, void* h_v, int num_layers, int max_
   if (rc) return rc;
   if (num_layers <= 0 || max_seq_len <= 0)
     return set_error(KVC_ERR_INVALID_ARG, "KV cache dimensions must all be positive.");
-  cudaError_t e = cudaSetDevice(device);
-  if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+  cudaError_t e;
+  if (device < 0 && (e = cudaGetDevice(&device)) != cudaSuccess)
+    return cuda_error(e, "cudaGetDevice");
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_error(e, "cudaSetDevice");
 
   kvc_offload* o = new kvc_offload();
   o->device = device;
@@ -274,15 +289,14 @@ extern "C" int kvc_offload_create(void* h_k, void* h_v, int num_layers, int max_
   const size_t host_bytes = o->layer_bytes * num_layers;
 
   auto fail = [&](int code) {
-    destroy_locked(o);
-    delete o;
+    if (destroy_locked(o) == KVC_OK) delete o;  // nothing of it is queued yet
     return code;
   };
   if (flags & KVC_OFFLOAD_PINNED) {
     o->dma_ok = true;
   } else if (flags & KVC_OFFLOAD_REGISTER) {
-    if (cudaHostRegister(h_k, host_bytes, cudaHostRegisterDefault) == cudaSuccess) {
-      if (cudaHostRegister(h_v, host_bytes, cudaHostRegisterDefault) == cudaSuccess) {
+    if (host_register(h_k, host_bytes) == cudaSuccess) {
+      if (host_register(h_v, host_bytes) == cudaSuccess) {
         o->registered = true;
         o->dma_ok = true;
       } else {
@@ -322,7 +336,7 @@ extern "C" int kvc_offload_destroy(kvc_offload_t* off) {
   if (!off) return KVC_OK;
   {
     std::lock_guard<std::mutex> lock(off->mu);
-    destroy_locked(off);
+    if (const int rc = destroy_locked(off)) return rc;  // still in use: kept, call again
   }
   delete off;
   return KVC_OK;
@@ -345,7 +359,7 @@ extern "C" int kvc_offload_set_mirror(kvc_offload_t* off, size_t budget_bytes, i
   std::lock_guard<std::mutex> lock(o->mu);
   cudaError_t e = cudaSetDevice(o->device);
   if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
-  if ((e = cudaStreamSynchronize(o->compute))) return cuda_error(e, "cudaStreamSynchronize");
+  if (const int rc = wait_stream(o->compute, "offload compute stream")) return rc;
   pool_release(&o->mirror);
   o->n_mirror = 0;
   o->mirror_rows.clear();
@@ -380,7 +394,7 @@ extern "C" int kvc_offload_stats(const kvc_offload_t* off, double* h2d_bytes, do
   kvc_offload* o = const_cast<kvc_offload*>(off);
   std::lock_guard<std::mutex> lock(o->mu);
   if (const int rc_dev = use_device(o->device)) return rc_dev;
-  harvest(o, true);
+  if (const int rc = harvest(o, true)) return rc;
   if (h2d_bytes) *h2d_bytes = o->h2d_bytes;
   if (h2d_ms) *h2d_ms = o->h2d_ms;
   if (prefetch_hits) *prefetch_hits = o->hits;
@@ -402,21 +416,24 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
   if (num_heads <= 0 || num_heads % o->num_kv_heads != 0)
     return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
   if (q_len == 0) return KVC_OK;
-  if (!h_Q || !h_K_new || !h_V_new || !h_Out)
+  if (!h_Q || !h_Out || (!h_K_new) != (!h_V_new))
     return set_error(KVC_ERR_INVALID_ARG, "host buffers must not be null.");
   const int total = static_cast<int>(total64);
   cudaError_t e = cudaSetDevice(o->device);
   if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
   o->calls++;
-  harvest(o, false);
+  harvest(o, false);  // never waits
 
-  // 1. host append (kv_cache.py:222-225).  A prefetch of this layer that covered
+  // 1. host append (kv_cache.py:222-225), unless the caller has written the rows
+  //    already (null h_K_new / h_V_new).  A prefetch of this layer that covered
   //    rows >= start_pos is stale from start_pos on.
-  const size_t lay = static_cast<size_t>(layer_idx) * o->layer_bytes;
-  const size_t off0 = static_cast<size_t>(start_pos) * o->row_bytes;
-  const size_t nb = static_cast<size_t>(q_len) * o->row_bytes;
-  memcpy(o->h_k + lay + off0, h_K_new, nb);
-  memcpy(o->h_v + lay + off0, h_V_new, nb);
+  if (h_K_new) {
+    const size_t lay = static_cast<size_t>(layer_idx) * o->layer_bytes;
+    const size_t off0 = static_cast<size_t>(start_pos) * o->row_bytes;
+    const size_t nb = static_cast<size_t>(q_len) * o->row_bytes;
+    memcpy(o->h_k + lay + off0, h_K_new, nb);
+    memcpy(o->h_v + lay + off0, h_V_new, nb);
+  }
   for (auto& B : o->b)
     if (B.layer == layer_idx && B.rows > start_pos) B.rows = start_pos;
 

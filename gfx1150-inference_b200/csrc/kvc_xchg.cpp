@@ -53,7 +53,7 @@ extern "C" int kvc_xchg_create(int device, int rank, int world, size_t slot_byte
   x->slot_stride = (slot_bytes + 255) & ~static_cast<size_t>(255);
   x->n_slots = n_slots;
   const size_t bytes = kXchgSlotsOff + x->slot_stride * static_cast<size_t>(n_slots);
-  if ((e = cudaMalloc(&x->base, bytes)) != cudaSuccess) {
+  if ((e = dev_alloc(reinterpret_cast<void**>(&x->base), bytes)) != cudaSuccess) {
     delete x;
     return cuda_error(e, "cudaMalloc(exchange buffer)");
   }

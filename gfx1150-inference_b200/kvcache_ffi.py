@@ -41,6 +41,12 @@ PLAN_KV_STABLE = 1
 OFFLOAD_PINNED = 1
 OFFLOAD_REGISTER = 2
 
+# kvc_test_inject_failure sites
+FAULT_DEVICE_ALLOC = 1
+FAULT_HOST_ALLOC = 2
+FAULT_HOST_REGISTER = 3
+FAULT_WAIT = 4
+
 _NP_DTYPE = {DTYPE_F16: np.dtype(np.float16), DTYPE_F32: np.dtype(np.float32)}
 
 _c_int = ctypes.c_int
@@ -63,6 +69,8 @@ SIGNATURES = {
     "kvc_device_error": (_c_int, [_c_int, _c_int, ctypes.POINTER(ctypes.c_uint32),
                                   ctypes.POINTER(ctypes.c_uint32)]),
     "kvc_device_sm_count": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
+    "kvc_set_host_wait_limit": (_c_int, [ctypes.c_double]),
+    "kvc_test_inject_failure": (_c_int, [_c_int, _c_int, _c_int]),
     "kvc_cache_init": (_c_int, [_c_int, _c_int, _c_int, _c_int]),
     "kvc_cache_init_ex": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int]),
     "kvc_cache_free": (_c_int, []),
@@ -217,6 +225,17 @@ def device_error(device: int = 0, clear: bool = True):
     info = ctypes.c_uint32(0)
     check(lib.kvc_device_error(device, int(clear), ctypes.byref(code), ctypes.byref(info)))
     return int(code.value), int(info.value)
+
+
+def set_host_wait_limit(seconds: float) -> None:
+    """Limit of the library's host waits for its own GPU work (kvc_set_host_wait_limit)."""
+    check(lib.kvc_set_host_wait_limit(float(seconds)))
+
+
+def inject_failure(site: int, count: int = 1, skip: int = 0) -> None:
+    """Test hook: the next ``count`` calls at ``site`` (FAULT_*) after ``skip``
+    successful ones fail on the host (kvc_test_inject_failure); count 0 disarms."""
+    check(lib.kvc_test_inject_failure(int(site), int(skip), int(count)))
 
 
 def np_dtype_of(dtype_code: int) -> np.dtype:

@@ -82,6 +82,24 @@ KVC_API int kvc_device_error(int device, int clear, uint32_t* code, uint32_t* in
 /* Number of streaming multiprocessors of `device` (grid sizing helper). */
 KVC_API int kvc_device_sm_count(int device, int* out);
 
+/* No counterpart in the reference (its HIP calls block without a limit).  Limit,
+ * in seconds, of every wait of the host for the library's own GPU work: the end
+ * of a host-buffer call, a plan upload, the offload engine's copies.  A wait that
+ * runs out returns KVC_ERR_TIMEOUT; the call's work may still be queued, so
+ * synchronise its stream before reusing its buffers.  Default 60 s; (0, 86400]. */
+KVC_API int kvc_set_host_wait_limit(double seconds);
+
+/* No counterpart in the reference.  Host-side fault injection for tests: after
+ * `skip` further calls at `site` succeed, the next `count` fail the way the CUDA
+ * call would (device / page-locked allocations: cudaErrorMemoryAllocation;
+ * page-locking caller memory: cudaErrorNotPermitted; a host wait: its limit runs
+ * out at once).  Nothing reaches the GPU.  count 0 disarms the site. */
+#define KVC_FAULT_DEVICE_ALLOC 1   /* cudaMalloc of pools, scratch, staging */
+#define KVC_FAULT_HOST_ALLOC 2     /* cudaHostAlloc of page-locked staging */
+#define KVC_FAULT_HOST_REGISTER 3  /* cudaHostRegister of caller memory (offload) */
+#define KVC_FAULT_WAIT 4           /* bounded host waits */
+KVC_API int kvc_test_inject_failure(int site, int skip, int count);
+
 /* ==== 1. Reference-compatible process-wide pool ============================ */
 
 /* Replaces init_device_kv_cache_fp16 (src/kernels/attention.h:27-32,

@@ -32,7 +32,6 @@ if HAS_GPU:
 
     import kvcache_ffi as ffi
     import matmul_module
-    from kv_cache import KVCacheManager
 
 TYPES = [L.F16, L.Q4_0, L.Q8_0, L.Q4_K, L.Q6_K]
 
@@ -40,7 +39,6 @@ TYPES = [L.F16, L.Q4_0, L.Q8_0, L.Q4_K, L.Q6_K]
 @pytest.fixture(autouse=True)
 def _clean(cuda_device):
     yield
-    KVCacheManager._active_gpu_instance = False
     matmul_module.kv_cache_free()
     code, info = ffi.device_error(0, clear=True)
     assert code == 0, f"device error word left set: {code} {info}"

@@ -2,22 +2,23 @@
 
 Tolerances (the path's parity targets and the reference's own tests):
   fp32 storage                 max-abs <= 1e-5
-  fp16 storage, fp32 accumulate max-abs <= 2e-3 * max(1, max|ref|)
-                               (test_layer.py:179 uses 2e-3, test_full_model.py:104/124 1e-3)
-  pool contents, offload vs resident, fused vs separate calls: bit-exact.
+  fp16 storage, fp32 accumulate per query row max|got - ref| <= 2e-3 * max|ref|
+                               (conftest.assert_attention_close); the reference's own
+                               tests use max-abs 2e-3 (test_layer.py:179) and 1e-3
+                               (test_full_model.py:104/124)
+  pool contents, fused vs separate calls: bit-exact.
+The reference's KVCacheManager flows (gpu / cpu / mmap modes, offload engine)
+are replayed in tests/test_gpu_reference_callsites.py.
 """
 
 from __future__ import annotations
-
-import os
-import tempfile
 
 import numpy as np
 import pytest
 
 import cases
 import gqa_ref
-from conftest import HAS_GPU
+from conftest import HAS_GPU, assert_attention_close
 
 pytestmark = pytest.mark.gpu
 
@@ -27,13 +28,8 @@ if HAS_GPU:
     import kvcache_ffi as ffi
     import matmul_module
     import paged
-    from kv_cache import KVCacheManager
 
 G = cases.load_golden() if HAS_GPU else {}
-
-
-def _fp16_tol(ref):
-    return 2e-3 * max(1.0, float(np.max(np.abs(ref.astype(np.float32)))))
 
 
 def _maxerr(a, b):
@@ -43,7 +39,6 @@ def _maxerr(a, b):
 @pytest.fixture(autouse=True)
 def _clean(cuda_device):
     yield
-    KVCacheManager._active_gpu_instance = False
     matmul_module.kv_cache_free()
     code, info = ffi.device_error(0, clear=True)
     assert code == 0, f"device error word left set: {code} {info}"
@@ -58,7 +53,8 @@ def test_reference_layer_cases_gqa_attention():
         out = np.zeros_like(c["Q"])
         matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out, c["q_len"], c["kv_len"], 16, 4,
                                     64, c["start_pos"], c["scale"], True)
-        assert _maxerr(out, G[f"layer{i}_out"]) < 2e-3
+        assert _maxerr(out, G[f"layer{i}_out"]) < 2e-3  # the reference test's tolerance
+        assert_attention_close(out, G[f"layer{i}_out"], f"reference layer case {i}")
 
 
 @pytest.mark.parametrize("name", list(cases.EDGE_CASES))
@@ -73,7 +69,7 @@ def test_edge_cases_gqa_attention(name):
     if c["Q"].dtype == np.float32:
         assert _maxerr(out, ref) <= 1e-5
     else:
-        assert _maxerr(out, ref) <= _fp16_tol(ref)
+        assert_attention_close(out, ref, f"edge case {name}")
 
 
 def test_scale_zero_follows_the_kernel():
@@ -83,7 +79,7 @@ def test_scale_zero_follows_the_kernel():
     matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out, 1, c["kv_len"], 8, 2, 64,
                                 c["start_pos"], 0.0, True)
     expect = gqa_ref.online_softmax_attention(c["Q"], c["K"], c["V"], c["start_pos"], 0.0)
-    assert _maxerr(out, expect) <= 2e-3
+    assert_attention_close(out, expect, "scale 0 (equal scores)")
 
 
 def test_empty_context_gives_zeros():
@@ -98,31 +94,6 @@ def test_empty_context_gives_zeros():
 # ---------------------------------------------------------------------------
 # GPU-resident pool (kv_cache_init / gqa_attention_cached / KVCacheManager)
 # ---------------------------------------------------------------------------
-def test_gpu_kv_cache_manager_reference_sequence():
-    """tests/test_full_model.py:78-129 with the drop-in KVCacheManager."""
-    c = cases.kv_manager_case()
-    L, H, Hkv, D = c["num_layers"], c["num_heads"], c["num_kv_heads"], c["head_dim"]
-    with KVCacheManager(L, c["max_seq_len"], Hkv, D) as kv:
-        for l in range(L):
-            out = np.zeros((4, H, D), np.float16)
-            kv.attend(c["Q"][l, :4], c["K"][l, :4], c["V"][l, :4], out, layer_idx=l, q_len=4,
-                      start_pos=0, num_heads=H, scale=c["scale"], causal=True)
-            assert _maxerr(out, G[f"kvm_prefill_l{l}"]) < 1e-3
-        for pos in (4, 5):
-            for l in range(L):
-                out = np.zeros((1, H, D), np.float16)
-                kv.attend(c["Q"][l, pos:pos + 1], c["K"][l, pos:pos + 1], c["V"][l, pos:pos + 1],
-                          out, layer_idx=l, q_len=1, start_pos=pos, num_heads=H,
-                          scale=c["scale"], causal=True)
-                assert _maxerr(out, G[f"kvm_decode_l{l}_p{pos}"]) < 1e-3
-        assert kv.current_seq_len == 6
-        # pool contents are bit-exact with the reference's host-mode append
-        for l in range(L):
-            k, v = matmul_module.kv_cache_gather(l, 0, 6)
-            np.testing.assert_array_equal(k, c["K"][l, :6])
-            np.testing.assert_array_equal(v, c["V"][l, :6])
-
-
 def test_config1_fp32_pool_within_1e5():
     """benchmark config 1: fp32 pool, 511 cached + 1 appended, max-abs 1e-5."""
     c = cases.config1_case()
@@ -154,7 +125,7 @@ def test_cached_prefill_matches_host_attention_bit_exact():
     out = np.zeros_like(c["Q"])
     matmul_module.gqa_attention_cached(c["Q"], c["K"][P - 1:], c["V"][P - 1:], out, 0, 1, P - 1,
                                        H, Hkv, D, c["scale"], True)
-    assert _maxerr(out, G["split_boundary_1025_out"]) <= _fp16_tol(G["split_boundary_1025_out"])
+    assert_attention_close(out, G["split_boundary_1025_out"], "cached decode at the 1025 split boundary")
     out2 = np.zeros_like(c["Q"])
     matmul_module.gqa_attention(c["Q"], c["K"], c["V"], out2, 1, P, H, Hkv, D, P - 1, c["scale"])
     np.testing.assert_array_equal(out, out2)
@@ -165,9 +136,9 @@ def test_cached_prefill_matches_host_attention_bit_exact():
     outp2 = np.zeros_like(qp[:3])
     matmul_module.gqa_attention(qp[600:603], c["K"][:603], c["V"][:603], outp2, 3, 603, H, Hkv,
                                 D, 600, c["scale"])
-    assert _maxerr(outp[600:603], outp2) <= 2e-3
+    assert_attention_close(outp[600:603], outp2, "prefill rows vs the same queries alone")
     ref = gqa_ref.ref_gqa_attention(qp[600:603], c["K"][:603], c["V"][:603], 600, c["scale"])
-    assert _maxerr(outp[600:603], ref) <= _fp16_tol(ref)
+    assert_attention_close(outp[600:603], ref, "cached prefill rows 600-602")
 
 
 def test_validation_matches_reference_exception_classes():
@@ -203,110 +174,6 @@ def test_validation_matches_reference_exception_classes():
 
 
 # ---------------------------------------------------------------------------
-# offload modes: bit-identical to the resident pool
-# ---------------------------------------------------------------------------
-def _run_sequence(kv, c, chunk=None):
-    """Prefill 8 positions (optionally chunked) then decode 3, over all layers."""
-    L, H, D = c["L"], c["H"], c["D"]
-    outs = []
-    pos = 0
-    spans = [(0, 8)] if chunk is None else [(s, min(8, s + chunk)) for s in range(0, 8, chunk)]
-    spans += [(8, 9), (9, 10), (10, 11)]
-    for s, e in spans:
-        for l in range(L):
-            out = np.zeros((e - s, H, D), np.float16)
-            kv.attend(c["Q"][l, s:e], c["K"][l, s:e], c["V"][l, s:e], out, layer_idx=l,
-                      q_len=e - s, start_pos=s, num_heads=H, scale=c["scale"], causal=True)
-            outs.append((l, s, e, out))
-        pos = e
-    assert kv.current_seq_len == pos
-    return outs
-
-
-def _seq_case():
-    rng = np.random.default_rng(77)
-    L, T, H, Hkv, D = 3, 11, 8, 2, 64
-    return dict(L=L, H=H, Hkv=Hkv, D=D, scale=0.125,
-                Q=(rng.standard_normal((L, T, H, D), dtype=np.float32) * 0.5).astype(np.float16),
-                K=(rng.standard_normal((L, T, Hkv, D), dtype=np.float32) * 0.5).astype(np.float16),
-                V=(rng.standard_normal((L, T, Hkv, D), dtype=np.float32) * 0.5).astype(np.float16))
-
-
-def _by_position(outs):
-    rows = {}
-    for l, s, e, out in outs:
-        for i in range(e - s):
-            rows[(l, s + i)] = out[i]
-    return rows
-
-
-def test_offload_cpu_and_mmap_bit_identical_to_resident():
-    c = _seq_case()
-    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"]) as kv:
-        gpu = _by_position(_run_sequence(kv, c))
-    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], offload_to_cpu=True) as kv:
-        cpu = _by_position(_run_sequence(kv, c))
-        st = kv.offload_stats()
-        assert st["attend_calls"] == 4 * c["L"] and st["prefetch_hits"] >= 3 * c["L"] - 1
-        assert st["h2d_bytes"] > 0
-        np.testing.assert_array_equal(kv._k_host[:, :11], c["K"])  # host append, bit-exact
-    with tempfile.TemporaryDirectory() as d:
-        with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], mmap_dir=d) as kv:
-            mm = _by_position(_run_sequence(kv, c))
-    for key in gpu:
-        np.testing.assert_array_equal(cpu[key], gpu[key], err_msg=str(key))
-        np.testing.assert_array_equal(mm[key], gpu[key], err_msg=str(key))
-    for (l, p), row in gpu.items():
-        ref = gqa_ref.ref_gqa_attention(c["Q"][l, p:p + 1], c["K"][l, :p + 1], c["V"][l, :p + 1],
-                                        p, c["scale"])[0]
-        assert _maxerr(row, ref) < 2e-3
-
-
-def test_offload_hbm_mirror_bit_identical_and_uploads_only_new_rows():
-    """offload_mirror_bytes: some layers mirrored in HBM (the rest streamed), every
-    output bit-identical to the resident pool; after the prefill a decode step
-    uploads just the appended rows of the mirrored layers; invalidate re-uploads."""
-    c = _seq_case()
-    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"]) as kv:
-        gpu = _by_position(_run_sequence(kv, c))
-    layer_bytes = 2 * 64 * c["Hkv"] * c["D"] * 2     # K + V pages of one layer (64 positions)
-    for budget, expect_layers in ((layer_bytes * 2, 2), (layer_bytes * 10, 3)):
-        with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], offload_to_cpu=True,
-                            offload_mirror_bytes=budget) as kv:
-            got = _by_position(_run_sequence(kv, c))
-            st = kv.offload_stats()
-            assert st["mirror_layers"] == expect_layers
-            row = c["Hkv"] * c["D"] * 2
-            # prefill chunks: 8 rows per mirrored layer; then 3 decode steps of 1 row each
-            assert st["mirror_bytes"] == 2 * row * expect_layers * (8 + 3)
-            if expect_layers == c["L"]:
-                assert st["h2d_bytes"] == 0  # nothing streamed
-            # a further step after invalidate re-uploads whole layers, same results
-            ffi.check(ffi.lib.kvc_offload_invalidate(kv._offload))
-            out = np.zeros((1, c["H"], c["D"]), np.float16)
-            kv.attend(c["Q"][0, 10:11], c["K"][0, 10:11], c["V"][0, 10:11], out, layer_idx=0,
-                      q_len=1, start_pos=10, num_heads=c["H"], scale=c["scale"], causal=True)
-            np.testing.assert_array_equal(out[0], gpu[(0, 10)])
-            assert kv.offload_stats()["mirror_bytes"] == st["mirror_bytes"] + 2 * row * 11
-        for key in gpu:
-            np.testing.assert_array_equal(got[key], gpu[key], err_msg=f"{budget} {key}")
-
-
-def test_chunked_prefill_bit_identical():
-    """test_phase5_scale.py:199-206 (full vs chunked prefill) at the attention level."""
-    c = _seq_case()
-    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"]) as kv:
-        full = _by_position(_run_sequence(kv, c))
-        kv.reset()
-        chunked = _by_position(_run_sequence(kv, c, chunk=3))
-    with KVCacheManager(c["L"], 64, c["Hkv"], c["D"], offload_to_cpu=True) as kv:
-        off_chunked = _by_position(_run_sequence(kv, c, chunk=2))
-    for key in full:
-        np.testing.assert_array_equal(chunked[key], full[key])
-        np.testing.assert_array_equal(off_chunked[key], full[key])
-
-
-# ---------------------------------------------------------------------------
 # paged batched decode
 # ---------------------------------------------------------------------------
 def _ragged_pool(page_size=16, dtype=None, seed=3):
@@ -333,7 +200,7 @@ def test_paged_ragged_batch_decode_and_pool_bit_exact():
     out = torch.zeros_like(q)
     pool.decode(plan, 0, q, out, bt, c["scale"])
     res = out.cpu().numpy()
-    assert _maxerr(res, G["ragged_out"]) <= _fp16_tol(G["ragged_out"])
+    assert_attention_close(res, G["ragged_out"], "paged ragged batch")
     for i, ctx in enumerate(c["ctx"]):
         k, v = pool.gather(0, bt, i, 0, ctx)
         np.testing.assert_array_equal(k.cpu().numpy(), c["ks"][i])
@@ -346,7 +213,7 @@ def test_paged_ragged_batch_decode_and_pool_bit_exact():
         o1 = torch.zeros_like(q[i:i + 1])
         pool.decode(p1, 0, q[i:i + 1].contiguous(), o1, bt, c["scale"])
         ref = out[i].float().cpu().numpy()
-        assert _maxerr(o1[0].cpu().numpy(), ref) <= _fp16_tol(ref)
+        assert_attention_close(o1[0].cpu().numpy(), ref, f"one-sequence plan, query {i}")
         # the same one-sequence plan twice: bit for bit
         o2 = torch.zeros_like(o1)
         pool.decode(p1, 0, q[i:i + 1].contiguous(), o2, bt, c["scale"])
@@ -363,8 +230,8 @@ def test_page_size_does_not_change_results(page_size):
     poolp.decode(poolp.plan(c["ctx"], c["H"]), 0, q, op, btp, c["scale"])
     # splits are whole pages, so the partition may differ with the page size
     ref = o16.float().cpu().numpy()
-    assert _maxerr(op.cpu().numpy(), ref) <= _fp16_tol(ref)
-    assert _maxerr(op.cpu().numpy(), G["ragged_out"]) <= _fp16_tol(G["ragged_out"])
+    assert_attention_close(op.cpu().numpy(), ref, f"page size {page_size} vs page size 16")
+    assert_attention_close(op.cpu().numpy(), G["ragged_out"], f"page size {page_size} vs golden")
 
 
 def test_append_decode_fused_equals_separate_and_host_call():
@@ -401,7 +268,7 @@ def test_append_decode_fused_equals_separate_and_host_call():
         assert torch.equal(k[c - 1], kn[i]) and torch.equal(v[c - 1], vn[i])
         ref = gqa_ref.ref_gqa_attention(q[i:i + 1].cpu().numpy(), k.cpu().numpy(),
                                         v.cpu().numpy(), c - 1, 0.088)
-        assert _maxerr(o_fused[i:i + 1].cpu().numpy(), ref) <= _fp16_tol(ref)
+        assert_attention_close(o_fused[i:i + 1].cpu().numpy(), ref, f"fused append + decode, query {i}")
 
 
 def test_bf16_pool_against_fp32_reference():
@@ -437,7 +304,7 @@ def test_head_dim_80_uses_cuda_core_path():
     out = np.zeros_like(Q)
     matmul_module.gqa_attention(Q, K, V, out, 1, P, H, Hkv, D, P - 1, 0.11)
     ref = gqa_ref.ref_gqa_attention(Q, K, V, P - 1, 0.11)
-    assert _maxerr(out, ref) <= 2e-3
+    assert_attention_close(out, ref, "head_dim 80 (CUDA-core path)")
 
 
 def test_bad_block_table_is_reported_and_context_survives():
@@ -544,7 +411,7 @@ def test_append_decode_rope_equals_rope_then_append_decode():
             assert torch.equal(k[c - 1], kr[i]) and torch.equal(v[c - 1], vn[i])
             ref = gqa_ref.ref_gqa_attention(qr[i:i + 1].cpu().numpy(), k.cpu().numpy(),
                                             v.cpu().numpy(), c - 1, 0.088)
-            assert _maxerr(o1[i:i + 1].cpu().numpy(), ref) <= _fp16_tol(ref)
+            assert_attention_close(o1[i:i + 1].cpu().numpy(), ref, f"rope + append + decode, query {i}")
         # rotated q/k against the oracle rotation
         ref_k = gqa_ref.ref_rope(kn.cpu().numpy(), neox_style=neox, positions=pos.cpu().numpy(),
                                  inv_freq=gqa_ref.libm_inv_freq(500000.0, D))
@@ -587,5 +454,5 @@ def test_paged_decode_loop_with_growing_contexts():
             for i in range(n):
                 c = int(ctx[i])
                 ref = gqa_ref.ref_gqa_attention(q[i:i + 1], ks[l][i][:c], vs[l][i][:c], c - 1, 0.09)
-                assert _maxerr(got[i:i + 1], ref) <= _fp16_tol(ref), (s, l, i)
+                assert_attention_close(got[i:i + 1], ref, f"step {s} layer {l} query {i}")
     assert ffi.device_error(0) == (0, 0)

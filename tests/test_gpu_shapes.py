@@ -3,9 +3,9 @@
 The persistent decode kernel is instantiated per head dim (32 ... 256) and
 handles q-head groups in chunks of eight; these cases run each instantiation on
 a ragged batch whose contexts cross split boundaries (so the split merge runs)
-and compare with the oracle on the gathered pool contents.  Tolerances: fp16
-storage 2e-3 x max(1, |ref|) as in the other parity tests; bf16 (8-bit
-mantissa) 1.6e-2 x max(1, |ref|).
+and compare with the oracle on the gathered pool contents.  Tolerances, per
+query row relative to its largest |ref| (conftest.assert_attention_close):
+fp16 storage 2e-3 as in the other parity tests; bf16 (8-bit mantissa) 1.6e-2.
 """
 
 from __future__ import annotations
@@ -13,7 +13,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import HAS_GPU
+from conftest import HAS_GPU, assert_attention_close
 
 pytestmark = pytest.mark.gpu
 
@@ -56,19 +56,16 @@ def _run(D, group, dtype, seed):
 @pytest.mark.parametrize("D", HEAD_DIMS)
 def test_head_dims_fp16(D):
     got, ref = _run(D, 4, torch.float16, 40 + D)
-    err = float(np.max(np.abs(got - ref)))
-    assert err <= 2e-3 * max(1.0, float(np.max(np.abs(ref)))), (D, err)
+    assert_attention_close(got, ref, f"fp16 head_dim {D}")
 
 
 @pytest.mark.parametrize("group", GROUPS)
 def test_group_sizes_fp16(group):
     got, ref = _run(128, group, torch.float16, 70 + group)
-    err = float(np.max(np.abs(got - ref)))
-    assert err <= 2e-3 * max(1.0, float(np.max(np.abs(ref)))), (group, err)
+    assert_attention_close(got, ref, f"fp16 group {group}")
 
 
 @pytest.mark.parametrize("D", [64, 128, 256])
 def test_head_dims_bf16(D):
     got, ref = _run(D, 8, torch.bfloat16, 90 + D)
-    err = float(np.max(np.abs(got - ref)))
-    assert err <= 1.6e-2 * max(1.0, float(np.max(np.abs(ref)))), (D, err)
+    assert_attention_close(got, ref, f"bf16 head_dim {D}", rel=1.6e-2)

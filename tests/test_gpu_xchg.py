@@ -16,7 +16,7 @@ import socket
 import numpy as np
 import pytest
 
-from conftest import HAS_GPU
+from conftest import HAS_GPU, assert_attention_close
 
 pytestmark = pytest.mark.gpu
 
@@ -81,8 +81,8 @@ def test_xchg_one_rank_matches_decode_and_oracle(cuda_device):
             assert ffi.device_error(0) == (0, 0)
             got = view[:, H:].float()
             assert torch.isnan(view[:, :H].float()).all(), "heads outside the rank's range were written"
-            err = (got - expect.float()).abs().max().item()
-            assert err <= 2e-3 * max(1.0, expect.float().abs().max().item()), (call, err)
+            assert_attention_close(got.cpu().numpy(), expect.float().cpu().numpy(),
+                                   f"exchange slot call {call} vs kvc_decode")
         # and against the oracle, per sequence
         info = pool.info()
         for i, c in enumerate(ctx):
@@ -90,8 +90,7 @@ def test_xchg_one_rank_matches_decode_and_oracle(cuda_device):
             ref = gqa_ref.ref_gqa_attention(q[i:i + 1].cpu().numpy(), k.cpu().numpy(),
                                             v.cpu().numpy(), start_pos=c - 1, scale=scale,
                                             out_dtype=np.float32)[0]
-            err = np.abs(got[i].cpu().numpy() - ref).max()
-            assert err <= 2e-3 * max(1.0, np.abs(ref).max()), (i, err)
+            assert_attention_close(got[i].cpu().numpy(), ref, f"exchange slot vs oracle, query {i}")
         assert info["k"]
     finally:
         ffi.lib.kvc_xchg_destroy(h)
@@ -115,8 +114,8 @@ def test_xchg_fused_append_matches_append_decode(cuda_device):
         pool2.append_decode_xchg(plan2, 0, q, kn, vn, h, 0, H, 0, bt, scale)
         torch.cuda.synchronize()
         got = _slot(h, 0, (len(ctx), H, D))
-        err = (got.float() - expect.float()).abs().max().item()
-        assert err <= 2e-3 * max(1.0, expect.float().abs().max().item()), err
+        assert_attention_close(got.float().cpu().numpy(), expect.float().cpu().numpy(),
+                               "exchange with fused append vs append_decode")
         # the appended rows are in the pool, bit for bit
         for i, c in enumerate(ctx):
             k2, v2 = pool2.gather(0, bt, i, c - 1, 1)
@@ -219,7 +218,10 @@ def _two_rank_main(rank, port, results):
                 a = p2p.append_decode(plans[0], l, q[l], kn[l], vn[l], None, bt, scale).clone()
                 b = nccl.append_decode(plans[1], l, q[l], kn[l], vn[l], None, bt, scale)
                 torch.cuda.synchronize()
-                worst = max(worst, (a.float() - b.float()).abs().max().item())
+                # per query row: max|p2p - nccl| / max|nccl| (the fp16 bound's form)
+                d = (a.float() - b.float()).abs().amax(dim=(1, 2))
+                m = b.float().abs().amax(dim=(1, 2)).clamp_min(1e-30)
+                worst = max(worst, (d / m).max().item())
         code, info = ffi.device_error(rank)
         p2p.close()
         results[rank] = (worst, code, info)
@@ -245,4 +247,4 @@ def test_two_gpu_p2p_exchange_matches_nccl_all_gather():
     for rank in (0, 1):
         worst, code, info = results[rank]
         assert code == 0, (rank, code, info)
-        assert worst <= 2e-3 * 8, (rank, worst)
+        assert worst <= 2e-3, (rank, worst)
