@@ -145,10 +145,16 @@ struct XchgTarget {
 void* mapped_host_ptr(void* h);
 // End of a host-buffer call on stream s: copy `bytes` of d_out to h_out unless
 // the kernels wrote h_out directly (d_out == nullptr), read the device error
-// word into page-locked memory on the same stream, wait for the stream, and
-// report a device error under `what`.
+// word into page-locked memory on the same stream (unless `merged`: the split
+// merge stored it there), wait for the stream, and report a device error under
+// `what`.
 int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t bytes,
-                     const char* what);
+                     const char* what, bool merged = false);
+// Creates the page-locked copy of the device error word (once per device) before
+// a host-buffer call launches its kernels; until finish_host_call, the decodes
+// this thread launches store the word there (host_call_error_copy()).
+int prepare_host_call();
+uint32_t* host_call_error_copy();
 
 // Host buffers of one host-buffer call (q, new K rows, new V rows; out).
 // stage_host_call moves the inputs to d_in[] with the input staging kernel,
@@ -165,8 +171,10 @@ struct HostCallStage {
 int stage_host_call(kvc::HostBuf& pinned, const void* const h_in[3], const size_t in_bytes[3],
                     uint8_t* const d_in[3], void* h_out, size_t out_bytes, cudaStream_t s,
                     HostCallStage* st);
+// merged: the call's last kernel is the tensor-core decode's split merge, which
+// keeps the error word's page-locked mirror current (no copy of its own needed).
 int finish_staged_call(cudaStream_t s, void* h_out, const HostCallStage& st, size_t out_bytes,
-                       const char* what);
+                       const char* what, bool merged = false);
 
 // Plans q_len queries at start_pos (row 0 of the block table) of a single
 // sequence; run before any input staging so the plan's upload does not sit

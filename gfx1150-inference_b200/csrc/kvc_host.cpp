@@ -149,9 +149,13 @@ void* mapped_host_ptr(void* h) {
 namespace {
 // Page-locked landing place of each device's error word, and the word's address.
 struct ErrMirror {
-  uint32_t* host = nullptr;
-  void* dev = nullptr;
+  uint32_t* host = nullptr;      // page-locked copy of the device error word
+  uint32_t* host_dev = nullptr;  // its device address (null: not mapped)
+  void* dev = nullptr;           // the device error word
 };
+// The error-word copy the kernels of this thread's host-buffer call in progress
+// store (DecodeArgs::err_host), between stage_host_call and finish_host_call.
+thread_local uint32_t* t_err_host = nullptr;
 std::mutex g_mirror_mu;
 ErrMirror g_mirror[64];
 
@@ -165,36 +169,57 @@ cudaError_t error_mirror(ErrMirror** out) {
   if (!m.host) {
     void* h = nullptr;
     if ((e = host_alloc(&h, 64, cudaHostAllocDefault)) != cudaSuccess) return e;
+    memset(h, 0, 64);
     if ((e = device_error_address(&m.dev)) != cudaSuccess) {
       cudaFreeHost(h);
       return e;
     }
     m.host = static_cast<uint32_t*>(h);
+    m.host_dev = static_cast<uint32_t*>(mapped_host_ptr(h));
   }
   *out = &m;
   return cudaSuccess;
 }
 }  // namespace
 
+int prepare_host_call() {
+  ErrMirror* m = nullptr;
+  const cudaError_t e = error_mirror(&m);
+  if (e != cudaSuccess) return cuda_error(e, "device error mirror");
+  t_err_host = m->host_dev;
+  return KVC_OK;
+}
+
+uint32_t* host_call_error_copy() { return t_err_host; }
+
 int finish_host_call(cudaStream_t s, void* h_out, const void* d_out, size_t bytes,
-                     const char* what) {
+                     const char* what, bool merged) {
   cudaError_t e;
   if (d_out && bytes && (e = cudaMemcpyAsync(h_out, d_out, bytes, cudaMemcpyDeviceToHost, s)))
     return cuda_error(e, "cudaMemcpyAsync(D2H)");
   ErrMirror* m = nullptr;
   if ((e = error_mirror(&m)) != cudaSuccess) return cuda_error(e, "device error mirror");
   // Concurrent calls on one device copy the same word into the same place: a call
-  // sees at least every error raised before its own kernels finished.
-  if ((e = cudaMemcpyAsync(m->host, m->dev, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s)))
+  // sees at least every error raised before its own kernels finished.  When the
+  // call's last kernel is a split merge, that merge stored the word there already
+  // (no copy-engine round trip on the call's critical path).
+  const bool stored = merged && t_err_host != nullptr && t_err_host == m->host_dev;
+  t_err_host = nullptr;
+  if (!stored &&
+      (e = cudaMemcpyAsync(m->host, m->dev, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s)))
     return cuda_error(e, "cudaMemcpyAsync(error word)");
   if (const int rc = wait_stream(s, what)) return rc;
   if ((reinterpret_cast<volatile uint32_t*>(m->host)[0]) == KVC_DEVERR_NONE) return KVC_OK;
-  return check_device_error(what);  // rare: read, clear and report
+  const int rc = check_device_error(what);  // rare: read, clear and report
+  reinterpret_cast<volatile uint32_t*>(m->host)[0] = KVC_DEVERR_NONE;  // the word is clear now
+  return rc;
 }
 
 int stage_host_call(HostBuf& pinned, const void* const h_in[3], const size_t in_bytes[3],
                     uint8_t* const d_in[3], void* h_out, size_t out_bytes, cudaStream_t s,
                     HostCallStage* st) {
+  // the error word's page-locked mirror exists before this call's kernels run
+  if (const int rc = prepare_host_call()) return rc;
   auto al16 = [](size_t b) { return (b + 15) & ~static_cast<size_t>(15); };
   const void* src[3] = {nullptr, nullptr, nullptr};
   size_t need = 0;
@@ -239,8 +264,8 @@ int stage_host_call(HostBuf& pinned, const void* const h_in[3], const size_t in_
 }
 
 int finish_staged_call(cudaStream_t s, void* h_out, const HostCallStage& st, size_t out_bytes,
-                       const char* what) {
-  const int rc = finish_host_call(s, h_out, nullptr, 0, what);
+                       const char* what, bool merged) {
+  const int rc = finish_host_call(s, h_out, nullptr, 0, what, merged);
   if (rc) return rc;
   if (st.out_bounce && out_bytes) memcpy(h_out, st.out_bounce, out_bytes);
   return KVC_OK;
@@ -924,6 +949,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.n_sched_ctas = plan->n_sched_ctas;
   a.early_prefetch = early >= 0 ? early : ((plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0);
   a.l2_ahead = l2_ahead_slabs(plan->split_tokens);
+  a.err_host = host_call_error_copy();
   a.merge_queries = plan->dev_merge;
   a.n_merge_queries = static_cast<int>(plan->merge_queries.size());
   a.k_new = static_cast<const uint8_t*>(d_k_new);
@@ -1236,7 +1262,8 @@ extern "C" int kvc_decode_host(kvc_pool_t* pool, const kvc_plan_t* plan, int lay
   rc = append_then_decode(pool, plan, layer, d_in[0], d_in[1], d_in[2], st.out_dev, d_block_tables,
                           bt_stride, scale, s, nullptr, 1);
   if (rc) return rc;
-  return finish_staged_call(s, h_out, st, qb, "kvc_decode_host");
+  return finish_staged_call(s, h_out, st, qb, "kvc_decode_host",
+                            decode_uses_mma(g.dtype, g.head_dim, g.page_size));
 }
 
 // ============================================================================
@@ -1438,7 +1465,8 @@ extern "C" int kvc_gqa_attention_cached(const void* h_Q, const void* h_K_new,
   rc = cached_run(&S.pool, &S.plan, static_cast<const int32_t*>(S.bt.ptr), S.bt_len, d_in[0],
                   d_in[1], d_in[2], st.out_dev, layer_idx, q_len, start_pos, scale, s, 1);
   if (rc) return rc;
-  return finish_staged_call(s, h_Out, st, qb, "gqa_attention_cached");
+  return finish_staged_call(s, h_Out, st, qb, "gqa_attention_cached",
+                            decode_uses_mma(g.dtype, g.head_dim, g.page_size));
 }
 
 extern "C" int kvc_gqa_attention_cached_device(const void* d_Q, const void* d_K_new,
@@ -1667,7 +1695,8 @@ extern "C" int kvc_gqa_attention_ex(const void* h_Q, const void* h_K, const void
   HostCallStage st;
   if ((rc = stage_host_call(C.pool.io_host, h_in, in_b, d_in, h_Out, qb, s, &st))) return rc;
   if ((rc = do_decode(&C.pool, &C.plan, 0, d_q, st.out_dev, bt, C.bt_len, scale, s))) return rc;
-  return finish_staged_call(s, h_Out, st, qb, "gqa_attention");
+  return finish_staged_call(s, h_Out, st, qb, "gqa_attention",
+                            decode_uses_mma(g.dtype, g.head_dim, g.page_size));
 }
 
 extern "C" int kvc_gqa_attention(const void* h_Q, const void* h_K, const void* h_V, void* h_Out,

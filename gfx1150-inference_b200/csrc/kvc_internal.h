@@ -175,6 +175,10 @@ struct DecodeArgs {
   unsigned int* peer_flag[kMaxPeers] = {};
   const unsigned int* my_flags = nullptr;  // this rank's flag words, one per source rank
   unsigned long long wait_limit_ns = 0;
+  // Host-buffer calls: device address of the page-locked copy of the device error
+  // word, which the split merge (the last kernel of the call) stores, so the host
+  // reads it after its wait without a copy of its own.  Null otherwise.
+  uint32_t* err_host = nullptr;
 };
 
 struct FillArgs {

@@ -895,9 +895,15 @@ __global__ void __launch_bounds__(512) merge_splits_kernel(const DecodeArgs a) {
   __shared__ float red_m[kMergeWarps], red_l[kMergeWarps];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The decode grid has finished: re-arm its unit counter for the next launch,
-  // visibly to the whole device before the next launch may start.
+  // visibly to the whole device before the next launch may start, and copy the
+  // device error word (every error of the decode is in it now) to its host mirror.
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
     *a.queue = 0u;
+    if (uint32_t* m = a.err_host) {
+      const volatile uint32_t* w = g_kvc_deverr;
+      m[1] = w[1];
+      m[0] = w[0];
+    }
     __threadfence();
   }
   __syncthreads();

@@ -252,7 +252,9 @@ int attend_mirrored(kvc_offload* o, const void* h_Q, void* h_Out, int layer, int
   if ((rc = stage_q(o, h_Q, d_q, qb, h_Out, s, &st))) return rc;
   if ((rc = do_decode(&o->mirror, &o->plan, layer, d_q, st.out_dev, bt, o->bt_len, scale, s)))
     return rc;
-  return finish_staged_call(s, h_Out, st, qb, "offload attend");
+  const PoolGeom& g = o->mirror.g;
+  return finish_staged_call(s, h_Out, st, qb, "offload attend",
+                            decode_uses_mma(g.dtype, g.head_dim, g.page_size));
 }
 
 }  // namespace
@@ -476,5 +478,7 @@ extern "C" int kvc_offload_attend(kvc_offload_t* off, const void* h_Q, const voi
                          o->device, s)))
     return rc;
   if ((rc = do_decode(&o->slot, &o->plan, 0, d_q, st.out_dev, bt, o->bt_len, scale, s))) return rc;
-  return finish_staged_call(s, h_Out, st, qb, "offload attend");
+  const PoolGeom& g = o->slot.g;
+  return finish_staged_call(s, h_Out, st, qb, "offload attend",
+                            decode_uses_mma(g.dtype, g.head_dim, g.page_size));
 }

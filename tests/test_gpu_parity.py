@@ -323,6 +323,19 @@ def test_bad_block_table_is_reported_and_context_survives():
     torch.cuda.synchronize()
     assert ffi.device_error(0, clear=True) == (0, 0)
     assert torch.isfinite(out).all()
+    # the host-buffer call learns of it from the copy of the error word its split
+    # merge stores (no copy of its own), then the word is clear again
+    plan = pool.plan([40, 60], H)
+    bt2 = torch.tensor([[0, 1, 3, 4], [5, 6, 99, 7]], dtype=torch.int32, device="cuda")
+    hq = torch.ones((2, H, D), dtype=torch.float16).pin_memory()
+    hk = torch.zeros((2, Hkv, D), dtype=torch.float16).pin_memory()
+    ho = torch.zeros_like(hq).pin_memory()
+    with pytest.raises(ffi.KVCacheDeviceError, match="block table"):
+        pool.decode_host(plan, 0, hq, hk, hk, ho, bt2, 0.1)
+    assert ffi.device_error(0, clear=True) == (0, 0)
+    bt2[1, 2] = 2
+    pool.decode_host(plan, 0, hq, hk, hk, ho, bt2, 0.1)  # no stale error
+    assert torch.isfinite(ho).all()
 
 
 # ---- rotary position embedding (rope.hip:21-55; ref_rope, test_layer.py:44-73) --------
