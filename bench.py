@@ -227,6 +227,41 @@ class CpuWorkload:
         return time.perf_counter() - t0
 
 
+def blas_threads() -> int:
+    """Threads numpy's BLAS may use (the numpy path's matrix-vector products)."""
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [d.get("num_threads", 1) for d in threadpool_info() if d.get("user_api") == "blas"]
+        return int(max(n)) if n else 1
+    except Exception:
+        return 1
+
+
+def numpy_path_sample(w, min_seconds=5.0):
+    """The reference's numpy path for this step: per sequence, the host append
+    (KVCacheManager's slice assignment, src/kv_cache.py:222-225) and
+    ref_gqa_attention (tests/test_layer.py:76-105) over its whole context, as
+    oracle/gqa_ref.py restates them; sequences of one layer in turn until
+    min_seconds.  Returns (GB/s, seconds, sequences timed)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import gqa_ref  # test infrastructure: the CPU baseline leg only
+
+    nbytes, total, done = 0, 0.0, 0
+    while total < min_seconds:
+        i = done % w.n
+        k, v = w.ks[i], w.vs[i]
+        ctx = k.shape[0]
+        t0 = time.perf_counter()
+        k[ctx - 1] = w.q[i, :w.Hkv]  # the appended row (host append of the new token)
+        v[ctx - 1] = w.q[i, :w.Hkv]
+        gqa_ref.ref_gqa_attention(w.q[i:i + 1], k, v, start_pos=ctx - 1, scale=w.scale)
+        total += time.perf_counter() - t0
+        nbytes += ctx * w.Hkv * w.D * 2 * 2 + w.H * w.D * 2 * 2
+        done += 1
+    return nbytes / total / 1e9, total, done
+
+
 def cpu_sample(cfg, ctx, min_seconds=10.0, max_reps=50):
     """Time one layer of the workload (all sequences) on the host cores, repeated
     until min_seconds.  Returns (GB/s, seconds per layer, threads, reps)."""
@@ -1237,6 +1272,7 @@ def run_reference(args, rank, world):
     times = [w.run_layer() for _ in range(args.warmup + args.steps)][args.warmup:]
     dt = float(np.mean(times))
     gbs = w.layer_bytes / dt / 1e9
+    np_gbs, np_s, np_n = numpy_path_sample(w)
     sample = (f"each step: 1 of {cfg['layers']} layers x {cfg['batch']} sequences of the "
               f"workload; oracle/gqa_online.c, the reference kernel's algorithm "
               f"(attention.hip:35-123), OpenMP")
@@ -1263,6 +1299,12 @@ def run_reference(args, rank, world):
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "numpy_path": {"value": round(np_gbs, 4), "unit": "GB/s", "cores": blas_threads(),
+                       "kind": "port",
+                       "sample": (f"{np_n} sequences of one layer in turn, {np_s:.1f} s: host "
+                                  f"append + ref_gqa_attention (the reference's numpy path, "
+                                  f"tests/test_layer.py:76-105, as oracle/gqa_ref.py restates "
+                                  f"it)")},
     }
 
 

@@ -83,6 +83,9 @@ struct kvc_plan {
   std::vector<int32_t> built_from;
   kvc::DevBuf d_blob;          // items, qinfo, rows, positions, unit records, merge list, counter
   kvc::DevBuf d_part_o, d_part_ml, d_counters;
+  // device-error count when d_counters was last zeroed (a kernel that gave up
+  // may leave split counters armed: a later build zeroes them again)
+  uint32_t counters_zeroed_at = 0;
   // parts of d_blob (set by the upload)
   const int4* dev_items = nullptr;
   const int4* dev_qinfo = nullptr;

@@ -853,10 +853,12 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   const size_t cnt_b = sizeof(unsigned) * std::max<size_t>(1, static_cast<size_t>(n_queries) * g.num_kv_heads * p->n_hchunk);
   if ((e = p->d_part_o.ensure(po_b)) || (e = p->d_part_ml.ensure(pml_b)))
     return cuda_error(e, "plan buffers");
-  if (cnt_b > p->d_counters.cap) {
+  const uint32_t dev_errors = g_device_errors.load();
+  if (cnt_b > p->d_counters.cap || dev_errors != p->counters_zeroed_at) {
     if ((e = p->d_counters.ensure(cnt_b))) return cuda_error(e, "plan counters");
     if ((e = cudaMemsetAsync(p->d_counters.ptr, 0, p->d_counters.cap, s)))
       return cuda_error(e, "cudaMemsetAsync(counters)");
+    p->counters_zeroed_at = dev_errors;
   }
   // The plan itself: one block {items | qinfo | rows | positions | unit records |
   // merge list | unit counter (zero)}, 256-byte aligned parts, staged in pinned

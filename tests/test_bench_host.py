@@ -38,3 +38,16 @@ def test_layer_launch_counts():
     assert bench.layer_launches(bench.LAYER_TYPES["q4_0"]) == 9
     assert bench.layer_launches(bench.LAYER_TYPES["q4_k_m"]) == 10   # v is Q6_K
     assert bench.layer_launches((1, 8, 2, 1, 2, 8, 1)) == 7 + 3 + 3  # every run split
+
+
+def test_reference_numpy_path_sample_counts_its_bytes():
+    """The reference arm's numpy-path leg (host append + ref_gqa_attention per
+    sequence) times whole sequences and divides the bytes they read."""
+    cfg = {"H": 4, "Hkv": 2, "D": 16, "seed": 3}
+    ctx = np.array([5, 9])
+    w = bench.CpuWorkload(cfg, ctx, threads=1)
+    gbs, secs, n = bench.numpy_path_sample(w, min_seconds=0.01)
+    assert n >= 1 and secs > 0 and gbs > 0
+    per_seq = [int(c) * 2 * 16 * 2 * 2 + 4 * 16 * 2 * 2 for c in ctx]
+    expect = sum(per_seq[i % 2] for i in range(n))
+    assert abs(gbs * secs * 1e9 - expect) <= 1e-6 * expect
