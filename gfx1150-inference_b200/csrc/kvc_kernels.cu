@@ -150,26 +150,60 @@ cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s) {
 // straight from page-locked host memory (over PCIe) into device staging.  The
 // kernel triggers its dependents first, so the decode launched behind it streams
 // KV from HBM while the inputs cross the host link; the decode reads them only
-// after griddepcontrol.wait.
+// after griddepcontrol.wait.  Its CTAs are small enough to share an SM with a
+// decode CTA (4 warps at <= 32 registers: the 4,096 registers a 240-register
+// decode CTA leaves free, and no shared memory), so the decode's CTAs start on
+// every SM at once instead of waiting for the SMs the staging holds.
 // =====================================================================================
-__global__ void __launch_bounds__(256) stage_inputs_kernel(const StageArgs a) {
+constexpr int kStageThreads = 128;
+constexpr int kStageUnroll = 4;  // 16-byte loads in flight per thread
+
+__global__ void __launch_bounds__(kStageThreads, 16) stage_inputs_kernel(const StageArgs a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const unsigned stride = gridDim.x * blockDim.x;
+  const unsigned t0 = blockIdx.x * blockDim.x + threadIdx.x;
 #pragma unroll
   for (int b = 0; b < 3; ++b) {
-    const size_t n16 = a.bytes[b] / 16;
+    // staging sizes are far below 2^32 16-byte units (checked by the launcher)
+    const unsigned n16 = static_cast<unsigned>(a.bytes[b] / 16);
     const uint4* src = reinterpret_cast<const uint4*>(a.src[b]);
     uint4* dst = reinterpret_cast<uint4*>(a.dst[b]);
-    for (size_t i = t0; i < n16; i += stride) dst[i] = src[i];
-    for (size_t i = n16 * 16 + t0; i < a.bytes[b]; i += stride) a.dst[b][i] = a.src[b][i];
+#pragma unroll 1
+    for (unsigned i0 = t0; i0 < n16; i0 += kStageUnroll * stride) {
+      uint4 v[kStageUnroll];
+#pragma unroll
+      for (int u = 0; u < kStageUnroll; ++u)
+        if (i0 + u * stride < n16) v[u] = src[i0 + u * stride];
+#pragma unroll
+      for (int u = 0; u < kStageUnroll; ++u)
+        if (i0 + u * stride < n16) dst[i0 + u * stride] = v[u];
+    }
+    for (size_t i = static_cast<size_t>(n16) * 16 + t0; i < a.bytes[b]; i += stride)
+      a.dst[b][i] = a.src[b][i];
   }
 }
 
 cudaError_t launch_stage_inputs(const StageArgs& a, cudaStream_t s) {
+  // Same shared-memory carveout as the decode kernel, so a staging CTA never
+  // keeps an SM in a configuration a decode CTA cannot join.
+  static std::atomic<bool> carveout_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  if (dev >= 0 && dev < 64 && !carveout_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(stage_inputs_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) == cudaSuccess)
+      carveout_set[dev].store(true, std::memory_order_release);
+    else
+      cudaGetLastError();  // a preference only: the staging still runs
+  }
   const size_t n16 = (a.bytes[0] + a.bytes[1] + a.bytes[2]) / 16 + 1;
-  const unsigned grid = static_cast<unsigned>(std::min<size_t>(1184, (n16 + 255) / 256));
-  stage_inputs_kernel<<<grid, 256, 0, s>>>(a);
+  if (n16 >= (static_cast<size_t>(1) << 31)) return cudaErrorInvalidValue;
+  const size_t per_cta = static_cast<size_t>(kStageThreads) * kStageUnroll;
+  const unsigned grid = static_cast<unsigned>(std::min<size_t>(64, (n16 + per_cta - 1) / per_cta));
+  stage_inputs_kernel<<<grid, kStageThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -549,14 +583,22 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
       }
     }
   };
+  // The first unit's record is plan data (never written by the preceding kernel);
+  // its page ids come from the block tables, read before griddepcontrol.wait only
+  // when they are declared stable.
   if (p_pos < n_units) {
     const int4* rec = a.sched_recs + static_cast<size_t>(p_pos) * 3;
     p_r0 = rec[0];
     p_r1 = rec[1];
     p_r2 = rec[2];
-    load_pages(p_r0, p_r1, p_pg0, p_page0, p_page1);
-    start_unit();
   }
+  auto first_unit_pages = [&]() {
+    if (p_pos < n_units) {
+      load_pages(p_r0, p_r1, p_pg0, p_page0, p_page1);
+      start_unit();
+    }
+  };
+  if (a.early_prefetch) first_unit_pages();
   int issued = 0;
   auto p_issue = [&]() {  // all lanes; lane 0 issues the bulk copies
     while (p_j >= p_end) {  // current unit fully issued: move to the next one
@@ -611,6 +653,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const Dec
   if (!a.early_prefetch) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     dep_ready = true;
+    first_unit_pages();
   }
 #pragma unroll 1
   for (int k = 0; k < NS; ++k) p_issue();
@@ -893,6 +936,16 @@ template <typename T, int EPL>
 __global__ void __launch_bounds__(512) merge_splits_kernel(const DecodeArgs a) {
   __shared__ float red_acc[kMergeWarps][EPL * 32];
   __shared__ float red_m[kMergeWarps], red_l[kMergeWarps];
+  const bool xchg = a.xchg_peers > 0;
+  // The query's record is plan data, which the decode grid does not write: read
+  // it before the wait, so only the partials' loads follow the decode's end.
+  // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
+  int query = 0;
+  int4 qi = make_int4(0, 0, 0, 0);
+  if (xchg || a.n_merge_queries > 0) {
+    query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
+    qi = a.qinfo[query];
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The decode grid has finished: re-arm its unit counter for the next launch,
   // visibly to the whole device before the next launch may start, and copy the
@@ -909,22 +962,18 @@ __global__ void __launch_bounds__(512) merge_splits_kernel(const DecodeArgs a) {
   __syncthreads();
   // the next decode launch may start filling its ring while the merge runs
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const bool xchg = a.xchg_peers > 0;
   if (!xchg && a.n_merge_queries == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wph = a.merge_wph;                 // 1, 2, 4, 8 or 16
   const int sub = warp % wph;
   const int h = blockIdx.y * (kMergeWarps / wph) + warp / wph;
   const bool active = h < a.num_heads;
-  // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
-  const int query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
   const int H = a.num_heads, D = a.head_dim;
   float m_run = kNegBig, sum = 0.f;
   float acc[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
   if (active) {
-    const int4 qi = a.qinfo[query];
     const int slot0 = qi.z, n = qi.w;
     const float2* ml = a.part_ml + static_cast<size_t>(slot0) * H + h;
     const float* po = a.part_o + (static_cast<size_t>(slot0) * H + h) * D + lane;
