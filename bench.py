@@ -371,6 +371,13 @@ class DecodeWorkload:
         # block tables are static and pages are written only by the decode kernels
         # themselves, so each launch may start streaming KV before the previous one ends
         self.plan.set_kv_stable(kv_stable)
+        # The step loop calls the C ABI with its pointer arguments prepared once (the
+        # tensors above never move), as a native caller would: the per-layer checks of
+        # the Python wrappers would otherwise bound the loop on small shards.
+        self.layer_ptrs = [(int(self.q[l].data_ptr()), int(self.kn[l].data_ptr()),
+                            int(self.vn[l].data_ptr()), int(self.out[l].data_ptr()))
+                           for l in range(L)]
+        self.bt_args = (int(self.bt.data_ptr()), int(self.bt.shape[-1]))
         torch.cuda.synchronize()
 
     @property
@@ -388,6 +395,7 @@ class DecodeWorkload:
         by one position first (a new plan on the host, then the layers).  results:
         a dict that receives layer -> a copy of that layer's (all-heads) output."""
         s = self.stream if s is None else s
+        sp = int(s.cuda_stream) or None
         if grow:
             if self.grown >= self.grow_extra:
                 raise RuntimeError("the workload was set up for fewer growing steps")
@@ -407,8 +415,22 @@ class DecodeWorkload:
                                              self.out[l], self.bt, self.scale, ROPE_BASE, False,
                                              stream=s)
             elif self.hsd is None:
-                self.pool.append_decode(self.plan, l, self.q[l], self.kn[l], self.vn[l],
-                                        self.out[l], self.bt, self.scale, stream=s)
+                qp, kp, vp, op = self.layer_ptrs[l]
+                rc = self.ffi.lib.kvc_append_decode(self.pool.handle, self.plan.handle, l, qp, kp,
+                                                    vp, op, *self.bt_args, self.scale, sp)
+                if rc:
+                    self.ffi.check(rc)
+            elif self.xchg == "p2p" and results is None:
+                # the merge kernel pushes this rank's heads into every rank's slot
+                hx = self.hsd.exchange
+                slot = self.hsd._calls % hx.n_slots
+                self.hsd._calls += 1
+                qp, kp, vp, _ = self.layer_ptrs[l]
+                rc = self.ffi.lib.kvc_append_decode_xchg(
+                    self.pool.handle, self.plan.handle, l, qp, kp, vp, hx.handle, slot,
+                    self.H_full, self.head_offset, *self.bt_args, self.scale, sp)
+                if rc:
+                    self.ffi.check(rc)
             else:
                 # fused append + attention on this rank's heads; p2p: the merge kernel
                 # pushes the heads to every rank (result in an exchange slot), nccl:
