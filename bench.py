@@ -982,10 +982,11 @@ def run_offload(args, rank, world, local_rank):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # decode_persistent_kernel launch of config 3, measured by
 #   ncu --set full --clock-control none -k regex:"decode_persistent|merge_splits" -s 8 -c 2 \
-#       -o prof python bench.py --layers 2 --steps 3 --warmup 3 --no-cpu-baseline --no-e2e --no-clocks
+#       -o prof python bench.py --layers 2 --steps 3 --warmup 3 --min-timed-s 0 --max-passes 1 \
+#       --no-cpu-baseline --no-e2e --no-clocks
 # (a 2-layer subset with the same per-launch shape); None for other workloads.
 TRAFFIC_PER_LAUNCH = {
-    "3": 566_632_960 + 7_981_824,
+    "3": 566_632_192 + 4_846_080,
 }
 
 
