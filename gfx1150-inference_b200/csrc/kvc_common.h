@@ -238,9 +238,9 @@ int append_then_decode(kvc_pool* pool, const kvc_plan* plan, int layer, const vo
                        const void* d_k_new, const void* d_v_new, void* d_out, const int32_t* d_bt,
                        int bt_stride, float scale, cudaStream_t s,
                        const XchgTarget* xt = nullptr, int early = -1);
-// Split length (positions) for a batch: see kvc_host.cpp.
+// Split length (positions) for a batch on a grid of `sms` SMs: see kvc_host.cpp.
 int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
-                        int device);
+                        int sms);
 // SM count of `device`; 148 when the query fails (its error is cleared).
 int device_sms(int device);
 // The split partition of a batch, shared by every planner (kvc_plan_decode and
@@ -249,6 +249,9 @@ int device_sms(int device);
 // into quarters.  ups = work units per split (KV heads x q-head chunks).
 int split_partition(int page_size, const int* ctxs, int n_queries, int ups, int device,
                     int* refine);
+// The same for a grid spanning `sms` streaming multiprocessors (no device query).
+int split_partition_sms(int page_size, const int* ctxs, int n_queries, int ups, int sms,
+                        int* refine);
 // The splits of query q (context ctx, split length C, `refine` of its last full
 // splits quartered), in position order: emit(int4{q, split, first, end}) for each.
 // An empty context has one empty split.  Returns the number of splits.

@@ -693,10 +693,10 @@ int device_sms(int device) {
 }
 
 int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_per_split,
-                        int device) {
+                        int sms) {
   const int forced = split_tokens_for(page_size);
   if (forced > 0) return round_split(forced, page_size);
-  return split_tokens_model(page_size, ctx, n_queries, units_per_split, device_sms(device));
+  return split_tokens_model(page_size, ctx, n_queries, units_per_split, sms);
 }
 
 // Tail refinement: with even contexts (nothing but full splits), a multi-wave
@@ -708,7 +708,12 @@ int choose_split_tokens(int page_size, const int* ctx, int n_queries, int units_
 // -9 %), so they are left alone.  KVC_TAIL_REFINE = n overrides the count.
 int split_partition(int page_size, const int* ctxs, int n_queries, int ups, int device,
                     int* refine) {
-  const int C = choose_split_tokens(page_size, ctxs, n_queries, ups, device);
+  return split_partition_sms(page_size, ctxs, n_queries, ups, device_sms(device), refine);
+}
+
+int split_partition_sms(int page_size, const int* ctxs, int n_queries, int ups, int sms,
+                        int* refine) {
+  const int C = choose_split_tokens(page_size, ctxs, n_queries, ups, sms);
   for (int i = 0; i < n_queries; ++i) refine[i] = 0;
   static const int forced = [] {
     const char* e = getenv("KVC_TAIL_REFINE");
@@ -717,7 +722,7 @@ int split_partition(int page_size, const int* ctxs, int n_queries, int ups, int 
   int n_refine = forced;
   if (n_refine < 0) {
     n_refine = 0;
-    const int64_t warps = static_cast<int64_t>(device_sms(device)) * kPersistWarps;
+    const int64_t warps = static_cast<int64_t>(sms) * kPersistWarps;
     int64_t full_units = 0, partial_pos = 0;
     for (int i = 0; i < n_queries; ++i) {
       full_units += static_cast<int64_t>(std::max(0, ctxs[i]) / C) * ups;
@@ -1037,6 +1042,37 @@ extern "C" int kvc_plan_split_tokens(const int32_t* h_ctx_lens, int n_queries, i
   const int group = num_heads / num_kv_heads;
   *out = split_tokens_model(page_size, h_ctx_lens, n_queries, num_kv_heads * ((group + 7) / 8),
                             sm_count);
+  return KVC_OK;
+}
+
+extern "C" int kvc_plan_split_counts(const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                                     int num_kv_heads, int page_size, int sm_count,
+                                     int* split_tokens_out, int32_t* splits_out,
+                                     int* n_splits_out) {
+  if (!split_tokens_out || !n_splits_out)
+    return set_error(KVC_ERR_INVALID_ARG, "split_tokens_out and n_splits_out must not be null.");
+  if (n_queries < 0 || (n_queries > 0 && !h_ctx_lens))
+    return set_error(KVC_ERR_INVALID_ARG, "ctx_lens must hold n_queries lengths.");
+  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "num_heads must be a positive multiple of num_kv_heads.");
+  if (page_size <= 0 || page_size % kSlab != 0)
+    return set_error(KVC_ERR_INVALID_ARG, "page_size must be a positive multiple of 16.");
+  if (sm_count <= 0) return set_error(KVC_ERR_INVALID_ARG, "sm_count must be positive.");
+  for (int i = 0; i < n_queries; ++i)
+    if (h_ctx_lens[i] < 0) return set_error(KVC_ERR_INVALID_ARG, "context length must be non-negative.");
+  const int group = num_heads / num_kv_heads;
+  std::vector<int> refine(std::max(0, n_queries), 0);
+  const int C = split_partition_sms(page_size, h_ctx_lens, n_queries,
+                                    num_kv_heads * ((group + 7) / 8), sm_count, refine.data());
+  int64_t total = 0;
+  for (int i = 0; i < n_queries; ++i) {
+    const int ns = emit_splits(i, h_ctx_lens[i], C, refine[i], [](const int4&) {});
+    if (splits_out) splits_out[i] = ns;
+    total += ns;
+  }
+  if (total > INT32_MAX) return set_error(KVC_ERR_INVALID_ARG, "too many splits.");
+  *split_tokens_out = C;
+  *n_splits_out = static_cast<int>(total);
   return KVC_OK;
 }
 

@@ -98,6 +98,8 @@ SIGNATURES = {
     "kvc_plan_set_flags": (_c_int, [_vp, _c_int]),
     "kvc_plan_split_tokens": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                        ctypes.POINTER(_c_int)]),
+    "kvc_plan_split_counts": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                       ctypes.POINTER(_c_int), _vp, ctypes.POINTER(_c_int)]),
     "kvc_plan_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
                                ctypes.POINTER(_c_size)]),
     "kvc_decode": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_float, _vp]),

@@ -216,6 +216,18 @@ KVC_API int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const int3
 KVC_API int kvc_plan_split_tokens(const int32_t* h_ctx_lens, int n_queries, int num_heads,
                                   int num_kv_heads, int page_size, int sm_count, int* out);
 
+/* The whole split partition kvc_plan_decode (and kvc_decode_noalloc) gives a batch
+ * on a GPU with sm_count SMs, computed on the host: *split_tokens_out = the split
+ * length, splits_out[i] (n_queries entries; may be NULL) = query i's splits,
+ * including any full split the tail refinement cut into quarters, and
+ * *n_splits_out = their sum, the split slots a plan's partials take (each
+ * num_heads x (head_dim + 2) floats).  Unlike kvc_plan_split_tokens it follows the
+ * KVC_SPLIT_TOKENS / KVC_TAIL_REFINE overrides, as the plan does.  Host only; no
+ * counterpart in the reference. */
+KVC_API int kvc_plan_split_counts(const int32_t* h_ctx_lens, int n_queries, int num_heads,
+                                  int num_kv_heads, int page_size, int sm_count,
+                                  int* split_tokens_out, int32_t* splits_out, int* n_splits_out);
+
 /* Plan flags.  KVC_PLAN_KV_STABLE: the block tables and KV pages the plan reads
  * are not written by the kernel launched immediately before each decode on the
  * stream (e.g. they change only through host copies or earlier steps), so the

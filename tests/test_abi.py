@@ -119,3 +119,45 @@ def test_split_length_model_on_the_baseline_shapes():
         rc = ffi.lib.kvc_plan_split_tokens(ffi.np_ptr(c), len(c), bad[1], bad[2], 16, 148,
                                            ctypes.byref(out))
         assert rc == ffi.KVC_ERR_INVALID_ARG
+
+
+def test_split_partition_counts_on_the_baseline_shapes():
+    """The whole partition (kvc_plan_split_counts, host only) on a 148-SM B200: the
+    split slots a plan of each benchmark shape holds (the figures the bench reports
+    as "splits"), ragged batches left unrefined, and the tail refinement cutting
+    full splits into quarters only for even multi-wave batches."""
+    import ctypes
+
+    import numpy as np
+
+    import bench
+    import kvcache_ffi as ffi
+
+    def counts(ctx, H, Hkv, ps=16, sms=148):
+        c = np.ascontiguousarray(np.asarray(ctx, dtype=np.int32))
+        per = np.zeros(len(c), dtype=np.int32)
+        C, tot = ctypes.c_int(0), ctypes.c_int(0)
+        ffi.check(ffi.lib.kvc_plan_split_counts(ffi.np_ptr(c), len(c), H, Hkv, ps, sms,
+                                                ctypes.byref(C), ffi.np_ptr(per),
+                                                ctypes.byref(tot)))
+        assert int(per.sum()) == tot.value
+        return C.value, per, tot.value
+
+    c3 = bench.cached_lengths(bench.CONFIGS["3"]) + 1
+    C, per, tot = counts(c3, 32, 8)
+    assert (C, tot) == (512, 286)
+    assert np.array_equal(per, -(-c3 // 512))          # ragged: no quartered splits
+    C, per, tot = counts([32769] * 8, 64, 8)           # config 4: 4,096 full units, 1,184 warps
+    assert C == 512 and tot == 724
+    extra = per - -(-32769 // 512)
+    assert np.all(extra % 3 == 0) and int(extra.sum()) == 3 * 68   # 68 full splits quartered
+    C, per, tot = counts([32769] * 8, 8, 1)             # its 8-way KV-head shard: one wave
+    assert C == 224 and tot == 1176 and np.all(per == 147)
+    c3s = counts(c3, 4, 1)                              # config 3, 8-way KV-head shard
+    assert (c3s[0], c3s[2]) == (128, 1093)
+    assert counts([4096], 32, 32)[::2] == (112, 37)     # config 2
+    assert counts([0, 5], 8, 8)[1].tolist() == [1, 1]   # an empty context has one split
+    C, tot = ctypes.c_int(0), ctypes.c_int(0)
+    bad = np.ascontiguousarray(np.asarray([-1], dtype=np.int32))
+    assert ffi.lib.kvc_plan_split_counts(ffi.np_ptr(bad), 1, 8, 8, 16, 148, ctypes.byref(C), None,
+                                         ctypes.byref(tot)) == ffi.KVC_ERR_INVALID_ARG
