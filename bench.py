@@ -420,8 +420,9 @@ class DecodeWorkload:
                                                     vp, op, *self.bt_args, self.scale, sp)
                 if rc:
                     self.ffi.check(rc)
-            elif self.xchg == "p2p" and results is None:
+            elif self.xchg == "p2p":
                 # the merge kernel pushes this rank's heads into every rank's slot
+                # (the same calls HeadShardedDecode.append_decode makes)
                 hx = self.hsd.exchange
                 slot = self.hsd._calls % hx.n_slots
                 self.hsd._calls += 1
@@ -431,6 +432,8 @@ class DecodeWorkload:
                     self.H_full, self.head_offset, *self.bt_args, self.scale, sp)
                 if rc:
                     self.ffi.check(rc)
+                if results is not None:
+                    res = hx.slot(slot)[: self.B]
             else:
                 # fused append + attention on this rank's heads; p2p: the merge kernel
                 # pushes the heads to every rank (result in an exchange slot), nccl:
