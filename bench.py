@@ -1310,8 +1310,10 @@ def run_reference(args, rank, world):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(dt * cfg["layers"] * 1e3, 3),
-        "ms_per_step_note": "extrapolated from the 1-layer sample x layers",
+        "ms_per_step": round(dt * 1e3, 3),
+        "ms_per_step_note": ("one step = the timed sample (1 layer of the workload); the whole "
+                             "32-layer step would take ms_per_full_step"),
+        "ms_per_full_step": round(dt * cfg["layers"] * 1e3, 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -1319,8 +1321,14 @@ def run_reference(args, rank, world):
         "data": "synthetic: seeded N(0,1) K/V/q",
         "config": {"workload": f"{cfg['workload']} (benchmark config {args.config})",
                    "layers": cfg["layers"], "q_heads": cfg["H"], "kv_heads": cfg["Hkv"],
-                   "head_dim": cfg["D"], "sequences": cfg["batch"],
-                   "ctx_tokens": int(ctx.sum())},
+                   "head_dim": cfg["D"], "global_batch": cfg["batch"],
+                   "cached_len": (f"U[{cfg['lens'][1]},{cfg['lens'][2]}] seed {cfg['seed']}"
+                                  if cfg["lens"][0] == "uniform" else int(cfg["lens"][1])),
+                   "ctx_tokens_per_gpu_start": int(ctx.sum()),
+                   "kv_bytes_read_per_step_per_gpu": int(sum(step_bytes(cfg, ctx)[:1])),
+                   "timed": (f"{args.steps} samples after {args.warmup} warm-up samples, each "
+                             f"one layer of the workload on {threads} host threads; value = "
+                             f"bytes / mean sample time")},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
