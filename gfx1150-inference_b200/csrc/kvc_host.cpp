@@ -653,7 +653,7 @@ int round_split(int c, int page_size) {
 
 int split_tokens_model(int page_size, const int* ctx, int n_queries, int units_per_split,
                        int sms) {
-  const double warps = static_cast<double>(sms) * kPersistWarps;
+  const double warps = static_cast<double>(sms) * kPersistWarpsPerSm;
   constexpr double kUnitCost = 64.0;   // c0, in positions
   constexpr int kMinSplit = 64;
   int64_t total = 0, max_ctx = 1;
@@ -722,7 +722,7 @@ int split_partition_sms(int page_size, const int* ctxs, int n_queries, int ups, 
   int n_refine = forced;
   if (n_refine < 0) {
     n_refine = 0;
-    const int64_t warps = static_cast<int64_t>(sms) * kPersistWarps;
+    const int64_t warps = static_cast<int64_t>(sms) * kPersistWarpsPerSm;
     int64_t full_units = 0, partial_pos = 0;
     for (int i = 0; i < n_queries; ++i) {
       full_units += static_cast<int64_t>(std::max(0, ctxs[i]) / C) * ups;
@@ -815,7 +815,8 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
     const int nhc = (group + 7) / 8;
     const int per_item = g.num_kv_heads * nhc;
     const int n_units = static_cast<int>(p->items.size()) * per_item;
-    const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
+    const int n_ctas = std::max(1, std::min(sms * kPersistCtasPerSm,
+                                            (n_units + kPersistWarps - 1) / kPersistWarps));
     p->sched_recs.clear();
     for (int k = 0; k < static_cast<int>(p->items.size()); ++k) {
       const int4 it = p->items[k];

@@ -442,7 +442,8 @@ __device__ void finish_split(const DecodeArgs& a, float* sm, int query, int kvh,
 // =====================================================================================
 // Persistent tensor-core decode kernel (16-bit storage, head_dim multiple of 32).
 //
-// One CTA of NW warps per SM; every warp is an independent streaming engine.
+// kPersistCtasPerSm CTAs of NW warps per SM; every warp is an independent
+// streaming engine.
 // The host lists whole split units (one split of one query for one KV head and
 // <= 8 of its q-heads) longest first; warp w of the grid starts with unit w and
 // then takes the next unlisted unit from a global counter, so every warp keeps
@@ -456,19 +457,20 @@ __device__ void finish_split(const DecodeArgs& a, float* sm, int query, int kvh,
 // partial state (merged by merge_splits_kernel, launched behind it).
 // There is no CTA-wide synchronisation after start-up.
 // =====================================================================================
-constexpr int kPersistBarBytes = 1024;   // NW * NS mbarriers
-constexpr int kPersistMetaBytes = 8192;  // NW * NS stage records (4 x int4 each)
+constexpr int kPersistBarBytes = 512;    // NW * NS mbarriers
+constexpr int kPersistMetaBytes = 4096;  // NW * NS stage records (4 x int4 each)
 
 template <int D>
 constexpr int persist_stages() {
-  // ~192 KiB of ring per CTA, at most 12 stages per warp
-  return (196608 / (kPersistWarps * 2 * kSlab * D * 2)) > 12
+  // ~192 KiB of ring per SM (24 KiB per warp), at most 12 stages per warp
+  return (196608 / (kPersistWarpsPerSm * 2 * kSlab * D * 2)) > 12
              ? 12
-             : (196608 / (kPersistWarps * 2 * kSlab * D * 2));
+             : (196608 / (kPersistWarpsPerSm * 2 * kSlab * D * 2));
 }
 
 template <typename T, int D, int NW, int NS>
-__global__ void __launch_bounds__(NW * 32, 1) decode_persistent_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
+    decode_persistent_kernel(const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int SLAB_BYTES = kSlab * D * 2;
   constexpr int STAGE_BYTES = 2 * SLAB_BYTES;
@@ -1557,7 +1559,8 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   const size_t off_qinfo = align256(off_items + sizeof(int4) * 2 * n_items);
   const size_t off_recs = align256(off_qinfo + sizeof(int4) * n_queries);
   const int sms = device_sms(dev);
-  const int n_ctas = std::max(1, std::min(sms, (n_units + kPersistWarps - 1) / kPersistWarps));
+  const int n_ctas = std::max(1, std::min(sms * kPersistCtasPerSm,
+                                          (n_units + kPersistWarps - 1) / kPersistWarps));
   const size_t off_merge = align256(off_recs + sizeof(int4) * 3 * n_units);
   const size_t plan_bytes = align256(off_merge + sizeof(int32_t) * n_queries);
   const size_t off_part_ml = plan_bytes;
