@@ -926,7 +926,7 @@ __global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
 // after decode_persistent_kernel and waits for it (griddepcontrol.wait) before
 // reading the partial states:
 //   M = max_k M_k,  L = sum_k L_k 2^(M_k - M),  out = sum_k O_k 2^(M_k - M) / L
-// One CTA of 16 warps serves 16 / WPH q-heads of one query.  The WPH warps of a
+// One CTA of kMergeWarps (8) warps serves 8 / WPH q-heads of one query.  The WPH warps of a
 // head take contiguous ranges of its splits; each warp merges its range in one
 // pass (running maximum per 32 splits, eight splits' loads in flight), and the
 // ranges are then combined in range order through shared memory.  The order of
@@ -935,7 +935,7 @@ __global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
 // round trips.
 // =====================================================================================
 template <typename T, int EPL>
-__global__ void __launch_bounds__(512) merge_splits_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(32 * kMergeWarps) merge_splits_kernel(const DecodeArgs a) {
   __shared__ float red_acc[kMergeWarps][EPL * 32];
   __shared__ float red_m[kMergeWarps], red_l[kMergeWarps];
   const bool xchg = a.xchg_peers > 0;
@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(512) merge_splits_kernel(const DecodeArgs a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (!xchg && a.n_merge_queries == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wph = a.merge_wph;                 // 1, 2, 4, 8 or 16
+  const int wph = a.merge_wph;                 // 1, 2, 4 or 8
   const int sub = warp % wph;
   const int h = blockIdx.y * (kMergeWarps / wph) + warp / wph;
   const bool active = h < a.num_heads;
