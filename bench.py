@@ -776,7 +776,7 @@ def run_b200(args, rank, world, local_rank):
         # exchange the merge also pushes the outputs and a one-warp kernel
         # publishes and waits for the peers' epochs
         "gpu_launches": launches,
-        "plan": {"ctas_per_launch": info.n_ctas, "splits": info.n_items},
+        "plan": {"work_units_per_launch": info.n_ctas, "splits": info.n_items},
     }
     if grow is not None:
         res["grow"] = grow

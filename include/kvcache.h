@@ -236,7 +236,9 @@ KVC_API int kvc_plan_split_counts(const int32_t* h_ctx_lens, int n_queries, int 
 #define KVC_PLAN_KV_STABLE 1
 KVC_API int kvc_plan_set_flags(kvc_plan_t* plan, int flags);
 
-/* Number of split items, CTAs and bytes of split scratch of the last plan. */
+/* Of the last plan: split items, work units (item x KV head x q-head chunk: one CTA
+ * each in the CUDA-core kernel, handed out to the warps of the persistent
+ * tensor-core kernel) and bytes of split scratch. */
 KVC_API int kvc_plan_info(const kvc_plan_t* plan, int* n_items, int* n_ctas, size_t* scratch_bytes);
 
 /* Split-K GQA decode attention for one layer.  d_q, d_out: (n_queries,
