@@ -296,7 +296,7 @@ class DecodeWorkload:
 
     def __init__(self, config="3", layers=0, rank=0, world=1, local_rank=0, shard="seq",
                  xchg="p2p", page_size=PAGE, grow_extra=0, rope=False, one_rank_of=0,
-                 kv_stable=True):
+                 kv_stable=True, graph_plan=True):
         import torch
 
         import kvcache_ffi as ffi
@@ -367,10 +367,17 @@ class DecodeWorkload:
         self.scale = 1.0 / math.sqrt(D)
         self.stream = torch.cuda.current_stream()
         self.grown = 0
-        self.plan = self.pool.plan(self.ctx, H, stream=self.stream)
         # block tables are static and pages are written only by the decode kernels
-        # themselves, so each launch may start streaming KV before the previous one ends
+        # themselves, so each launch may start streaming KV before the previous one ends;
+        # graph-stable: the step's launches are captured once and replayed after each
+        # rebuild of the plan for grown contexts (re-captured when its layout moves)
+        self.plan = paged.DecodePlan()
         self.plan.set_kv_stable(kv_stable)
+        self.plan.set_graph_stable(graph_plan)
+        self.pool.plan(self.ctx, H, plan=self.plan, stream=self.stream)
+        self.step_graph = None
+        self.step_graph_gen = -1
+        self.captures = 0
         # The step loop calls the C ABI with its pointer arguments prepared once (the
         # tensors above never move), as a native caller would: the per-layer checks of
         # the Python wrappers would otherwise bound the loop on small shards.
@@ -448,12 +455,39 @@ class DecodeWorkload:
                 with self.torch.cuda.stream(s):
                     results[l] = res.clone()
 
+    def step_graphed(self):
+        """One step of the growing decode loop as a serving loop runs it: the plan is
+        rebuilt on the host for contexts one position longer, then the step's
+        launches are replayed from a CUDA graph (captured again only when the
+        plan's layout generation moved)."""
+        torch = self.torch
+        if self.grown >= self.grow_extra:
+            raise RuntimeError("the workload was set up for fewer growing steps")
+        self.grown += 1
+        self.pool.plan(self.ctx + self.grown, self.H, plan=self.plan, stream=self.stream)
+        gen = self.plan.generation
+        if self.step_graph is None or gen != self.step_graph_gen:
+            if self.step_graph is not None:
+                self.step_graph.reset()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.step(s=torch.cuda.current_stream())
+            self.step_graph, self.step_graph_gen = g, gen
+            self.captures += 1
+        self.step_graph.replay()
+
+    def release_graph(self):
+        if self.step_graph is not None:
+            self.step_graph.reset()
+            self.step_graph = None
+
     def step_bytes(self, ctx=None):
         """Algorithmic bytes of one step on this rank: (KV read, appended, q + out)."""
         return step_bytes(dict(self.cfg, H=self.H, Hkv=self.Hkv),
                           self.current_ctx() if ctx is None else ctx)
 
     def close(self):
+        self.release_graph()
         if self.hsd is not None:
             self.hsd.close()  # collective: exchange buffers freed after every rank is done
             self.hsd = None
@@ -485,10 +519,12 @@ def _sum_over_ranks(x, world, dev):
     return float(t.item())
 
 
-def timed_passes(wl, steps, passes, grow=False, graph=None, events=None):
+def timed_passes(wl, steps, passes, grow=False, graph=None, events=None, graphed=False):
     """``passes`` timed passes of exactly ``steps`` steps each, every pass
     bracketed by a barrier and a device synchronisation, timed with CUDA events
-    on the launching stream.  Returns [(ms, bytes of the pass on this rank)]."""
+    on the launching stream.  grow: contexts grow by one position per step (the
+    plan rebuilt every step), the step's launches replayed from a graph when
+    ``graphed``.  Returns [(ms, bytes of the pass on this rank)]."""
     torch = wl.torch
     out = []
     for p in range(passes):
@@ -502,6 +538,8 @@ def timed_passes(wl, steps, passes, grow=False, graph=None, events=None):
         for i in range(steps):
             if graph is not None:
                 graph.replay()
+            elif grow and graphed:
+                wl.step_graphed()
             else:
                 wl.step(grow=grow, events=events[i] if events else None)
             if grow:
@@ -633,16 +671,22 @@ def run_b200(args, rank, world, local_rank):
     grow = None
     clocks = fixed_clocks
     if not args.no_grow:
+        graphed = not args.no_graph and not args.launch_events
         for _ in range(args.warmup):
-            wl.step(grow=True)
+            if graphed:
+                wl.step_graphed()
+            else:
+                wl.step(grow=True)
         torch.cuda.synchronize()
         _check_device(wl, "during the growing loop's warm-up")
+        captures0 = wl.captures
         sampler = ClockSampler(local_rank) if not args.no_clocks else None
         if sampler:
             sampler.start()
-        grow_res = timed_passes(wl, args.steps, passes, grow=True)
+        grow_res = timed_passes(wl, args.steps, passes, grow=True, graphed=graphed)
         clocks = sampler.stop() if sampler else fixed_clocks
         _check_device(wl, "during the growing loop")
+        wl.release_graph()  # before any collective teardown (it may hold NCCL calls)
         g_ms, g_bytes, g_local = _pass_figures(wl, grow_res)
         if not dec_ms:
             dec_bytes = g_local / (args.steps * L)
@@ -652,8 +696,13 @@ def run_b200(args, rank, world, local_rank):
         grow = {"value": round(g_bytes / (g_ms / 1e3) / 1e9, 1),
                 "ms_per_step": round(g_ms / args.steps, 4), "passes": passes,
                 "ctx_tokens_per_gpu_last": int(wl.current_ctx().sum()),
-                "launch": "direct launches from the host loop; the plan is rebuilt on the "
-                          "host every step inside the timed region"}
+                "launch": ((f"the plan is rebuilt on the host every step inside the timed "
+                            f"region, then the step's launches replay from a CUDA graph "
+                            f"(graph-stable plan; {wl.captures - captures0} captures in the "
+                            f"timed passes, when the plan's layout moved)")
+                           if graphed else
+                           "direct launches from the host loop; the plan is rebuilt on the "
+                           "host every step inside the timed region")}
 
     # ---- exchange check (head-sharded runs) ----
     xparity = None

@@ -77,6 +77,7 @@ struct kvc_plan {
   std::vector<int4> sched_recs;   // 3 per scheduled unit
   std::vector<int32_t> merge_queries;
   int n_sched_ctas = 0, n_units = 0;
+  int sms = 0;                  // SMs of the plan's device (its persistent grid's width)
   // Inputs of the last successful build (geometry, queries, contexts, rows): a
   // build with the same inputs keeps the uploaded plan (every layer of one
   // decode step plans the same queries).
@@ -86,6 +87,12 @@ struct kvc_plan {
   // device-error count when d_counters was last zeroed (a kernel that gave up
   // may leave split counters armed: a later build zeroes them again)
   uint32_t counters_zeroed_at = 0;
+  // KVC_PLAN_GRAPH: capacities the blob is laid out for (grow-only), the device
+  // addresses and launch shape captured launches hold, and the generation that
+  // advances whenever a rebuild changes any of them.
+  size_t cap_items = 0, cap_queries = 0, cap_sched = 0, cap_merge = 0;
+  std::vector<uintptr_t> launch_sig;
+  uint64_t generation = 0;
   // parts of d_blob (set by the upload)
   const int4* dev_items = nullptr;
   const int4* dev_qinfo = nullptr;
@@ -94,6 +101,7 @@ struct kvc_plan {
   const int4* dev_sched = nullptr;
   const int32_t* dev_merge = nullptr;
   unsigned int* dev_queue = nullptr;
+  const int* dev_hdr = nullptr;  // kHdr* counts (KVC_PLAN_GRAPH), next to the unit counter
   kvc::DevBuf d_rope;          // rotated q and new K rows (kvc_append_decode_rope)
   kvc::DevBuf d_layer;         // activations of kvc_forward_layer_paged
   kvc::HostBuf h_stage;

@@ -759,6 +759,11 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   if (n_queries < 0) return set_error(KVC_ERR_INVALID_ARG, "n_queries must be non-negative.");
   if (num_heads <= 0 || num_heads % g.num_kv_heads != 0)
     return set_error(KVC_ERR_INVALID_ARG, "num_heads must be divisible by num_kv_heads.");
+  if ((p->flags & KVC_PLAN_GRAPH) &&
+      (!decode_uses_mma(g.dtype, g.head_dim, g.page_size) || g.layout != kLayoutCore))
+    return set_error(KVC_ERR_INVALID_ARG,
+                     "KVC_PLAN_GRAPH needs fp16/bf16 KV with head_dim in {32,64,96,128,160,192,256} "
+                     "and a page size multiple of 16.");
   std::vector<int> ctxs(std::max(0, n_queries));
   for (int i = 0; i < n_queries; ++i) ctxs[i] = ctx_of(i);
   std::vector<int32_t> inputs = {n_queries, num_heads, g.num_kv_heads, g.head_dim, g.page_size,
@@ -829,6 +834,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
     }
     p->n_units = n_units;
     p->n_sched_ctas = n_units > 0 ? n_ctas : 0;
+    p->sms = sms;
     p->merge_queries.clear();
     for (int i = 0; i < n_queries; ++i)
       if (p->qinfo[i].w > 1) p->merge_queries.push_back(i);
@@ -869,19 +875,33 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   // The plan itself: one block {items | qinfo | rows | positions | unit records |
   // merge list | unit counter (zero)}, 256-byte aligned parts, staged in pinned
   // memory and uploaded with one copy.
+  // A graph-stable plan lays the block out for grow-only capacities (25 % headroom),
+  // so its parts keep their device addresses while rebuilds stay within them.
   auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+  const bool graph = (p->flags & KVC_PLAN_GRAPH) != 0;
+  auto cap = [graph](size_t& c, size_t n) {
+    if (!graph) return c = n;
+    if (n > c) c = n + n / 4 + 16;
+    return c;
+  };
   const size_t items_n = sizeof(int4) * p->item_pairs.size();
   const size_t qinfo_n = sizeof(int4) * n_queries;
   const size_t rows_n = sizeof(int32_t) * n_queries;
   const size_t sched_n = sizeof(int4) * p->sched_recs.size();
   const size_t merge_n = sizeof(int32_t) * p->merge_queries.size();
+  const size_t items_cap = sizeof(int4) * cap(p->cap_items, p->item_pairs.size());
+  const size_t q_cap = cap(p->cap_queries, static_cast<size_t>(n_queries));
+  const size_t sched_cap = sizeof(int4) * cap(p->cap_sched, p->sched_recs.size());
+  // (a graph-stable plan's merge grid has a CTA per query, each of which may read
+  // its slot of the list: room for every query)
+  const size_t merge_cap = sizeof(int32_t) * (graph ? q_cap : cap(p->cap_merge, p->merge_queries.size()));
   const size_t o_items = 0;
-  const size_t o_qinfo = o_items + al(std::max<size_t>(items_n, 1));
-  const size_t o_rows = o_qinfo + al(std::max<size_t>(qinfo_n, 1));
-  const size_t o_pos = o_rows + al(std::max<size_t>(rows_n, 1));
-  const size_t o_sched = o_pos + al(std::max<size_t>(rows_n, 1));
-  const size_t o_merge = o_sched + al(std::max<size_t>(sched_n, 1));
-  const size_t o_queue = o_merge + al(std::max<size_t>(merge_n, 1));
+  const size_t o_qinfo = o_items + al(std::max<size_t>(items_cap, 1));
+  const size_t o_rows = o_qinfo + al(std::max<size_t>(sizeof(int4) * q_cap, 1));
+  const size_t o_pos = o_rows + al(std::max<size_t>(sizeof(int32_t) * q_cap, 1));
+  const size_t o_sched = o_pos + al(std::max<size_t>(sizeof(int32_t) * q_cap, 1));
+  const size_t o_merge = o_sched + al(std::max<size_t>(sched_cap, 1));
+  const size_t o_queue = o_merge + al(std::max<size_t>(merge_cap, 1));
   const size_t blob_b = o_queue + 256;
   if ((e = p->d_blob.ensure(blob_b))) return cuda_error(e, "plan buffers");
   if (p->upload_done) {  // the staging is free once the previous upload has landed
@@ -898,6 +918,12 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   if (sched_n) memcpy(h + o_sched, p->sched_recs.data(), sched_n);
   if (merge_n) memcpy(h + o_merge, p->merge_queries.data(), merge_n);
   memset(h + o_queue, 0, 256);  // the unit counter starts at zero (the merge re-arms it)
+  // counts the kernels of a graph-stable plan read (64 bytes past the counter)
+  int32_t* hdr = reinterpret_cast<int32_t*>(h + o_queue + 64);
+  hdr[kHdrUnits] = p->n_units;
+  hdr[kHdrL2Ahead] = l2_ahead_slabs(C);
+  hdr[kHdrMergeQueries] = static_cast<int32_t>(p->merge_queries.size());
+  hdr[kHdrMergeWph] = merge_warps_per_head(max_splits);
   if ((e = cudaMemcpyAsync(p->d_blob.ptr, h, blob_b, cudaMemcpyHostToDevice, s)))
     return cuda_error(e, "plan upload");
   uint8_t* d = static_cast<uint8_t*>(p->d_blob.ptr);
@@ -908,7 +934,21 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->dev_sched = reinterpret_cast<const int4*>(d + o_sched);
   p->dev_merge = reinterpret_cast<const int32_t*>(d + o_merge);
   p->dev_queue = reinterpret_cast<unsigned*>(d + o_queue);
+  p->dev_hdr = reinterpret_cast<const int*>(d + o_queue + 64);
   if ((e = cudaEventRecord(p->upload_done, s))) return cuda_error(e, "cudaEventRecord(plan)");
+  // what launches of this plan hold: a change makes captured launches stale
+  std::vector<uintptr_t> sig = {
+      reinterpret_cast<uintptr_t>(p->d_blob.ptr), o_qinfo, o_rows, o_pos, o_sched, o_merge,
+      o_queue, reinterpret_cast<uintptr_t>(p->d_part_o.ptr),
+      reinterpret_cast<uintptr_t>(p->d_part_ml.ptr), reinterpret_cast<uintptr_t>(p->d_counters.ptr),
+      static_cast<uintptr_t>(n_queries), static_cast<uintptr_t>(num_heads),
+      static_cast<uintptr_t>(g.num_kv_heads), static_cast<uintptr_t>(g.head_dim),
+      static_cast<uintptr_t>(g.page_size), static_cast<uintptr_t>(g.dtype),
+      static_cast<uintptr_t>(device)};
+  if (sig != p->launch_sig) {
+    p->launch_sig.swap(sig);
+    p->generation++;
+  }
   p->pool_geom = g;
   p->built_from.swap(inputs);
   p->valid = true;
@@ -953,6 +993,8 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.counters = static_cast<unsigned*>(plan->d_counters.ptr);
   a.sched_recs = plan->dev_sched;
   a.n_units = plan->n_units;
+  a.sched_cap = (plan->flags & KVC_PLAN_GRAPH) ? static_cast<int>(plan->cap_sched / 3)
+                                               : plan->n_units;
   a.queue = plan->dev_queue;
   a.n_sched_ctas = plan->n_sched_ctas;
   a.early_prefetch = early >= 0 ? early : ((plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0);
@@ -973,6 +1015,11 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.scale_log2 = scale * kLog2e;
   a.n_queries_total = plan->n_queries;
   a.merge_wph = merge_warps_per_head(plan->max_splits);
+  if ((plan->flags & KVC_PLAN_GRAPH) && plan->n_sched_ctas > 0) {
+    // counts from the plan's device header; grids for any rebuild of the plan
+    a.plan_hdr = plan->dev_hdr;
+    a.n_sched_ctas = plan->sms * kPersistCtasPerSm;
+  }
   if (xt) {
     kvc_xchg* x = xt->x;
     if (!decode_uses_mma(g.dtype, g.head_dim, g.page_size) || g.layout != kLayoutCore)
@@ -1106,8 +1153,21 @@ extern "C" int kvc_plan_decode(kvc_plan_t* plan, const kvc_pool_t* pool, const i
 
 extern "C" int kvc_plan_set_flags(kvc_plan_t* plan, int flags) {
   if (!plan) return set_error(KVC_ERR_INVALID_ARG, "plan must not be null.");
-  if (flags & ~KVC_PLAN_KV_STABLE) return set_error(KVC_ERR_INVALID_ARG, "unknown plan flags %d.", flags);
+  if (flags & ~(KVC_PLAN_KV_STABLE | KVC_PLAN_GRAPH))
+    return set_error(KVC_ERR_INVALID_ARG, "unknown plan flags %d.", flags);
+  if ((flags ^ plan->flags) & KVC_PLAN_GRAPH) {
+    // the layout rules change: the next build lays the plan out again
+    plan->valid = false;
+    plan->built_from.clear();
+    plan->generation++;
+  }
   plan->flags = flags;
+  return KVC_OK;
+}
+
+extern "C" int kvc_plan_generation(const kvc_plan_t* plan, uint64_t* out) {
+  if (!plan || !out) return set_error(KVC_ERR_INVALID_ARG, "plan and out must not be null.");
+  *out = plan->generation;
   return KVC_OK;
 }
 

@@ -146,6 +146,7 @@ struct DecodeArgs {
   // launches; the merge kernel re-arms it).
   const int4* sched_recs;
   int n_units;
+  int sched_cap = 0;             // unit records sched_recs holds (>= n_units)
   unsigned int* queue;
   int n_sched_ctas;
   // Block tables and KV pages are not written by the kernel launched just before
@@ -185,7 +186,19 @@ struct DecodeArgs {
   // word, which the split merge (the last kernel of the call) stores, so the host
   // reads it after its wait without a copy of its own.  Null otherwise.
   uint32_t* err_host = nullptr;
+  // Graph-stable plans (KVC_PLAN_GRAPH): the plan's device header, from which the
+  // kernels read n_units, l2_ahead, the multi-split query count and the merge's
+  // warps per head (kHdr*), so launches captured in a CUDA graph stay valid when
+  // the plan is rebuilt for grown contexts.  The decode grid then spans every SM
+  // and the merge grid n_queries x num_heads.  Null: the values above are used.
+  const int* plan_hdr = nullptr;
 };
+// Slots of the plan's device header (int32).
+constexpr int kHdrUnits = 0;
+constexpr int kHdrL2Ahead = 1;
+constexpr int kHdrMergeQueries = 2;
+constexpr int kHdrMergeWph = 3;
+constexpr int kHdrInts = 4;
 
 struct FillArgs {
   uint8_t* base;                 // first byte of the range to fill

@@ -498,7 +498,10 @@ __global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
 
   const int gw = blockIdx.x * NW + warp;
   const int W = gridDim.x * NW;
-  const int n_units = a.n_units;
+  // A graph-stable plan keeps its counts in the plan's device header (its launches
+  // are replayed as contexts grow); otherwise they come with the launch.
+  const int n_units = a.plan_hdr ? a.plan_hdr[kHdrUnits] : a.n_units;
+  const int l2_ahead = a.plan_hdr ? a.plan_hdr[kHdrL2Ahead] : a.l2_ahead;
   const size_t page_stride = static_cast<size_t>(a.num_kv_heads) * ps * D * 2;
   const uint64_t policy = l2_policy_evict_first();
 
@@ -587,8 +590,10 @@ __global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
   };
   // The first unit's record is plan data (never written by the preceding kernel);
   // its page ids come from the block tables, read before griddepcontrol.wait only
-  // when they are declared stable.
-  if (p_pos < n_units) {
+  // when they are declared stable.  The record is loaded while the unit count may
+  // still be on its way (graph-stable plans read it from the device): sched_cap
+  // bounds the load, the count decides whether the record is used.
+  if (p_pos < a.sched_cap) {
     const int4* rec = a.sched_recs + static_cast<size_t>(p_pos) * 3;
     p_r0 = rec[0];
     p_r1 = rec[1];
@@ -667,7 +672,7 @@ __global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
     const int idx = j / spp - p_pg0;
     const int v0 = __shfl_sync(0xffffffffu, p_page0, idx & 31);
     const int v1 = __shfl_sync(0xffffffffu, p_page1, idx & 31);
-    if (lane < a.l2_ahead && p_pos < n_units && j < p_end && p_r0.w > p_r0.z) {
+    if (lane < l2_ahead && p_pos < n_units && j < p_end && p_r0.w > p_r0.z) {
       const int phys = idx < 32 ? v0 : v1;
       if (phys >= 0) {
         const size_t off = static_cast<size_t>(phys) * page_stride +
@@ -939,12 +944,31 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_splits_kernel(const De
   __shared__ float red_acc[kMergeWarps][EPL * 32];
   __shared__ float red_m[kMergeWarps], red_l[kMergeWarps];
   const bool xchg = a.xchg_peers > 0;
+  // Counts: from the launch, or from the plan's device header for a graph-stable
+  // plan, whose grid is sized for the most CTAs any of its rebuilds can need
+  // (n_queries x num_heads); the CTAs a rebuild does not need leave at once
+  // (CTA (0, 0) always stays: it re-arms the unit counter).
   // The query's record is plan data, which the decode grid does not write: read
   // it before the wait, so only the partials' loads follow the decode's end.
   // exchanged outputs: every query (grid.x = n_queries); else the multi-split ones
+  int n_merge = a.n_merge_queries, wph = a.merge_wph;
   int query = 0;
   int4 qi = make_int4(0, 0, 0, 0);
-  if (xchg || a.n_merge_queries > 0) {
+  if (a.plan_hdr) {
+    // the counts, this CTA's list entry and its query's record, all loads at once
+    // (the list has a slot per query; an entry past the count may be stale, so
+    // it is clamped and its record used only when the CTA turns out to be needed)
+    n_merge = a.plan_hdr[kHdrMergeQueries];
+    wph = a.plan_hdr[kHdrMergeWph];
+    query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
+    query = min(max(query, 0), a.n_queries_total - 1);
+    qi = a.qinfo[query];
+  }
+  const int heads_per_cta = kMergeWarps / wph;
+  const bool mine = (xchg || static_cast<int>(blockIdx.x) < n_merge) &&
+                    static_cast<int>(blockIdx.y) * heads_per_cta < a.num_heads;
+  if (!mine && (blockIdx.x | blockIdx.y) != 0) return;
+  if (mine && !a.plan_hdr) {
     query = xchg ? static_cast<int>(blockIdx.x) : a.merge_queries[blockIdx.x];
     qi = a.qinfo[query];
   }
@@ -964,11 +988,10 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_splits_kernel(const De
   __syncthreads();
   // the next decode launch may start filling its ring while the merge runs
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  if (!xchg && a.n_merge_queries == 0) return;
+  if (!mine) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wph = a.merge_wph;                 // 1, 2, 4 or 8
-  const int sub = warp % wph;
-  const int h = blockIdx.y * (kMergeWarps / wph) + warp / wph;
+  const int sub = warp % wph;                  // wph: 1, 2, 4 or 8
+  const int h = blockIdx.y * heads_per_cta + warp / wph;
   const bool active = h < a.num_heads;
   const int H = a.num_heads, D = a.head_dim;
   float m_run = kNegBig, sum = 0.f;
@@ -1346,10 +1369,17 @@ cudaError_t run_persistent(const DecodeArgs& a, cudaStream_t s) {
   // merge (and counter re-arm) as a programmatic dependent launch: scheduled while
   // the decode grid drains
   cudaLaunchConfig_t cfg = {};
-  const int n_merge = a.xchg_peers > 0 ? a.n_queries_total : a.n_merge_queries;
-  const int heads_per_cta = kMergeWarps / a.merge_wph;
-  cfg.gridDim = dim3(static_cast<unsigned>(n_merge > 0 ? n_merge : 1),
-                     n_merge > 0 ? (a.num_heads + heads_per_cta - 1) / heads_per_cta : 1, 1);
+  if (a.plan_hdr) {
+    // graph-stable plan: room for every query and one q-head per CTA (the most
+    // any rebuild of the plan can use); the kernel reads the counts
+    cfg.gridDim = dim3(static_cast<unsigned>(a.n_queries_total > 0 ? a.n_queries_total : 1),
+                       static_cast<unsigned>(a.num_heads), 1);
+  } else {
+    const int n_merge = a.xchg_peers > 0 ? a.n_queries_total : a.n_merge_queries;
+    const int heads_per_cta = kMergeWarps / a.merge_wph;
+    cfg.gridDim = dim3(static_cast<unsigned>(n_merge > 0 ? n_merge : 1),
+                       n_merge > 0 ? (a.num_heads + heads_per_cta - 1) / heads_per_cta : 1, 1);
+  }
   cfg.blockDim = dim3(32 * kMergeWarps, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
@@ -1619,6 +1649,7 @@ extern "C" int kvc_decode_noalloc(const void* d_k_layer, const void* d_v_layer, 
   a.counters = nullptr;  // not used by the tensor-core path
   a.sched_recs = reinterpret_cast<const int4*>(base + off_recs);
   a.n_units = n_units;
+  a.sched_cap = n_units;
   a.queue = reinterpret_cast<unsigned*>(base + off_queue);
   a.n_sched_ctas = n_units > 0 ? n_ctas : 0;
   a.early_prefetch = 0;

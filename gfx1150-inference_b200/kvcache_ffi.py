@@ -37,6 +37,7 @@ DTYPE_BF16 = 1
 DTYPE_F32 = 2
 
 PLAN_KV_STABLE = 1
+PLAN_GRAPH = 2
 
 OFFLOAD_PINNED = 1
 OFFLOAD_REGISTER = 2
@@ -96,6 +97,7 @@ SIGNATURES = {
     "kvc_plan_destroy": (_c_int, [_vp]),
     "kvc_plan_decode": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
     "kvc_plan_set_flags": (_c_int, [_vp, _c_int]),
+    "kvc_plan_generation": (_c_int, [_vp, ctypes.POINTER(ctypes.c_uint64)]),
     "kvc_plan_split_tokens": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                        ctypes.POINTER(_c_int)]),
     "kvc_plan_split_counts": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int,

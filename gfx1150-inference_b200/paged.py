@@ -67,12 +67,31 @@ class DecodePlan:
         self.n_queries = 0
         self.num_heads = 0
         self.ctx_lens: Optional[np.ndarray] = None
+        self.flags = 0
+
+    def _set_flag(self, flag: int, on: bool) -> None:
+        flags = (self.flags | flag) if on else (self.flags & ~flag)
+        ffi.check(ffi.lib.kvc_plan_set_flags(self.handle, flags))
+        self.flags = flags
 
     def set_kv_stable(self, stable: bool = True) -> None:
         """Declare that block tables and KV pages are not written by the kernel
         launched right before each decode (lets the kernel start streaming KV
         early; see KVC_PLAN_KV_STABLE)."""
-        ffi.check(ffi.lib.kvc_plan_set_flags(self.handle, ffi.PLAN_KV_STABLE if stable else 0))
+        self._set_flag(ffi.PLAN_KV_STABLE, stable)
+
+    def set_graph_stable(self, on: bool = True) -> None:
+        """Let decode launches of this plan be captured in a CUDA graph and replayed
+        after rebuilds for grown contexts (KVC_PLAN_GRAPH); re-capture whenever
+        ``generation`` changes.  Set before the first build."""
+        self._set_flag(ffi.PLAN_GRAPH, on)
+
+    @property
+    def generation(self) -> int:
+        """Layout generation: launches captured under another value are stale."""
+        g = ctypes.c_uint64()
+        ffi.check(ffi.lib.kvc_plan_generation(self.handle, ctypes.byref(g)))
+        return g.value
 
     def info(self) -> PlanInfo:
         n_items, n_ctas = ctypes.c_int(), ctypes.c_int()

@@ -234,7 +234,19 @@ KVC_API int kvc_plan_split_counts(const int32_t* h_ctx_lens, int n_queries, int 
  * decode kernel may start streaming KV pages before that kernel's results are
  * visible (programmatic dependent launch).  Without it, the kernel waits first. */
 #define KVC_PLAN_KV_STABLE 1
+/* KVC_PLAN_GRAPH: decode launches of this plan may be captured in a CUDA graph
+ * and replayed after the plan is rebuilt for other contexts (a decode loop whose
+ * contexts grow by one position per step).  The kernels then read the plan's
+ * counts from its device buffers, the decode grid spans every SM, the merge grid
+ * has room for every query and head, and the plan keeps its device buffers (and
+ * their layout) across rebuilds, growing them with headroom when a rebuild needs
+ * more.  A rebuild that had to move them, or that changes the query count, head
+ * count or pool, advances kvc_plan_generation: captured launches are then stale
+ * and must be captured again.  Set the flag before the first build. */
+#define KVC_PLAN_GRAPH 2
 KVC_API int kvc_plan_set_flags(kvc_plan_t* plan, int flags);
+/* The plan's layout generation (see KVC_PLAN_GRAPH).  No counterpart in the reference. */
+KVC_API int kvc_plan_generation(const kvc_plan_t* plan, uint64_t* out);
 
 /* Of the last plan: split items, work units (item x KV head x q-head chunk: one CTA
  * each in the CUDA-core kernel, handed out to the warps of the persistent
