@@ -388,7 +388,7 @@ __device__ __forceinline__ void append_row_to_pool(const DecodeArgs& a, int layo
                                                    const int32_t* bt_row, int lane) {
   const int U = a.head_dim * es / 16;
   const int slot = pos / a.page_size;
-  const int phys = bt_row[slot];
+  const int phys = slot < a.bt_stride ? bt_row[slot] : -1;
   if (phys < 0 || phys >= a.num_pages) return;  // reported by the slab loader
   const int t = pos - slot * a.page_size;
   const size_t page_head = static_cast<size_t>(a.page_size) * a.head_dim * es;
@@ -512,13 +512,15 @@ __global__ void __launch_bounds__(NW * 32, kPersistCtasPerSm)
     const int npages = (r0.w + ps - 1) / ps - pg0;
     const int32_t* bt_row = a.block_tables + static_cast<size_t>(r1.x) * a.bt_stride;
     page0 = page1 = -1;
+    // A replayed launch of a rebuilt plan skips the host's check of the contexts
+    // against the table width: an entry past the row's end counts as a bad page.
     if (lane < npages) {
-      const int v = bt_row[pg0 + lane];
+      const int v = pg0 + lane < a.bt_stride ? bt_row[pg0 + lane] : -1;
       page0 = (v >= 0 && v < a.num_pages) ? v : -1;
       if (page0 < 0) report_error(1u, static_cast<uint32_t>(v));
     }
     if (lane + 32 < npages) {
-      const int v = bt_row[pg0 + lane + 32];
+      const int v = pg0 + lane + 32 < a.bt_stride ? bt_row[pg0 + lane + 32] : -1;
       page1 = (v >= 0 && v < a.num_pages) ? v : -1;
       if (page1 < 0) report_error(1u, static_cast<uint32_t>(v));
     }
@@ -1186,7 +1188,7 @@ __global__ void __launch_bounds__(256) decode_simt_kernel(const DecodeArgs a, in
   if (threadIdx.x < kMaxSplitPages) {
     int v = -1;
     if (static_cast<int>(threadIdx.x) < npages) {
-      v = bt_row[pg0 + threadIdx.x];
+      v = pg0 + static_cast<int>(threadIdx.x) < a.bt_stride ? bt_row[pg0 + threadIdx.x] : -1;
       if (v < 0 || v >= a.num_pages) {
         report_error(1u, static_cast<uint32_t>(v));
         v = -1;

@@ -65,7 +65,7 @@ extern "C" {
 
 /* device error codes written by kernels (kvc_device_error) */
 #define KVC_DEVERR_NONE 0u
-#define KVC_DEVERR_BAD_PAGE 1u        /* block table entry outside [0, num_pages) */
+#define KVC_DEVERR_BAD_PAGE 1u        /* block table entry outside [0, num_pages), or past the row's width */
 #define KVC_DEVERR_WAIT_LIMIT 2u      /* an mbarrier wait gave up after its limit */
 #define KVC_DEVERR_BAD_POSITION 3u    /* append position outside the block table */
 

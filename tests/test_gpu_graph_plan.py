@@ -121,3 +121,46 @@ def test_graph_plan_generation_and_validation(cuda_device):
         x.close()
     pool.close()
     pool32.close()
+
+
+def test_graph_replay_past_table_width_reports_bad_page(cuda_device):
+    # A replayed launch does not repeat the host's check of the contexts against
+    # the block-table width (a rebuild only uploads the plan): a context grown past
+    # the table's row is reported by the kernels as a bad page, and the entries
+    # past the row's end are never read.
+    H, Hkv, D = 8, 2, 128
+    pool, bt, q = _setup(np.array([64, 64]), H, Hkv, D, layers=1)
+    assert bt.shape[-1] == 4                       # 4 pages of 16 positions per row
+    scale = 1.0 / np.sqrt(D)
+    s = torch.cuda.current_stream()
+    out = torch.zeros((2, H, D), dtype=torch.float16, device="cuda")
+    p = paged.DecodePlan()
+    p.set_graph_stable(True)
+    ffi.device_error(0, clear=True)
+    # a first build at longer contexts sizes the plan's block and scratch, so the
+    # rebuilds below stay within them and keep the captured launch's addresses
+    pool.plan([200, 200], H, plan=p, stream=s)
+    pool.plan([60, 60], H, plan=p, stream=s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        pool.decode(p, 0, q[0], out, bt, scale, stream=torch.cuda.current_stream())
+    gen = p.generation
+    graph.replay()
+    torch.cuda.synchronize()
+    assert ffi.device_error(0, clear=True)[0] == 0
+    pool.plan([80, 80], H, plan=p, stream=s)       # 5 pages: one past the row
+    assert p.generation == gen                     # the captured launch stays valid
+    graph.replay()
+    torch.cuda.synchronize()
+    code, _ = ffi.device_error(0, clear=True)
+    assert code == 1                               # KVC_DEVERR_BAD_PAGE
+    # the context stays usable: back within the table, the replay is clean
+    pool.plan([60, 60], H, plan=p, stream=s)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert ffi.device_error(0, clear=True)[0] == 0
+    assert_attention_close(out.cpu().numpy(), _oracle(pool, 0, bt, [60, 60], q[0], scale),
+                           "graph replay back within the table")
+    del graph
+    p.close()
+    pool.close()

@@ -129,3 +129,58 @@ def test_gather_rejects_wrong_output_shape():
         assert torch.equal(out, local + 1)
     finally:
         dist.destroy_process_group()
+
+
+def _failing_rank_main(rank: int, port: int, mode: str, results):
+    # Rank 1 fails between two layers of a KV-head-sharded decode (it raises, or its
+    # process ends without a word); rank 0 goes on to the next layer's head gather.
+    # With a short process-group timeout that gather must end with an error on
+    # rank 0, so a serving loop learns of the lost rank instead of waiting for good.
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD,
+                            timeout=datetime.timedelta(seconds=3))
+    B, hl, D = 3, 4, 16
+    local = torch.full((B, hl, D), float(rank))
+    out = torch.empty((B, WORLD * hl, D))
+    sharding.gather_head_outputs(local, out)              # layer 0: both ranks present
+    results[(rank, "layer0")] = bool(torch.equal(out[:, hl:], torch.ones((B, hl, D))))
+    if rank == 1:
+        if mode == "raise":
+            results[(rank, "left")] = True
+            raise RuntimeError("rank 1 failed between layers (planted on the host)")
+        results[(rank, "left")] = True
+        os._exit(0)                                       # ends without a word
+    t0 = time.monotonic()
+    try:
+        sharding.gather_head_outputs(local, out)          # layer 1: rank 1 never comes
+        results[(rank, "error")] = None
+    except Exception as e:  # noqa: BLE001 - the backend's error type varies by version
+        results[(rank, "error")] = type(e).__name__
+    results[(rank, "waited_s")] = time.monotonic() - t0
+    os._exit(0)  # the group cannot be torn down collectively without the lost rank
+
+
+@pytest.mark.parametrize("mode", ["raise", "exit"])
+def test_lost_rank_ends_the_survivors_next_gather_with_an_error(mode):
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, port, mode, results))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    got = dict(results)
+    assert got.get((0, "layer0")) and got.get((1, "layer0")), got
+    assert got.get((1, "left")), got
+    assert procs[0].exitcode == 0, procs[0].exitcode
+    assert got.get((0, "error")) is not None, "the survivor's gather returned without its peer"
+    assert got[(0, "waited_s")] < 60.0, got
