@@ -374,6 +374,11 @@ class DecodeWorkload:
         self.plan = paged.DecodePlan()
         self.plan.set_kv_stable(kv_stable)
         self.plan.set_graph_stable(graph_plan)
+        if graph_plan and grow_extra:
+            # a serving loop reserves for the longest contexts it will reach: one build
+            # at those sizes the plan's block and scratch, so the rebuilds of the
+            # growing loop keep the captured launches' addresses
+            self.pool.plan(self.ctx + grow_extra, H, plan=self.plan, stream=self.stream)
         self.pool.plan(self.ctx, H, plan=self.plan, stream=self.stream)
         self.step_graph = None
         self.step_graph_gen = -1
@@ -611,7 +616,8 @@ def run_b200(args, rank, world, local_rank):
     # upper bound of the timed passes (each pass >= its bytes at 7 TB/s per GPU), so
     # the growing loop's pages can be laid out before anything runs
     ctx0 = cached_lengths(cfg0) + 1
-    t_min = sum(step_bytes(cfg0, ctx0)) / max(1, world if shard == "heads" else 1) / 7.0e12
+    t_min = (sum(step_bytes(cfg0, ctx0)) / max(1, world if shard == "heads" else 1)
+             / max(1, args.one_rank_of if world == 1 else 1) / 7.0e12)
     max_passes = max(1, min(args.max_passes,
                             math.ceil(args.min_timed_s / max(1e-6, args.steps * t_min)) + 1))
     grow_steps = (args.warmup + max_passes * args.steps + 2) if not args.no_grow else 0
@@ -807,6 +813,8 @@ def run_b200(args, rank, world, local_rank):
                                "merge kernel pushes outputs to every rank over NVLink (p2p)")
                             + f", {B * H * D * 2} B of head outputs per GPU per layer"
                             if shard == "heads" and world > 1 else
+                            f"one GPU running rank 0's shard of a {args.one_rank_of}-way KV-head "
+                            "split (profiling)" if args.one_rank_of > 1 else
                             f"sequence-sharded x{world} (independent batches, no collective)"),
         },
         "fixed_step": fixed,
@@ -818,7 +826,8 @@ def run_b200(args, rank, world, local_rank):
             "bytes_per_launch": int(dec_bytes), "avg_launch_us": round(dec_avg_ms * 1e3, 2),
             "duration_from": dec_from,
             "traffic": (TRAFFIC_PER_LAUNCH.get(args.config)
-                        if not args.layers and world == 1 and args.page_size == PAGE else None),
+                        if (not args.layers and world == 1 and args.page_size == PAGE
+                            and args.one_rank_of <= 1) else None),
             "traffic_from": "ncu dram__bytes_read.sum + dram__bytes_write.sum, decode kernel",
         },
         # per layer: the decode kernel and its split merge (PDL); with the p2p head

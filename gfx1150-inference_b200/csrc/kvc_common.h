@@ -70,6 +70,7 @@ struct kvc_plan {
   int num_heads = 0, num_kv_heads = 0, group = 0, n_hchunk = 0;
   int head_dim = 0, page_size = 0, max_ctx = 0, max_splits = 0, split_tokens = 0;
   bool rows_distinct = true;   // every query has its own block-table row
+  bool even_ctx = false;       // every query has the same context length
   int flags = 0;               // KVC_PLAN_*
   kvc::PoolGeom pool_geom;
   std::vector<int4> items, qinfo, item_pairs;
@@ -87,10 +88,10 @@ struct kvc_plan {
   // device-error count when d_counters was last zeroed (a kernel that gave up
   // may leave split counters armed: a later build zeroes them again)
   uint32_t counters_zeroed_at = 0;
-  // KVC_PLAN_GRAPH: capacities the blob is laid out for (grow-only), the device
-  // addresses and launch shape captured launches hold, and the generation that
-  // advances whenever a rebuild changes any of them.
-  size_t cap_items = 0, cap_queries = 0, cap_sched = 0, cap_merge = 0;
+  // KVC_PLAN_GRAPH: capacities the blob and the split scratch are laid out for
+  // (grow-only), the device addresses and launch shape captured launches hold,
+  // and the generation that advances whenever a rebuild changes any of them.
+  size_t cap_items = 0, cap_queries = 0, cap_sched = 0, cap_merge = 0, cap_slots = 0;
   std::vector<uintptr_t> launch_sig;
   uint64_t generation = 0;
   // parts of d_blob (set by the upload)

@@ -622,7 +622,7 @@ namespace kvc {
 // counts of the batch, so the same call always gets the same partition (the
 // resident and offloaded paths agree bit for bit).  KVC_SPLIT_TOKENS overrides
 // it for tuning.
-int l2_ahead_slabs(int split_tokens) {
+int l2_ahead_slabs(int split_tokens, bool even_ctx) {
   static int forced = [] {
     const char* e = getenv("KVC_L2_AHEAD");
     if (!e) return -1;
@@ -630,7 +630,7 @@ int l2_ahead_slabs(int split_tokens) {
     return x < 0 ? 0 : (x > 32 ? 32 : x);
   }();
   if (forced >= 0) return forced;
-  return split_tokens >= kL2AheadMinSplit ? kL2AheadSlabs : 0;
+  return (even_ctx && split_tokens >= kL2AheadMinSplit) ? kL2AheadSlabs : 0;
 }
 
 int split_tokens_for(int page_size) {
@@ -786,7 +786,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->qinfo.clear();
   p->rows.clear();
   p->positions.clear();
-  int slot = 0, max_ctx = 0, max_splits = 0;
+  int slot = 0, max_ctx = 0, min_ctx = n_queries > 0 ? ctxs[0] : 0, max_splits = 0;
   for (int i = 0; i < n_queries; ++i) {
     const int ctx = ctxs[i];
     const int row = row_of(i);
@@ -798,6 +798,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
     p->positions.push_back(ctx - 1);
     slot += ns;
     max_ctx = std::max(max_ctx, ctx);
+    min_ctx = std::min(min_ctx, ctx);
     max_splits = std::max(max_splits, ns);
   }
   // Longest splits first: CTAs are dispatched roughly in index order, so the
@@ -849,6 +850,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   p->head_dim = g.head_dim;
   p->page_size = g.page_size;
   p->max_ctx = max_ctx;
+  p->even_ctx = min_ctx == max_ctx;
   p->max_splits = max_splits;
   p->split_tokens = C;
   p->device = device;
@@ -859,9 +861,18 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   }
 
   cudaError_t e;
-  // Scratch (grow-only): split partials and the per-(query, head) counters.
-  const size_t po_b = sizeof(float) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads * g.head_dim);
-  const size_t pml_b = sizeof(float2) * std::max<size_t>(1, static_cast<size_t>(slot) * num_heads);
+  // Scratch (grow-only): split partials and the per-(query, head) counters.  A
+  // graph-stable plan sizes the partials with the same headroom as its block, so
+  // a context that adds a split does not move them (and stale the captured launches).
+  const bool graph = (p->flags & KVC_PLAN_GRAPH) != 0;
+  auto cap = [graph](size_t& c, size_t n) {
+    if (!graph) return c = n;
+    if (n > c) c = n + n / 4 + 16;
+    return c;
+  };
+  const size_t slots = cap(p->cap_slots, static_cast<size_t>(slot));
+  const size_t po_b = sizeof(float) * std::max<size_t>(1, slots * num_heads * g.head_dim);
+  const size_t pml_b = sizeof(float2) * std::max<size_t>(1, slots * num_heads);
   const size_t cnt_b = sizeof(unsigned) * std::max<size_t>(1, static_cast<size_t>(n_queries) * g.num_kv_heads * p->n_hchunk);
   if ((e = p->d_part_o.ensure(po_b)) || (e = p->d_part_ml.ensure(pml_b)))
     return cuda_error(e, "plan buffers");
@@ -878,12 +889,6 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   // A graph-stable plan lays the block out for grow-only capacities (25 % headroom),
   // so its parts keep their device addresses while rebuilds stay within them.
   auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
-  const bool graph = (p->flags & KVC_PLAN_GRAPH) != 0;
-  auto cap = [graph](size_t& c, size_t n) {
-    if (!graph) return c = n;
-    if (n > c) c = n + n / 4 + 16;
-    return c;
-  };
   const size_t items_n = sizeof(int4) * p->item_pairs.size();
   const size_t qinfo_n = sizeof(int4) * n_queries;
   const size_t rows_n = sizeof(int32_t) * n_queries;
@@ -921,7 +926,7 @@ int plan_build(kvc_plan* p, const PoolGeom& g, int n_queries, int num_heads, Ctx
   // counts the kernels of a graph-stable plan read (64 bytes past the counter)
   int32_t* hdr = reinterpret_cast<int32_t*>(h + o_queue + 64);
   hdr[kHdrUnits] = p->n_units;
-  hdr[kHdrL2Ahead] = l2_ahead_slabs(C);
+  hdr[kHdrL2Ahead] = l2_ahead_slabs(C, p->even_ctx);
   hdr[kHdrMergeQueries] = static_cast<int32_t>(p->merge_queries.size());
   hdr[kHdrMergeWph] = merge_warps_per_head(max_splits);
   if ((e = cudaMemcpyAsync(p->d_blob.ptr, h, blob_b, cudaMemcpyHostToDevice, s)))
@@ -998,7 +1003,7 @@ int do_decode_fused(kvc_pool* pool, const kvc_plan* plan, int layer, const void*
   a.queue = plan->dev_queue;
   a.n_sched_ctas = plan->n_sched_ctas;
   a.early_prefetch = early >= 0 ? early : ((plan->flags & KVC_PLAN_KV_STABLE) ? 1 : 0);
-  a.l2_ahead = l2_ahead_slabs(plan->split_tokens);
+  a.l2_ahead = l2_ahead_slabs(plan->split_tokens, plan->even_ctx);
   a.err_host = host_call_error_copy();
   a.merge_queries = plan->dev_merge;
   a.n_merge_queries = static_cast<int>(plan->merge_queries.size());

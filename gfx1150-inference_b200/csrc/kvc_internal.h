@@ -59,11 +59,14 @@ constexpr int kPersistWarps = 4;
 constexpr int kPersistCtasPerSm = 2;
 constexpr int kPersistWarpsPerSm = kPersistWarps * kPersistCtasPerSm;
 // Slabs per warp brought into L2 while a decode launch waits for the preceding
-// kernel (early KV streaming only), for plans whose splits are at least
-// kL2AheadMinSplit positions long; KVC_L2_AHEAD overrides (0 ... 32).  Measured
-// on B200: +1.9 % for one rank of an 8-way KV-head split of config 4 (224-position
-// splits), +0.5 % config 4, neutral config 3; 7 % slower for config 2's
-// 112-position splits, hence the threshold; deeper prefetch was slower everywhere.
+// kernel (early KV streaming only), for plans whose queries all have the same
+// context and whose splits are at least kL2AheadMinSplit positions long;
+// KVC_L2_AHEAD overrides (0 ... 32).  Measured on B200 (replayed steps, A/B on
+// one box): even contexts gain, one rank of config 4's 8-way and 2-way KV-head
+// splits 2.3 % and 1.3 %, config 4 itself neutral; ragged batches lose, config 3's
+// 2-way and 4-way shards 2.5 % and 1.3 % (growing loop 2-6 %), config 3 0.5 %;
+// config 2's 112-position splits lose 7 %, hence the threshold; deeper prefetch
+// was slower everywhere.
 constexpr int kL2AheadSlabs = 2;
 constexpr int kL2AheadMinSplit = 192;
 // Ranks a head exchange can span (one process per GPU of one node).
