@@ -1047,7 +1047,7 @@ def run_offload(args, rank, world, local_rank):
 #       --no-cpu-baseline --no-e2e --no-clocks
 # (a 2-layer subset with the same per-launch shape); None for other workloads.
 TRAFFIC_PER_LAUNCH = {
-    "3": 566_644_992 + 5_225_472,
+    "3": 566_637_824 + 5_116_416,
 }
 
 
