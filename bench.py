@@ -402,6 +402,11 @@ class DecodeWorkload:
     def current_ctx(self):
         return self.ctx + self.grown
 
+    def restart_growth(self):
+        """Contexts back to the configured lengths: the next growing step decodes
+        position ctx again (the rows appended past it are never read)."""
+        self.grown = 0
+
     def step(self, s=None, grow=False, events=None, results=None):
         """One decode step over all layers on stream ``s``.  grow: the contexts grow
         by one position first (a new plan on the host, then the layers).  results:
@@ -534,6 +539,10 @@ def timed_passes(wl, steps, passes, grow=False, graph=None, events=None, graphed
     out = []
     for p in range(passes):
         parts = []
+        if grow:
+            # every pass decodes the same positions past the configured contexts, so
+            # the workload does not drift from the config over many passes
+            wl.restart_growth()
         if wl.world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
@@ -620,7 +629,7 @@ def run_b200(args, rank, world, local_rank):
              / max(1, args.one_rank_of if world == 1 else 1) / 7.0e12)
     max_passes = max(1, min(args.max_passes,
                             math.ceil(args.min_timed_s / max(1e-6, args.steps * t_min)) + 1))
-    grow_steps = (args.warmup + max_passes * args.steps + 2) if not args.no_grow else 0
+    grow_steps = (max(args.warmup, args.steps) + 2) if not args.no_grow else 0
     wl = DecodeWorkload(args.config, layers=args.layers, rank=rank, world=world,
                         local_rank=local_rank, shard=shard, xchg=args.xchg,
                         page_size=args.page_size, grow_extra=grow_steps, rope=args.rope,

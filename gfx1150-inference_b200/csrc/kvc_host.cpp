@@ -615,7 +615,8 @@ namespace kvc {
 //   max( sum_u (len_u + c0) / W ,  max_u len_u + c0 )  +  (units > W ? s / 4 : 0)
 // (c0 = a unit's fixed cost: first-slab latency, q load, partial write; s / 4 =
 // the expected idle tail of the last wave) over the default 512 and every
-// length whose units fit one wave, and picks the cheapest, the longest on ties.  Long, even contexts with few units get one wave of equal units
+// length of at least kMinSplit positions whose units fit one wave, and picks the
+// cheapest, the longest on ties.  Long, even contexts with few units get one wave of equal units
 // (e.g. 8 x 32K positions on one KV head: 224-position splits, 1176 units on
 // 1184 warps); large ragged batches get 512-position splits and rely on the
 // dynamic schedule.  The choice depends only on the context lengths and head
@@ -655,7 +656,11 @@ int split_tokens_model(int page_size, const int* ctx, int n_queries, int units_p
                        int sms) {
   const double warps = static_cast<double>(sms) * kPersistWarpsPerSm;
   constexpr double kUnitCost = 64.0;   // c0, in positions
-  constexpr int kMinSplit = 64;
+  // Units of fewer than 8 slabs cost more than the model says: config 2 (one
+  // 4,096-position MHA sequence) ran 1.3 % faster per step with 128-position
+  // splits (1,024 units) than with the 112 (1,184 units) the model picks from 64 up,
+  // and 7 % faster over its growing contexts 4,097-4,196 (A/B on one B200).
+  constexpr int kMinSplit = 128;
   int64_t total = 0, max_ctx = 1;
   for (int i = 0; i < n_queries; ++i) {
     total += std::max(ctx[i], 1);

@@ -111,7 +111,7 @@ def test_split_length_model_on_the_baseline_shapes():
     assert split([32769] * 8, 32, 4) == 896     # 2-way KV-head shard: 1,184 units
     assert split([32769] * 8, 16, 2) == 448     # 4-way
     assert split([32769] * 8, 8, 1) == 224      # 8-way: 1,176 units
-    assert split([4096], 32, 32) == 112         # config 2: 1,184 units
+    assert split([4096], 32, 32) == 128         # config 2: 1,024 units (8 slabs each at least)
     assert split([4096], 32, 32, ps=32) % 32 == 0
     for bad in ((c3, 30, 8), (c3, 32, 0)):
         out = ctypes.c_int(0)
@@ -155,7 +155,7 @@ def test_split_partition_counts_on_the_baseline_shapes():
     assert C == 224 and tot == 1176 and np.all(per == 147)
     c3s = counts(c3, 4, 1)                              # config 3, 8-way KV-head shard
     assert (c3s[0], c3s[2]) == (128, 1093)
-    assert counts([4096], 32, 32)[::2] == (112, 37)     # config 2
+    assert counts([4096], 32, 32)[::2] == (128, 32)     # config 2
     assert counts([0, 5], 8, 8)[1].tolist() == [1, 1]   # an empty context has one split
     C, tot = ctypes.c_int(0), ctypes.c_int(0)
     bad = np.ascontiguousarray(np.asarray([-1], dtype=np.int32))

@@ -110,6 +110,32 @@ def test_config3_growing_decode_loop(cuda_device):
         wl.close()
 
 
+def test_config3_graphed_growing_loop_with_restarts(cuda_device):
+    # The headline measurement: the plan rebuilt every step, the step's launches
+    # replayed from one graph, contexts back to the configured lengths at every
+    # timed pass.  The replayed outputs must equal the oracle after growth and
+    # after a restart, with no capture after the first.
+    wl = bench.DecodeWorkload("3", layers=2, grow_extra=6)
+    try:
+        for _ in range(4):
+            wl.step_graphed()
+        torch.cuda.synchronize()
+        assert ffi.device_error(0) == (0, 0)
+        assert int(wl.current_ctx().max()) == int(wl.ctx.max()) + 4
+        _check_workload(wl, {l: wl.out[l].clone() for l in range(wl.L)}, "graphed growing loop")
+        wl.restart_growth()
+        for _ in range(2):
+            wl.step_graphed()
+        torch.cuda.synchronize()
+        assert ffi.device_error(0) == (0, 0)
+        assert int(wl.current_ctx().max()) == int(wl.ctx.max()) + 2
+        _check_workload(wl, {l: wl.out[l].clone() for l in range(wl.L)},
+                        "graphed growing loop after a restart")
+        assert wl.captures == 1
+    finally:
+        wl.close()
+
+
 def _expected_quartered(ctx, C, ups, warps):
     full = sum(c // C for c in ctx) * ups
     part = sum(c % C for c in ctx) * ups
